@@ -1,0 +1,362 @@
+"""Benchmark of the fused bf16 GEMM + allreduce megakernel.
+
+Workload: row-parallel GEMM + allreduce, M = 4096, N = 8192, K = 8192 split
+over tp = N GPUs (each PE: A [4096, 8192/tp], B [8192/tp, 8192], bf16 N(0,
+0.02^2)), output [4096, 8192] bf16 allreduced. Total work is fixed as tp
+grows (strong scaling). One "step" is one call of the megakernel.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints ONE JSON line on rank 0. Timing: every step is bracketed by CUDA
+events on the launching stream; L2 is flushed (a 256 MiB write) and the PEs
+are aligned by a device-side team barrier before every timed step, both
+outside the events; the whole timed region is bracketed by a barrier and a
+device synchronise; the reported time is the max over ranks.
+
+``--impl reference`` times the reference's path on the host cores instead:
+megacu has no CPU implementation of its GEMM/allreduce math (its numeric path
+is CUDA only), so this is the CPU restatement of its tile-task graph
+(oracle/, sequential-k fp32 tile GEMM + PE-order fp32 reduction), rank 0
+only, on a bounded sample of the same workload's output tiles.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, N, K_TOTAL = 4096, 8192, 8192
+WORKLOAD = "C2 row-parallel GEMM+allreduce M4096 N8192 K8192/tp bf16"
+METRIC = "GEMM+allreduce TFLOP/s (whole job), C2 M4096 N8192 K8192 split over tp"
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+FALLBACK_TFLOPS = 1590.0
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def seeded(seed, shape, std):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return FALLBACK_TFLOPS, "fallback (1.59 PFLOP/s, no MEASURED_PEAKS.json)"
+
+
+def traffic_for(key):
+    try:
+        with open(TRAFFIC_PATH) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU leg (oracle on the host cores): the reference arm and cpu_baseline
+# ---------------------------------------------------------------------------
+
+def cpu_sample(tp, seconds, threads):
+    """Times the CPU restatement on whole output tiles of the workload."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib
+    k = K_TOTAL // tp
+    a = [seeded(2000 + 10 * pe + 0, (M, k), 0.02).float().numpy() for pe in range(tp)]
+    b = [seeded(2000 + 10 * pe + 1, (k, N), 0.02).float().numpy() for pe in range(tp)]
+    tile_n = 256
+    tiles = (M // 128) * (N // tile_n)
+    rng = np.random.default_rng(0)
+    order = rng.permutation(tiles).astype(np.int32)
+    done, elapsed, i = 0, 0.0, 0
+    batch = max(threads, 1)
+    while (elapsed < seconds or done == 0) and i < tiles:
+        ids = order[i:i + batch]
+        t0 = time.perf_counter()
+        oracle_lib.bf16_tiles(a, b, ids, m=M, n=N, k=k, tile_n=tile_n, wire_bytes=2,
+                              threads=threads)
+        elapsed += time.perf_counter() - t0
+        done += len(ids)
+        i += batch
+    flops = 2.0 * 128 * tile_n * K_TOTAL * done
+    return flops / elapsed / 1e12, done, elapsed
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    tp = args.gpus
+    for _ in range(args.warmup):
+        cpu_sample(tp, 0.0, threads)
+    vals, per_step = [], []
+    for _ in range(args.steps):
+        v, done, el = cpu_sample(tp, args.cpu_seconds / max(args.steps, 1), threads)
+        vals.append(v)
+        per_step.append(el)
+    value = float(np.mean(vals))
+    sample = (f"{done} of {(M // 128) * (N // 256)} output tiles (128x256, full K={K_TOTAL} "
+              f"over {tp} logical PEs) per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * float(np.mean(per_step)), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "m": M, "n": N, "k_total": K_TOTAL, "tp": tp},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "megacu's GEMM/allreduce math exists only as a CUDA kernel; this arm is the "
+                "CPU restatement of its tile-task graph (oracle/) on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import megacu_b200 as mb
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    tp = world
+    k = K_TOTAL // tp
+    stream = torch.cuda.current_stream()
+
+    # ---- inputs (seeded per rank and tensor) ----
+    a_host = seeded(2000 + 10 * rank + 0, (M, k), 0.02).pin_memory()
+    b_host = seeded(2000 + 10 * rank + 1, (k, N), 0.02).pin_memory()
+    a = a_host.to(dev)
+    b = b_host.to(dev)
+
+    prob = mb.Problem(M, N, k, timeout_ns=30_000_000_000)
+    plan = mb.plan(prob, tp)
+    ws_bytes = mb.workspace_bytes(prob, tp)
+    ev_bytes = mb.events_bytes(prob, tp)
+    heap = ws_bytes + ev_bytes + M * N * 2 + (64 << 20)
+    exchange = mb.torch_exchange() if tp > 1 else None
+    team = mb.Team(rank, tp, local_rank, heap, exchange)
+    ws = team.tensor((max(ws_bytes, 16),), torch.uint8)
+    events = team.tensor((ev_bytes // 4,), torch.int32)
+    out = team.tensor((M, N), torch.bfloat16)
+    out_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def call(aa, bb):
+        mb.gemm_allreduce(aa, bb, out, workspace=ws, events=events, problem=prob, stream=stream,
+                          device=local_rank, team=team if tp > 1 else None)
+
+    def align():
+        flush.fill_(1)
+        if tp > 1:
+            team.barrier(stream)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if tp > 1:
+            dist.barrier()
+
+    def timed_steps(body, steps, warmup):
+        for _ in range(warmup):
+            align()
+            body()
+        sync_all()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for s, e in ev:
+            align()
+            s.record(stream)
+            body()
+            e.record(stream)
+        torch.cuda.synchronize()
+        ms = [s.elapsed_time(e) for s, e in ev]
+        total = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+        if tp > 1:
+            dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        sync_all()
+        return float(total.item()) / steps, ms
+
+    # ---- fused megakernel, inputs resident ----
+    with ClockSampler(local_rank) as clocks:
+        ms_fused, _ = timed_steps(lambda: call(a, b), args.steps, args.warmup)
+    mb.events_status(events, stream)
+    flops_total = 2.0 * M * N * K_TOTAL
+    flops_rank = flops_total / tp
+    value = flops_total / (ms_fused * 1e-3) / 1e12
+
+    # ---- end to end: pinned host inputs in, output back out ----
+    def e2e_body():
+        a.copy_(a_host, non_blocking=True)
+        b.copy_(b_host, non_blocking=True)
+        call(a, b)
+        out_host.copy_(out, non_blocking=True)
+
+    ms_e2e, _ = timed_steps(e2e_body, max(3, args.steps // 2), max(1, args.warmup // 2))
+    h2d = a_host.numel() * 2 + b_host.numel() * 2
+    d2h = out_host.numel() * 2
+
+    # ---- unfused baseline: cuBLAS GEMM then NCCL allreduce ----
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def unfused():
+        torch.matmul(a, b, out=c)
+        if tp > 1:
+            dist.all_reduce(c)
+
+    ms_unfused, _ = timed_steps(unfused, args.steps, args.warmup)
+    ms_gemm, _ = timed_steps(lambda: torch.matmul(a, b, out=c), args.steps, args.warmup)
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and tp == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        v, done, el = cpu_sample(tp, args.cpu_seconds, threads)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{done} output tiles of 128x256 with full K={K_TOTAL} "
+                         f"({el:.1f} s of CPU time, oracle/ restatement)"}
+
+    peak, peak_src = peaks()
+    achieved = flops_rank / (ms_fused * 1e-3) / 1e12
+    traffic = traffic_for(f"gemm_ar_megakernel_tp{tp}")
+    launches_per_step = 1 + (1 if tp > 1 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_fused,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "m": M, "n": N, "k_total": K_TOTAL, "k_per_pe": k,
+                       "tp": tp, "parallelism": f"tp{tp}", "tile": [plan.tile_m, plan.tile_n],
+                       "one_shot": plan.one_shot,
+                       "l2": "flushed (256 MiB write) before every timed step"},
+            "us_per_call": ms_fused * 1e3,
+            "tflops_per_gpu": achieved,
+            "e2e": {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e},
+            "gpu_launches": args.steps * launches_per_step,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": peak_src,
+                         "traffic": traffic,
+                         "kernel": "gemm_ar_megakernel", "per_launch_flops": flops_rank},
+            "cpu_baseline": cpu,
+            "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
+                                    "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
+                                    "tflops": flops_total / (ms_unfused * 1e-3) / 1e12},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    team.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="megacu_b200", choices=["megacu_b200", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_gpu(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

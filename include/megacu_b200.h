@@ -1,0 +1,273 @@
+/*
+ * megacu_b200 C ABI: the binary drop-in boundary of the fused
+ * GEMM + allreduce / reduce-scatter megakernel for B200 (sm_100a).
+ *
+ * Plain C: only pointers, sizes and POD structs cross this boundary. The
+ * structs below are layout-identical to megacu's C++ types so that a caller
+ * compiled against megacu's headers can bind these symbols directly:
+ *   megacu_status        == megacu::status          (views.h:27-31)
+ *   megacu_driver_view   == megacu::cuda_nvshmem::driver_view (runtime.h:416-419)
+ *   megacu_gemm_ar_problem == gemm_ar_problem       (examples/cuda_nvshmem/
+ *                                                    gemm_allreduce/common/
+ *                                                    gemm_allreduce.h:26-32)
+ *
+ * Conventions (same as megacu's launcher, megacu_gemm_allreduce_phased.cu:157-232):
+ *  - every call returns a status by value and never throws;
+ *  - the caller owns every buffer; nothing here allocates per call;
+ *  - a launch is asynchronous on driver.launch.stream; a null stream means
+ *    "validate only" and returns ok without touching the GPU;
+ *  - with team_n_pes > 1 every PE calls collectively, in the same order.
+ */
+#ifndef MEGACU_B200_H_
+#define MEGACU_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status and views (layout of megacu::status / driver_view) ---------- */
+
+enum megacu_status_code {
+  MEGACU_OK = 0,
+  MEGACU_INVALID_ARGUMENT = 1,
+  MEGACU_UNSUPPORTED = 2,
+  MEGACU_BACKEND_ERROR = 3,
+  MEGACU_LAUNCH_ERROR = 4
+};
+
+typedef struct megacu_status {
+  uint8_t code;        /* enum megacu_status_code */
+  uint16_t detail;     /* per-call-site number */
+  const char *message; /* static string, never freed */
+} megacu_status;
+
+typedef struct megacu_launch_view {
+  void *stream; /* cudaStream_t; NULL = validate only */
+  int32_t device_ordinal;
+} megacu_launch_view;
+
+typedef struct megacu_team_view {
+  void *team; /* megacu_b200_team handle when team_n_pes > 1, else NULL */
+  int32_t team_my_pe;
+  int32_t team_n_pes;
+  int32_t world_my_pe;
+  int32_t world_n_pes;
+  int32_t cuda_device_ordinal;
+  uint16_t backend;
+  uint64_t session;
+  uint8_t owner;
+} megacu_team_view;
+
+typedef struct megacu_driver_view {
+  megacu_launch_view launch;
+  megacu_team_view team;
+} megacu_driver_view;
+
+/* megacu's problem descriptor (fp32 launcher). */
+typedef struct megacu_gemm_ar_problem {
+  int64_t m;
+  int64_t n;
+  int64_t k;
+  int32_t tile_m;
+  int32_t tile_n;
+} megacu_gemm_ar_problem;
+
+/* ---- bf16 problem descriptor (new; no counterpart in megacu) ------------- */
+
+enum megacu_gemm_ar_mode {
+  MEGACU_MODE_ALLREDUCE = 0,     /* out[m, n] on every PE */
+  MEGACU_MODE_REDUCE_SCATTER = 1 /* PE p holds rows [p*m/tp, (p+1)*m/tp) */
+};
+
+enum megacu_gemm_ar_algo {
+  MEGACU_ALGO_AUTO = 0,
+  MEGACU_ALGO_ONE_SHOT = 1, /* every PE pushes its partial to every PE */
+  MEGACU_ALGO_TWO_SHOT = 2  /* push to the tile owner, owner reduces and
+                               pushes the sum to every PE */
+};
+
+/* Element type codes, numbered as megacu::dtype (views.h:12-17). */
+enum megacu_dtype {
+  MEGACU_DTYPE_UNKNOWN = 0,
+  MEGACU_DTYPE_F16 = 1,
+  MEGACU_DTYPE_BF16 = 2,
+  MEGACU_DTYPE_F32 = 3
+};
+
+typedef struct megacu_gemm_ar_problem_v2 {
+  int64_t m;             /* rows of A and of the full output */
+  int64_t n;             /* columns of B and of the output; multiple of 8 */
+  int64_t k;             /* this PE's slice of K; multiple of 8 */
+  int32_t tile_m;        /* 0 = auto (128) */
+  int32_t tile_n;        /* 0 = auto; else 64, 128 or 256 */
+  int32_t mode;          /* enum megacu_gemm_ar_mode */
+  int32_t algo;          /* enum megacu_gemm_ar_algo */
+  int32_t deterministic; /* 1 = partials cross NVLink as fp32 (one bf16
+                            rounding in total); 0 = as bf16. The rank-order
+                            fp32 reduction is fixed in both modes, so both are
+                            bit-reproducible run to run. */
+  int32_t dtype;         /* must be MEGACU_DTYPE_BF16 */
+  int32_t num_ctas;      /* 0 = one persistent CTA per SM */
+  int32_t reserved;
+  uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 2 s */
+  uint64_t *trace;       /* optional device buffer of trace records
+                            (4 x uint64 each), NULL = off */
+  int64_t trace_capacity; /* records that fit in `trace` */
+} megacu_gemm_ar_problem_v2;
+
+/* ---- megacu's fp32 phased launcher (binary drop-in) ---------------------- */
+
+/*
+ * Replaces megacu `megacu_cuda_gemm_allreduce_phased_f32`
+ * (examples/cuda_nvshmem/gemm_allreduce/phased/megacu/
+ *  megacu_gemm_allreduce_phased.cu:157-232; declared at
+ *  common/gemm_allreduce_orchestrate_common.h:8-11).
+ * out[m, n] = sum over PEs of a_pe[m, k] * b_pe[k, n], fp32, row-major.
+ * `partial` (>= m*n floats) and `events` (>= tiles*n_pes int32) must lie in
+ * the team's symmetric heap when team_n_pes > 1. Events are reset by the call.
+ */
+megacu_status megacu_cuda_gemm_allreduce_phased_f32(
+    megacu_driver_view driver, const float *a, const float *b, float *partial,
+    float *out, void *events, megacu_gemm_ar_problem problem);
+
+/* ---- bf16 fused megakernel (north-star path) ----------------------------- */
+
+/*
+ * Tensor-parallel bf16 GEMM (fp32 accumulate) fused with the allreduce of
+ * the per-PE partial products: out[m, n] = sum_pe a_pe[m, k] @ b_pe[k, n].
+ * a: row-major [m, k] bf16; b: row-major [k, n] bf16; out: row-major [m, n]
+ * bf16, in the symmetric heap when team_n_pes > 1.
+ * workspace: >= megacu_b200_workspace_bytes(); symmetric when team_n_pes > 1.
+ * events: >= megacu_b200_events_bytes(); symmetric when team_n_pes > 1,
+ * zero-filled once before first use, then reused across calls without reset.
+ * Replaces the same role as megacu_gemm_allreduce_phased.cu:157-232, for bf16.
+ */
+megacu_status megacu_cuda_gemm_allreduce_bf16(
+    megacu_driver_view driver, const void *a, const void *b, void *workspace,
+    void *out, void *events, megacu_gemm_ar_problem_v2 problem);
+
+/*
+ * Same GEMM fused with a reduce-scatter along M: PE p receives rows
+ * [p*m/tp, (p+1)*m/tp) of the sum in `out` (row-major [m/tp, n] bf16, local
+ * memory). m must be a multiple of tp * tile_m.
+ */
+megacu_status megacu_cuda_gemm_reduce_scatter_bf16(
+    megacu_driver_view driver, const void *a, const void *b, void *workspace,
+    void *out, void *events, megacu_gemm_ar_problem_v2 problem);
+
+/*
+ * Orchestrated entry: builds megacu's three-task phase (GEMM tile producer
+ * with tile_grid + publish, sync with join, reduce consumer with acquire),
+ * validates it with the dispatcher and ASAP scheduler, then calls the bf16
+ * launcher above (mode taken from problem.mode). Mirrors megacu
+ * `cuda_nvshmem_gemm_allreduce_phased_orchestrate`
+ * (phased/megacu/gemm_allreduce_phased_orchestrate.cc:3-20).
+ */
+megacu_status megacu_cuda_gemm_allreduce_bf16_orchestrate(
+    megacu_driver_view driver, const void *a, const void *b, void *workspace,
+    void *out, void *events, megacu_gemm_ar_problem_v2 problem);
+
+/*
+ * C-linkage form of megacu's fp32 orchestrate entry
+ * `cuda_nvshmem_gemm_allreduce_phased_orchestrate`
+ * (phased/megacu/gemm_allreduce_phased_orchestrate.cc:3-20): builds the same
+ * three-task phase, validates it, runs megacu_cuda_gemm_allreduce_phased_f32.
+ * The C++-linkage original is declared in <megacu/gemm_allreduce.h>.
+ */
+megacu_status megacu_cuda_gemm_allreduce_f32_orchestrate(
+    megacu_driver_view driver, const float *a, const float *b, float *partial,
+    float *out, void *events, megacu_gemm_ar_problem problem);
+
+/* Bytes of workspace / events a bf16 call needs for `problem` on n_pes PEs. */
+megacu_status megacu_b200_workspace_bytes(megacu_gemm_ar_problem_v2 problem,
+                                          int32_t n_pes, int64_t *bytes);
+megacu_status megacu_b200_events_bytes(megacu_gemm_ar_problem_v2 problem,
+                                       int32_t n_pes, int64_t *bytes);
+
+/*
+ * Tile plan of a bf16 call (host only, no GPU): info[0] tile_m, [1] tile_n,
+ * [2] m_tiles, [3] n_tiles, [4] one_shot, [5] receive slots per (parity, PE),
+ * [6] raster band height in tile rows, [7] bytes per element on the wire.
+ */
+megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem,
+                                    int32_t n_pes, int32_t info[8]);
+
+/*
+ * Where the device task queue sends raster index r (host only): out[0] tile
+ * row, out[1] tile column, out[2] owner PE, out[3] index among the owner's
+ * tiles. Tile id = out[0] * n_tiles + out[1].
+ */
+megacu_status megacu_b200_plan_tile(megacu_gemm_ar_problem_v2 problem,
+                                    int32_t n_pes, int32_t r, int32_t out[4]);
+
+/*
+ * Reads the device status word of `events` after the stream has finished
+ * (synchronises the stream). code MEGACU_OK if the last calls completed;
+ * MEGACU_BACKEND_ERROR with detail 40 if a cross-GPU wait timed out
+ * (info[0] = tile, info[1] = peer PE, info[2] = which wait) and 41 if a local
+ * pipeline wait timed out. The word is cleared by the call.
+ */
+megacu_status megacu_b200_events_status(void *events, void *stream,
+                                        int64_t info[4]);
+
+/*
+ * Cumulative device counters kept in `events` (task and event completions):
+ * counters[0] GEMM tile tasks, [1] reduce tasks, [2] partial publishes,
+ * [3] partial acquires, [4] final-tile publishes, [5] final-tile acquires,
+ * [6] launches. Synchronises the stream.
+ */
+megacu_status megacu_b200_events_counters(void *events, void *stream,
+                                          uint64_t counters[8]);
+
+/* ---- team: symmetric heap over NVLink peer mappings ---------------------- */
+
+/* Size of the opaque handle a PE exports for its heap. */
+#define MEGACU_B200_TEAM_HANDLE_BYTES 128
+
+/*
+ * Creates this PE's team object and its symmetric heap (one cudaMalloc of
+ * heap_bytes on `device`, zero-filled). Replaces nvshmem_init + the
+ * symmetric heap of megacu's NVSHMEM backend (backends/nvshmem.h:19-38).
+ */
+megacu_status megacu_b200_team_create(int32_t my_pe, int32_t n_pes,
+                                      int32_t device, int64_t heap_bytes,
+                                      void **team);
+/* Writes this PE's heap handle (MEGACU_B200_TEAM_HANDLE_BYTES bytes). */
+megacu_status megacu_b200_team_export(void *team, void *handle);
+/* Maps every peer's heap; handles = n_pes handles in PE order. */
+megacu_status megacu_b200_team_connect(void *team, const void *handles);
+/*
+ * Bump-allocates `bytes` (256-byte aligned) from the symmetric heap. Every PE
+ * must make the same sequence of calls, as with nvshmem_malloc.
+ */
+megacu_status megacu_b200_team_malloc(void *team, int64_t bytes, void **ptr);
+megacu_status megacu_b200_team_info(void *team, int32_t *my_pe,
+                                    int32_t *n_pes, void **heap_base,
+                                    int64_t *heap_bytes);
+/*
+ * Enqueues a team-wide barrier on `stream` (a one-warp kernel over the peer
+ * flags; bounded). Replaces nvshmem_barrier_all at megacu's call sites
+ * (megacu_gemm_allreduce_phased.cu:186-193) without a host synchronisation.
+ */
+megacu_status megacu_b200_team_barrier(void *team, void *stream);
+megacu_status megacu_b200_team_destroy(void *team);
+
+/* ---- component link anchors (megacu src/*: last line of each file) ------- */
+
+int megacu_dispatcher_explicit_attrs_component(void);
+int megacu_scheduler_explicit_asap_component(void);
+int megacu_platform_cuda_component(void);
+int megacu_backend_nvshmem_component(void);
+int megacu_target_runtime_component(void);
+
+/* Library version string. */
+const char *megacu_b200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEGACU_B200_H_ */

@@ -1,0 +1,293 @@
+"""Python host mirror of megacu's GEMM + allreduce entry points.
+
+Thin wrappers over the C ABI (``include/megacu_b200.h``): torch tensors are
+only device-memory holders here, every byte of work runs in
+``libmegacu_b200.so``. Names and argument meaning follow megacu:
+
+* :func:`cuda_nvshmem_gemm_allreduce_phased_orchestrate` — megacu's fp32
+  orchestrate entry (phased/megacu/gemm_allreduce_phased_orchestrate.cc:3-20);
+* :func:`megacu_cuda_gemm_allreduce_phased_f32` — its native launcher
+  (megacu_gemm_allreduce_phased.cu:157-232);
+* :func:`gemm_allreduce` / :func:`gemm_reduce_scatter` — the bf16 fused
+  megakernel (B200 path), orchestrated through the same phase API;
+* :class:`Team` — the symmetric heap that replaces NVSHMEM's.
+
+Errors come back as :class:`MegacuError` carrying megacu's status code and
+per-site detail number.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable, Optional, Sequence
+
+from . import _capi
+from ._capi import DriverView, GemmArProblem, GemmArProblemV2, Status
+
+
+class MegacuError(RuntimeError):
+    def __init__(self, status: Status):
+        self.code = int(status.code)
+        self.detail = int(status.detail)
+        self.message = status.message.decode() if status.message else ""
+        super().__init__(f"megacu {_capi.STATUS_NAMES[self.code]} (detail {self.detail}): "
+                         f"{self.message}")
+
+
+def check(status: Status) -> Status:
+    if status.code != _capi.OK:
+        raise MegacuError(status)
+    return status
+
+
+def lib() -> ctypes.CDLL:
+    return _capi.load()
+
+
+def _ptr(x) -> Optional[int]:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream_handle(stream) -> Optional[int]:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+# ---- team ----------------------------------------------------------------------
+
+class Team:
+    """This PE's symmetric heap, mapped by every peer of the team.
+
+    ``exchange`` maps this PE's handle (bytes) to the list of every PE's
+    handle in PE order — e.g. :func:`torch_exchange` over torch.distributed.
+    Every PE must create the team and allocate from it in the same order
+    (as with ``nvshmem_init`` / ``nvshmem_malloc``).
+    """
+
+    def __init__(self, my_pe: int, n_pes: int, device: int, heap_bytes: int,
+                 exchange: Optional[Callable[[bytes], Sequence[bytes]]] = None):
+        self.my_pe, self.n_pes, self.device = my_pe, n_pes, device
+        handle = ctypes.c_void_p()
+        check(lib().megacu_b200_team_create(my_pe, n_pes, device, heap_bytes,
+                                            ctypes.byref(handle)))
+        self.handle = handle.value
+        if n_pes > 1:
+            if exchange is None:
+                raise ValueError("a team of more than one PE needs an exchange function")
+            mine = ctypes.create_string_buffer(_capi.TEAM_HANDLE_BYTES)
+            check(lib().megacu_b200_team_export(self.handle, mine))
+            handles = list(exchange(mine.raw))
+            if len(handles) != n_pes or any(len(h) != _capi.TEAM_HANDLE_BYTES for h in handles):
+                raise ValueError("exchange must return one 128-byte handle per PE")
+            blob = ctypes.create_string_buffer(b"".join(handles), n_pes * _capi.TEAM_HANDLE_BYTES)
+            check(lib().megacu_b200_team_connect(self.handle, blob))
+        base = ctypes.c_void_p()
+        size = ctypes.c_int64()
+        check(lib().megacu_b200_team_info(self.handle, None, None, ctypes.byref(base),
+                                          ctypes.byref(size)))
+        self.heap_base, self.heap_bytes = base.value, size.value
+
+    def malloc(self, nbytes: int) -> int:
+        ptr = ctypes.c_void_p()
+        check(lib().megacu_b200_team_malloc(self.handle, nbytes, ctypes.byref(ptr)))
+        return ptr.value
+
+    def tensor(self, shape, dtype):
+        """A torch tensor over a fresh symmetric allocation (zero-filled heap)."""
+        import torch
+        numel = 1
+        for s in shape:
+            numel *= s
+        itemsize = torch.empty((), dtype=dtype).element_size()
+        ptr = self.malloc(max(numel * itemsize, 16))
+        return tensor_from_pointer(ptr, shape, dtype, self.device, owner=self)
+
+    def barrier(self, stream=None) -> None:
+        check(lib().megacu_b200_team_barrier(self.handle, _stream_handle(stream)))
+
+    def close(self) -> None:
+        if self.handle is not None:
+            check(lib().megacu_b200_team_destroy(self.handle))
+            self.handle = None
+
+    def view(self) -> _capi.TeamView:
+        return _capi.TeamView(team=self.handle, team_my_pe=self.my_pe, team_n_pes=self.n_pes,
+                              world_my_pe=self.my_pe, world_n_pes=self.n_pes,
+                              cuda_device_ordinal=self.device)
+
+
+def torch_exchange(group=None) -> Callable[[bytes], Sequence[bytes]]:
+    """Handle exchange over torch.distributed (any backend; gloo works)."""
+    import torch.distributed as dist
+
+    def exchange(mine: bytes) -> Sequence[bytes]:
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, mine, group=group)
+        return out
+
+    return exchange
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr, owner):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+        self._owner = owner
+
+
+def tensor_from_pointer(ptr: int, shape, dtype, device: int, owner=None):
+    """Wraps device memory at ``ptr`` as a torch tensor (no copy, no ownership)."""
+    import torch
+    codes = {torch.bfloat16: ("<i2", torch.bfloat16), torch.float16: ("<f2", None),
+             torch.float32: ("<f4", None), torch.int32: ("<i4", None),
+             torch.uint8: ("|u1", None), torch.int64: ("<i8", None)}
+    typestr, view_as = codes[dtype]
+    with torch.cuda.device(device):
+        t = torch.as_tensor(_CudaArray(ptr, shape, typestr, owner), device=f"cuda:{device}")
+    return t.view(view_as) if view_as is not None else t
+
+
+# ---- driver views ------------------------------------------------------------------
+
+def driver_view(stream=None, device: int = 0, team: Optional[Team] = None) -> DriverView:
+    """megacu's driver_view{launch_view, team_view} for this PE."""
+    d = DriverView()
+    d.launch.stream = _stream_handle(stream)
+    d.launch.device_ordinal = device
+    if team is not None:
+        d.team = team.view()
+    else:
+        d.team.team_my_pe, d.team.team_n_pes = 0, 1
+        d.team.world_my_pe, d.team.world_n_pes = 0, 1
+        d.team.cuda_device_ordinal = device
+    return d
+
+
+# ---- bf16 fused megakernel ---------------------------------------------------------
+
+@dataclass
+class Problem:
+    """megacu_gemm_ar_problem_v2: out[m, n] = sum over PEs of a[m, k] @ b[k, n]."""
+    m: int
+    n: int
+    k: int
+    mode: int = _capi.MODE_ALLREDUCE
+    algo: int = _capi.ALGO_AUTO
+    deterministic: bool = False
+    tile_n: int = 0
+    num_ctas: int = 0
+    timeout_ns: int = 0
+
+    def to_c(self, trace_ptr: Optional[int] = None, trace_capacity: int = 0) -> GemmArProblemV2:
+        return GemmArProblemV2(m=self.m, n=self.n, k=self.k, tile_m=0, tile_n=self.tile_n,
+                               mode=self.mode, algo=self.algo,
+                               deterministic=1 if self.deterministic else 0,
+                               dtype=_capi.DTYPE_BF16, num_ctas=self.num_ctas, reserved=0,
+                               timeout_ns=self.timeout_ns, trace=trace_ptr,
+                               trace_capacity=trace_capacity)
+
+
+def workspace_bytes(problem: Problem, n_pes: int) -> int:
+    out = ctypes.c_int64()
+    check(lib().megacu_b200_workspace_bytes(problem.to_c(), n_pes, ctypes.byref(out)))
+    return out.value
+
+
+def events_bytes(problem: Problem, n_pes: int) -> int:
+    out = ctypes.c_int64()
+    check(lib().megacu_b200_events_bytes(problem.to_c(), n_pes, ctypes.byref(out)))
+    return out.value
+
+
+@dataclass
+class Plan:
+    tile_m: int
+    tile_n: int
+    m_tiles: int
+    n_tiles: int
+    one_shot: bool
+    slots_per_src: int
+    group_m: int
+    wire_bytes: int
+
+    @property
+    def tiles(self) -> int:
+        return self.m_tiles * self.n_tiles
+
+
+def plan(problem: Problem, n_pes: int) -> Plan:
+    info = (ctypes.c_int32 * 8)()
+    check(lib().megacu_b200_plan_info(problem.to_c(), n_pes, info))
+    return Plan(info[0], info[1], info[2], info[3], bool(info[4]), info[5], info[6], info[7])
+
+
+def plan_tile(problem: Problem, n_pes: int, r: int) -> tuple[int, int, int, int]:
+    """(tile_row, tile_col, owner, local index) of raster index ``r``."""
+    out = (ctypes.c_int32 * 4)()
+    check(lib().megacu_b200_plan_tile(problem.to_c(), n_pes, r, out))
+    return tuple(out)
+
+
+def gemm_allreduce(a, b, out, *, workspace, events, problem: Problem, stream=None,
+                   device: int = 0, team: Optional[Team] = None, trace=None,
+                   orchestrate: bool = True) -> None:
+    """Launches the fused bf16 GEMM + allreduce / reduce-scatter (async).
+
+    ``orchestrate=True`` goes through megacu's phase API (dispatcher +
+    scheduler validation, then the launcher), as megacu's orchestrate entry
+    does; ``False`` calls the launcher directly.
+    """
+    trace_ptr = _ptr(trace)
+    cap = trace.numel() // 4 if trace is not None else 0
+    d = driver_view(stream, device, team)
+    p = problem.to_c(trace_ptr, cap)
+    args = (d, _ptr(a), _ptr(b), _ptr(workspace), _ptr(out), _ptr(events), p)
+    if orchestrate:
+        check(lib().megacu_cuda_gemm_allreduce_bf16_orchestrate(*args))
+    elif problem.mode == _capi.MODE_REDUCE_SCATTER:
+        check(lib().megacu_cuda_gemm_reduce_scatter_bf16(*args))
+    else:
+        check(lib().megacu_cuda_gemm_allreduce_bf16(*args))
+
+
+def gemm_reduce_scatter(a, b, out, *, workspace, events, problem: Problem, **kw) -> None:
+    problem.mode = _capi.MODE_REDUCE_SCATTER
+    gemm_allreduce(a, b, out, workspace=workspace, events=events, problem=problem, **kw)
+
+
+def events_status(events, stream=None) -> list[int]:
+    """Synchronises ``stream`` and raises MegacuError if a device wait failed."""
+    info = (ctypes.c_int64 * 4)()
+    check(lib().megacu_b200_events_status(_ptr(events), _stream_handle(stream), info))
+    return list(info)
+
+
+def events_counters(events, stream=None) -> list[int]:
+    out = (ctypes.c_uint64 * 8)()
+    check(lib().megacu_b200_events_counters(_ptr(events), _stream_handle(stream), out))
+    return list(out)
+
+
+# ---- megacu's fp32 phased entry points -------------------------------------------------
+
+def megacu_cuda_gemm_allreduce_phased_f32(driver: DriverView, a, b, partial, out, events,
+                                          m: int, n: int, k: int, tile_m: int,
+                                          tile_n: int) -> Status:
+    return lib().megacu_cuda_gemm_allreduce_phased_f32(
+        driver, _ptr(a), _ptr(b), _ptr(partial), _ptr(out), _ptr(events),
+        GemmArProblem(m=m, n=n, k=k, tile_m=tile_m, tile_n=tile_n))
+
+
+def cuda_nvshmem_gemm_allreduce_phased_orchestrate(driver: DriverView, a, b, partial, out,
+                                                   events, m: int, n: int, k: int,
+                                                   tile_m: int, tile_n: int) -> Status:
+    return lib().megacu_cuda_gemm_allreduce_f32_orchestrate(
+        driver, _ptr(a), _ptr(b), _ptr(partial), _ptr(out), _ptr(events),
+        GemmArProblem(m=m, n=n, k=k, tile_m=tile_m, tile_n=tile_n))

@@ -1,0 +1,652 @@
+// Persistent sm_100a megakernel: tensor-parallel bf16 GEMM tiles (fp32
+// accumulate in TMEM) fused with the allreduce / reduce-scatter of their
+// outputs over NVLink peer memory.
+//
+// This is megacu's phased GEMM+AllReduce (megacu_gemm_allreduce_phased.cu:
+// 56-148, three tasks per tile: 0 = GEMM tile producer, 1 = sync,
+// 2 = allreduce consumer, with an event tensor between task 0 and task 2)
+// re-designed for B200:
+//
+//  * one CTA per SM, 10 warps with fixed roles
+//      warp 0      task fetcher + TMA producer (GEMM task queue)
+//      warp 1      TMEM allocator + tcgen05.mma issuer (one thread)
+//      warps 2..5  epilogue: TMEM -> registers -> bf16/fp32 -> destination,
+//                  then publish (task 0's "after" hook)
+//      warps 6..9  reduce workers (task 2): each warp independently pulls
+//                  quarter-tile sub-tasks from the reduce queue, acquires
+//                  the event tensor, sums the PE partials in PE order in
+//                  fp32 and writes the result (plus the all-gather push)
+//  * the static tile_grid dispatcher (tile = blockIdx + i * gridDim,
+//    tile_grid_device.cuh:13-23) is replaced by device task queues: an
+//    atomic ticket per queue, tickets mapped to tiles by tile_schedule.h;
+//  * the event tensor is per (PE, tile, 32-row quarter), tagged with the
+//    call's epoch, published with st.release.sys after a sys-scope fence and
+//    acquired with ld.acquire.sys under a bounded wait;
+//  * partial tiles are pushed (not pulled): each epilogue warp stores its 32
+//    rows straight into the owner's receive slot over NVLink.
+//
+// No loads here use cluster multicast.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include <megacu/backends/nvshmem.h>
+
+#include "layout.h"
+#include "sm100_ptx.cuh"
+#include "tile_schedule.h"
+
+namespace megacu_b200 {
+
+inline constexpr int kBlockM = 128;
+inline constexpr int kBlockK = 64;
+inline constexpr int kThreads = 320;
+inline constexpr int kTaskRing = 4;
+inline constexpr int kEpilogueWarp0 = 2;
+inline constexpr int kReduceWarp0 = 6;
+inline constexpr int kReduceWarps = 4;
+inline constexpr std::uint64_t kLocalTimeoutNs = 4000000000ull;
+
+template <int BN>
+struct gemm_config {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "tile_n must be 64, 128 or 256");
+  static constexpr int a_bytes = kBlockM * kBlockK * 2;        // 16 KiB
+  static constexpr int b_panel_bytes = kBlockK * 64 * 2;       // 8 KiB per 64 columns
+  static constexpr int b_bytes = kBlockK * BN * 2;
+  static constexpr int stage_bytes = a_bytes + b_bytes;
+  static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8
+  static constexpr int reduce_bytes = kReduceWarps * 32 * 128; // transpose tiles
+  static constexpr int n_barriers = 2 * stages + 4 + 2 * kTaskRing + 1;
+  static constexpr int aux_bytes = n_barriers * 8 + kTaskRing * 4 + 16;
+  static constexpr int smem_bytes = 1024 + stages * stage_bytes + reduce_bytes + aux_bytes;
+  static constexpr int tmem_columns = 2 * BN;
+};
+
+struct gemm_ar_params {
+  std::int32_t m, n, k;
+  std::int32_t m_tiles, n_tiles, tiles;
+  std::int32_t n_pes, my_pe;
+  std::int32_t mode;          // mode_allreduce / mode_reduce_scatter
+  std::int32_t one_shot;      // 1: every PE reduces every tile
+  std::int32_t group_m;
+  std::int32_t n_reduce;      // reduce sub-tasks on this PE (quarters)
+  std::int32_t slots_per_src; // receive slots per (parity, src)
+  std::int32_t rows_per_pe;   // reduce-scatter: output rows per PE
+  std::uint64_t timeout_ns;   // bound of cross-GPU waits
+  __nv_bfloat16 *out;         // this PE's output
+  char *workspace;            // this PE's receive slots (symmetric)
+  std::uint32_t *events;      // this PE's events buffer (symmetric)
+  megacu::nvshmem::peer_table peers;
+  unsigned long long *trace;
+  std::int64_t trace_capacity;
+};
+
+namespace detail {
+
+__device__ __forceinline__ control_block *control(gemm_ar_params const &p) {
+  return reinterpret_cast<control_block *>(p.events);
+}
+
+__device__ __forceinline__ std::uint32_t *event_words(std::uint32_t *events) {
+  return reinterpret_cast<std::uint32_t *>(reinterpret_cast<char *>(events) + kControlBytes);
+}
+
+__device__ __forceinline__ void record_error(gemm_ar_params const &p, std::uint32_t code,
+                                             std::uint32_t tile, std::uint32_t peer,
+                                             std::uint32_t site) {
+  control_block *c = control(p);
+  if (atomicCAS(&c->error_code, 0u, code) == 0u) {
+    c->error_info[0] = tile;
+    c->error_info[1] = peer;
+    c->error_info[2] = site;
+  }
+  atomicAdd(&c->counters[ctr_errors], 1ull);
+}
+
+__device__ __forceinline__ void count(gemm_ar_params const &p, int which,
+                                      unsigned long long v) {
+  atomicAdd(&control(p)->counters[which], v);
+}
+
+__device__ __forceinline__ void trace(gemm_ar_params const &p, std::uint32_t kind,
+                                      std::uint32_t sub, std::uint32_t ticket,
+                                      std::uint32_t tile, std::uint64_t t0) {
+  if (p.trace == nullptr) {
+    return;
+  }
+  std::uint32_t const i = atomicAdd(&control(p)->trace_count, 1u);
+  if (static_cast<std::int64_t>(i) >= p.trace_capacity) {
+    return;
+  }
+  unsigned long long *rec = p.trace + static_cast<std::int64_t>(i) * 4;
+  rec[0] = static_cast<unsigned long long>(kind) | (static_cast<unsigned long long>(sub) << 8) |
+           (static_cast<unsigned long long>(blockIdx.x) << 16) |
+           (static_cast<unsigned long long>(ticket) << 32);
+  rec[1] = tile;
+  rec[2] = t0;
+  rec[3] = ptx::now_ns();
+}
+
+// Waits until `*flag == want`, polling with a short back-off. Gives up when
+// the abort word is set or `timeout_ns` elapses.
+__device__ __forceinline__ bool wait_flag(std::uint32_t const *flag, std::uint32_t want,
+                                          std::uint32_t const *abort_word,
+                                          std::uint64_t timeout_ns) {
+  if (ptx::ld_acquire_sys(flag) == want) {
+    return true;
+  }
+  std::uint64_t const start = ptx::now_ns();
+  for (std::uint32_t spin = 1;; ++spin) {
+    __nanosleep(spin < 64 ? 32 : 256);
+    if (ptx::ld_acquire_sys(flag) == want) {
+      return true;
+    }
+    if ((spin & 15u) == 0) {
+      if (ptx::ld_relaxed_gpu(abort_word) != 0) {
+        return false;
+      }
+      if (ptx::now_ns() - start > timeout_ns) {
+        return false;
+      }
+    }
+  }
+}
+
+// Byte offset of receive slot (parity, src, j).
+__device__ __forceinline__ std::int64_t slot_offset(gemm_ar_params const &p, std::uint32_t parity,
+                                                    std::int32_t src, std::int32_t j,
+                                                    std::int64_t slot_bytes) {
+  return ((static_cast<std::int64_t>(parity) * p.n_pes + src) * p.slots_per_src + j) *
+         slot_bytes;
+}
+
+}  // namespace detail
+
+template <int BN, bool kWireF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_ar_megakernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ gemm_ar_params p) {
+  using cfg = gemm_config<BN>;
+  constexpr int kWireBytes = kWireF32 ? 4 : 2;
+  constexpr int kVecCols = 16 / kWireBytes;                   // columns per 16 B wire vector
+  constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
+
+  extern __shared__ std::uint8_t smem_raw[];
+  std::uint32_t const raw_addr = ptx::smem_addr(smem_raw);
+  std::uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  std::uint8_t *stages = smem;
+  std::uint8_t *reduce_smem = smem + cfg::stages * cfg::stage_bytes;
+  auto *bars = reinterpret_cast<std::uint64_t *>(reduce_smem + cfg::reduce_bytes);
+  std::uint64_t *full = bars;
+  std::uint64_t *empty = full + cfg::stages;
+  std::uint64_t *acc_full = empty + cfg::stages;
+  std::uint64_t *acc_empty = acc_full + 2;
+  std::uint64_t *task_full = acc_empty + 2;
+  std::uint64_t *task_empty = task_full + kTaskRing;
+  std::uint64_t *mma_done = task_empty + kTaskRing;
+  auto *ring = reinterpret_cast<std::int32_t volatile *>(mma_done + 1);
+  auto *tmem_slot = reinterpret_cast<std::uint32_t *>(const_cast<std::int32_t *>(ring) + kTaskRing);
+  auto *epoch_slot = tmem_slot + 1;
+
+  int const warp = threadIdx.x / 32;
+  std::uint32_t const lane = threadIdx.x % 32;
+  control_block *ctrl = detail::control(p);
+  std::uint32_t const *abort_word = &ctrl->error_code;
+  tile_schedule const sched{p.m_tiles, p.n_tiles, p.n_pes, p.mode, p.group_m};
+  std::int32_t const k_blocks = (p.k + kBlockK - 1) / kBlockK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < cfg::stages; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&acc_full[b], 1);
+      ptx::mbar_init(&acc_empty[b], 4);
+    }
+    for (int i = 0; i < kTaskRing; ++i) {
+      ptx::mbar_init(&task_full[i], 1);
+      ptx::mbar_init(&task_empty[i], 5);
+    }
+    ptx::mbar_init(mma_done, 1);
+    ptx::fence_barrier_init();
+    *epoch_slot = ptx::ld_relaxed_gpu(&ctrl->launch_count) + 1u;
+    ptx::prefetch_tensor_map(&map_a);
+    ptx::prefetch_tensor_map(&map_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, cfg::tmem_columns);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before_sync();
+  __syncthreads();
+  ptx::tc_fence_after_sync();
+  std::uint32_t const tmem_base = *tmem_slot;
+  std::uint32_t const epoch = *epoch_slot;
+  std::uint32_t const parity = epoch & 1u;
+  std::uint32_t *const my_events = detail::event_words(p.events);
+
+  if (warp == 0) {
+    // ---------------- task fetcher + TMA producer ----------------
+    if (lane == 0) {
+      std::uint32_t it = 0;
+      bool ok = true;
+      for (std::uint32_t n = 0; ok; ++n) {
+        std::uint32_t const slot = n % kTaskRing;
+        if (!ptx::mbar_wait(&task_empty[slot], ((n / kTaskRing) & 1u) ^ 1u, abort_word,
+                            kLocalTimeoutNs)) {
+          detail::record_error(p, err_local_timeout, 0, 0, 1);
+          break;
+        }
+        std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
+        std::int32_t const r = ticket < static_cast<std::uint32_t>(p.tiles)
+                                   ? static_cast<std::int32_t>(ticket)
+                                   : -1;
+        ring[slot] = r;
+        ptx::mbar_arrive(&task_full[slot]);
+        if (r < 0) {
+          break;
+        }
+        tile_coord const c = locate(sched, r);
+        for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          std::uint32_t const s = it % cfg::stages;
+          if (!ptx::mbar_wait(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word,
+                              kLocalTimeoutNs)) {
+            detail::record_error(p, err_local_timeout, r, 0, 2);
+            ok = false;
+            break;
+          }
+          std::uint8_t *sa = stages + s * cfg::stage_bytes;
+          std::uint8_t *sb = sa + cfg::a_bytes;
+          ptx::mbar_arrive_expect_tx(&full[s], cfg::stage_bytes);
+          ptx::tma_load_2d(&map_a, &full[s], sa, kb * kBlockK, c.tile_row * kBlockM);
+#pragma unroll
+          for (int panel = 0; panel < BN / 64; ++panel) {
+            ptx::tma_load_2d(&map_b, &full[s], sb + panel * cfg::b_panel_bytes,
+                             c.tile_col * BN + panel * 64, kb * kBlockK);
+          }
+        }
+      }
+      // Drain: the most recent load of every stage must have landed before
+      // this CTA may exit (normally they were all consumed already).
+      for (std::uint32_t back = 1; back <= cfg::stages && back <= it; ++back) {
+        std::uint32_t const i = it - back;
+        ptx::mbar_wait(&full[i % cfg::stages], (i / cfg::stages) & 1u, nullptr,
+                       kLocalTimeoutNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- tcgen05.mma issuer ----------------
+    if (lane == 0) {
+      std::uint32_t const idesc = ptx::idesc_bf16_f32(kBlockM, BN, true);
+      std::uint32_t it = 0;
+      for (std::uint32_t n = 0;; ++n) {
+        std::uint32_t const slot = n % kTaskRing;
+        if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word,
+                            kLocalTimeoutNs)) {
+          detail::record_error(p, err_local_timeout, 0, 0, 3);
+          break;
+        }
+        std::int32_t const r = ring[slot];
+        ptx::mbar_arrive(&task_empty[slot]);
+        if (r < 0) {
+          break;
+        }
+        std::uint32_t const buf = n & 1u;
+        if (!ptx::mbar_wait(&acc_empty[buf], ((n >> 1) & 1u) ^ 1u, abort_word,
+                            kLocalTimeoutNs)) {
+          detail::record_error(p, err_local_timeout, r, 0, 4);
+          break;
+        }
+        ptx::tc_fence_after_sync();
+        std::uint32_t const d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          std::uint32_t const s = it % cfg::stages;
+          if (!ptx::mbar_wait(&full[s], (it / cfg::stages) & 1u, abort_word, kLocalTimeoutNs)) {
+            detail::record_error(p, err_local_timeout, r, 0, 5);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after_sync();
+          std::uint32_t const a_addr = ptx::smem_addr(stages + s * cfg::stage_bytes);
+          std::uint32_t const b_addr = a_addr + cfg::a_bytes;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            // A: K-major, 128 B swizzle, 8-row groups 1024 B apart; a K step
+            // of 16 elements is 32 B along the swizzled row.
+            std::uint64_t const a_desc = ptx::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            // B: MN-major, 128 B swizzle; 64-column panels `b_panel_bytes`
+            // apart (leading), 8-k-row groups 1024 B apart (stride); a K step
+            // of 16 rows is 2048 B.
+            std::uint64_t const b_desc =
+                ptx::smem_desc_sw128(b_addr + kk * 2048, cfg::b_panel_bytes, 1024);
+            ptx::umma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          ptx::umma_commit(&empty[s]);
+        }
+        if (!ok) {
+          break;
+        }
+        ptx::umma_commit(&acc_full[buf]);
+      }
+      // Every issued MMA must be complete before TMEM is released.
+      ptx::umma_commit(mma_done);
+      ptx::mbar_wait(mma_done, 0, nullptr, kLocalTimeoutNs);
+    }
+  } else if (warp < kReduceWarp0) {
+    // ---------------- epilogue: TMEM -> destination, publish ----------------
+    std::int32_t const quarter = warp % 4;  // TMEM lanes [32q, 32q+32)
+    std::int32_t const row_in_tile = quarter * 32 + static_cast<std::int32_t>(lane);
+    for (std::uint32_t n = 0;; ++n) {
+      std::uint32_t const slot = n % kTaskRing;
+      if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word,
+                          kLocalTimeoutNs)) {
+        if (lane == 0) detail::record_error(p, err_local_timeout, 0, 0, 6);
+        break;
+      }
+      std::int32_t const r = ring[slot];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&task_empty[slot]);
+      if (r < 0) {
+        break;
+      }
+      std::uint32_t const buf = n & 1u;
+      if (!ptx::mbar_wait(&acc_full[buf], (n >> 1) & 1u, abort_word, kLocalTimeoutNs)) {
+        if (lane == 0) detail::record_error(p, err_local_timeout, r, 0, 7);
+        break;
+      }
+      ptx::tc_fence_after_sync();
+      std::uint64_t const t0 = ptx::now_ns();
+      tile_coord const c = locate(sched, r);
+      std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+      std::int32_t const grow = c.tile_row * kBlockM + row_in_tile;
+      std::int32_t const gcol0 = c.tile_col * BN;
+      std::uint32_t const t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) +
+                                  buf * BN;
+      // Destinations of this tile's partial (n_pes > 1).
+      std::int32_t const first_dst = p.one_shot ? 0 : c.owner;
+      std::int32_t const n_dst = p.n_pes == 1 ? 0 : (p.one_shot ? p.n_pes : 1);
+      std::int32_t const slot_j = p.one_shot ? r : c.local;
+      // A 32-row quarter wholly below m carries no data: it is neither sent
+      // nor published, and no reduce task exists for it.
+      bool const active = c.tile_row * kBlockM + quarter * 32 < p.m;
+
+#pragma unroll 1
+      for (int ch = 0; active && ch < BN / 32; ++ch) {
+        std::uint32_t v[32];
+        ptx::tmem_load_32x32b_x32(t_row + ch * 32, v);
+        ptx::tmem_wait_load();
+        if (p.n_pes == 1) {
+          if (grow < p.m) {
+            __nv_bfloat16 *dst = p.out + static_cast<std::int64_t>(grow) * p.n;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              std::int32_t const col = gcol0 + ch * 32 + j * 8;
+              if (col < p.n) {
+                uint4 q;
+                q.x = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 0]), __uint_as_float(v[8 * j + 1]));
+                q.y = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+                q.z = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+                q.w = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+                ptx::st_v4(dst + col, q);
+              }
+            }
+          }
+        } else {
+          constexpr int kVecs = 32 / kVecCols;  // wire vectors per 32-column chunk
+          uint4 q[kVecs];
+#pragma unroll
+          for (int j = 0; j < kVecs; ++j) {
+            if constexpr (kWireF32) {
+              q[j] = make_uint4(v[4 * j + 0], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            } else {
+              q[j].x = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 0]), __uint_as_float(v[8 * j + 1]));
+              q[j].y = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+              q[j].z = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+              q[j].w = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+            }
+          }
+          for (std::int32_t d = 0; d < n_dst; ++d) {
+            std::int32_t const pe = first_dst + d;
+            char *slot_base = p.peers.translate(p.workspace, pe) +
+                              detail::slot_offset(p, parity, p.my_pe, slot_j, kSlotBytes);
+#pragma unroll
+            for (int j = 0; j < kVecs; ++j) {
+              std::int64_t const vec = ch * kVecs + j;
+              ptx::st_v4(slot_base + (vec * kBlockM + row_in_tile) * 16, q[j]);
+            }
+          }
+        }
+      }
+      // TMEM buffer is free for the next tile once every lane has read it.
+      ptx::tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+
+      if (lane == 0 && quarter == 0) {
+        detail::count(p, ctr_gemm_tasks, 1);
+        detail::trace(p, 0, 0, static_cast<std::uint32_t>(r), tile, t0);
+      }
+      if (!active) {
+        continue;
+      }
+      // Publish this quarter (task 0 "after" hook).
+      if (p.n_pes > 1) {
+        ptx::fence_acq_rel_sys();
+      } else {
+        __threadfence();
+      }
+      __syncwarp();
+      if (p.n_pes == 1) {
+        if (lane == 0) {
+          ptx::st_release_sys(my_events + event_index(parity, 0, tile, quarter, 1, p.tiles), epoch);
+          ptx::st_release_sys(my_events + event_index(parity, 1, tile, quarter, 1, p.tiles), epoch);
+        }
+      } else if (static_cast<std::int32_t>(lane) < n_dst) {
+        std::int32_t const pe = first_dst + static_cast<std::int32_t>(lane);
+        std::uint32_t *flags = p.peers.translate(my_events, pe);
+        ptx::st_release_sys(flags + event_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles),
+                            epoch);
+      }
+      if (lane == 0) {
+        detail::count(p, ctr_partial_publish, p.n_pes == 1 ? 1 : n_dst);
+      }
+    }
+  } else if (p.n_pes > 1) {
+    // ---------------- reduce workers (task 2) ----------------
+    int const rw = warp - kReduceWarp0;
+    std::uint8_t *xpose = reduce_smem + rw * (32 * 128);
+    for (;;) {
+      std::uint32_t ticket = 0;
+      if (lane == 0) ticket = atomicAdd(&ctrl->reduce_ticket, 1u);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket >= static_cast<std::uint32_t>(p.n_reduce)) {
+        break;
+      }
+      std::int32_t const j = static_cast<std::int32_t>(ticket) / kQuarters;
+      std::int32_t const quarter = static_cast<std::int32_t>(ticket) % kQuarters;
+      std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
+      tile_coord const c = locate(sched, r);
+      std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+      if (c.tile_row * kBlockM + quarter * 32 >= p.m) {
+        continue;  // no rows of this quarter exist
+      }
+
+      // Acquire: every PE's partial of this quarter has arrived (task 2
+      // "before" hook).
+      bool ok = true;
+      if (static_cast<std::int32_t>(lane) < p.n_pes) {
+        ok = detail::wait_flag(
+            my_events + event_index(parity, lane, tile, quarter, p.n_pes, p.tiles), epoch,
+            abort_word, p.timeout_ns);
+        if (!ok) detail::record_error(p, err_remote_timeout, tile, lane, 8);
+      }
+      if (!__all_sync(0xffffffffu, ok)) {
+        break;
+      }
+      std::uint64_t const t0 = ptx::now_ns();
+
+      std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
+      char const *slots0 = p.workspace + detail::slot_offset(p, parity, 0, j, kSlotBytes);
+      std::int64_t const src_stride = static_cast<std::int64_t>(p.slots_per_src) * kSlotBytes;
+      std::int32_t const out_row0 =
+          p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
+      bool const push_all = p.mode == mode_allreduce && !p.one_shot;
+
+      // 64-column blocks: sum the PE partials of rows [row0, row0 + 32) in
+      // PE order, transpose through shared memory, store row-major.
+#pragma unroll 1
+      for (int cb = 0; cb < BN / 64; ++cb) {
+        float acc[8][8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+        }
+#pragma unroll 1
+        for (std::int32_t src = 0; src < p.n_pes; ++src) {
+          char const *slot = slots0 + src * src_stride;
+          if constexpr (kWireF32) {
+            uint4 w[16];
+#pragma unroll
+            for (int h = 0; h < 16; ++h) {
+              std::int64_t const vec = cb * 16 + h;
+              w[h] = ptx::ld_cg_v4(slot + (vec * kBlockM + quarter * 32 + lane) * 16);
+            }
+#pragma unroll
+            for (int h = 0; h < 16; ++h) {
+              acc[h / 2][(h % 2) * 4 + 0] += __uint_as_float(w[h].x);
+              acc[h / 2][(h % 2) * 4 + 1] += __uint_as_float(w[h].y);
+              acc[h / 2][(h % 2) * 4 + 2] += __uint_as_float(w[h].z);
+              acc[h / 2][(h % 2) * 4 + 3] += __uint_as_float(w[h].w);
+            }
+          } else {
+            uint4 w[8];
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              std::int64_t const vec = cb * 8 + g;
+              w[g] = ptx::ld_cg_v4(slot + (vec * kBlockM + quarter * 32 + lane) * 16);
+            }
+#pragma unroll
+            for (int g = 0; g < 8; ++g) {
+              acc[g][0] += ptx::bf16_lo(w[g].x);
+              acc[g][1] += ptx::bf16_hi(w[g].x);
+              acc[g][2] += ptx::bf16_lo(w[g].y);
+              acc[g][3] += ptx::bf16_hi(w[g].y);
+              acc[g][4] += ptx::bf16_lo(w[g].z);
+              acc[g][5] += ptx::bf16_hi(w[g].z);
+              acc[g][6] += ptx::bf16_lo(w[g].w);
+              acc[g][7] += ptx::bf16_hi(w[g].w);
+            }
+          }
+        }
+        // Row `lane` of the 32 x 64 block -> shared, 16 B per 8 columns,
+        // XOR-swizzled so that both the write and the read are conflict-free.
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          uint4 q;
+          q.x = ptx::pack_bf16x2(acc[g][0], acc[g][1]);
+          q.y = ptx::pack_bf16x2(acc[g][2], acc[g][3]);
+          q.z = ptx::pack_bf16x2(acc[g][4], acc[g][5]);
+          q.w = ptx::pack_bf16x2(acc[g][6], acc[g][7]);
+          *reinterpret_cast<uint4 *>(xpose + lane * 128 + ((g ^ (lane & 7)) * 16)) = q;
+        }
+        __syncwarp();
+        // Read back row-major: 8 lanes cover one 128 B row segment.
+        std::int32_t const g = lane % 8;
+        std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
+          uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
+          if (row0 + rr < p.m && col < p.n) {
+            std::int64_t const off = static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
+            if (push_all) {
+              for (std::int32_t pe = 0; pe < p.n_pes; ++pe) {
+                ptx::st_v4(p.peers.translate(p.out, pe) + off, q);
+              }
+            } else {
+              ptx::st_v4(p.out + off, q);
+            }
+          }
+        }
+        __syncwarp();
+      }
+
+      if (push_all) {
+        // All-gather publish: this quarter of the summed tile is in every
+        // PE's output.
+        ptx::fence_acq_rel_sys();
+        __syncwarp();
+        if (static_cast<std::int32_t>(lane) < p.n_pes) {
+          std::uint32_t *flags = p.peers.translate(my_events, lane);
+          ptx::st_release_sys(flags + event_index(parity, p.n_pes, tile, quarter, p.n_pes, p.tiles),
+                              epoch);
+        }
+      }
+      if (lane == 0) {
+        detail::count(p, ctr_reduce_tasks, 1);
+        detail::count(p, ctr_partial_acquire, p.n_pes);
+        if (push_all) detail::count(p, ctr_final_publish, p.n_pes);
+        detail::trace(p, 2, quarter, ticket, tile, t0);
+      }
+    }
+
+    if (p.mode == mode_allreduce && !p.one_shot) {
+      // This PE's output is complete once every quarter's final flag is set.
+      std::int32_t const total = p.tiles * kQuarters;
+      std::int32_t const workers = gridDim.x * kReduceWarps;
+      std::int32_t const worker = blockIdx.x * kReduceWarps + rw;
+      std::uint32_t seen = 0;
+      for (std::int32_t base = worker * 32; base < total; base += workers * 32) {
+        std::int32_t const idx = base + static_cast<std::int32_t>(lane);
+        bool ok = true;
+        bool const active = idx < total && (idx / kQuarters / p.n_tiles) * kBlockM +
+                                                   (idx % kQuarters) * 32 < p.m;
+        if (active) {
+          ok = detail::wait_flag(my_events + event_index(parity, p.n_pes, 0, 0, p.n_pes, p.tiles) + idx,
+                                 epoch, abort_word, p.timeout_ns);
+          if (!ok) {
+            detail::record_error(p, err_remote_timeout, idx / kQuarters, 0xffffffffu, 9);
+          } else {
+            ++seen;
+          }
+        }
+        if (!__all_sync(0xffffffffu, ok)) {
+          break;
+        }
+      }
+      for (int off = 16; off > 0; off >>= 1) seen += __shfl_xor_sync(0xffffffffu, seen, off);
+      if (lane == 0 && seen != 0) detail::count(p, ctr_final_acquire, seen);
+    }
+  }
+
+  // ---------------- teardown ----------------
+  ptx::tc_fence_before_sync();
+  __syncthreads();
+  ptx::tc_fence_after_sync();
+  if (warp == 1) {
+    ptx::tmem_dealloc(tmem_base, cfg::tmem_columns);
+  }
+  if (threadIdx.x == 0) {
+    __threadfence();
+    std::uint32_t const done = atomicAdd(&ctrl->done_ctas, 1u);
+    if (done == gridDim.x - 1) {
+      // Last CTA of this launch: rewind the queues and advance the epoch.
+      __threadfence();
+      ctrl->gemm_ticket = 0;
+      ctrl->reduce_ticket = 0;
+      ctrl->trace_count = 0;
+      ctrl->launch_count = epoch;
+      atomicAdd(&ctrl->counters[ctr_launches], 1ull);
+      __threadfence();
+      atomicExch(&ctrl->done_ctas, 0u);
+    }
+  }
+}
+
+}  // namespace megacu_b200

@@ -1,0 +1,86 @@
+// Memory layout of the caller-provided `events` and `workspace` buffers of
+// the bf16 megakernel.
+//
+// events (uint32 words, symmetric when n_pes > 1):
+//   [0, 256 B)  control block: device task-queue tickets, the launch counter
+//               that tags every flag with the call's epoch, the error word
+//               and cumulative completion counters.
+//   [256 B, …)  event tensor, uint32 [2 parity][n_pes + 1][tiles][4 quarters]
+//     arrive[p][src][t][q] = epoch once PE `src` has delivered rows
+//                            [32q, 32q + 32) of its partial tile t;
+//     final [p][t][q]      = arrive[p][n_pes][t][q] = epoch once rows
+//                            [32q, 32q + 32) of the summed tile t are in this
+//                            PE's `out` (two-shot allreduce; written by the
+//                            owner on every PE).
+//   This is megacu's event tensor int32 [n_pes][tiles]
+//   (backends/nvshmem/cuda_event_tensor.cuh:13-39) refined to quarter tiles
+//   and tagged with the epoch (the golden's ready_base idiom,
+//   golden_gemm_allreduce.cu:384-385) so consecutive calls need no memset and
+//   no host barrier; the parity plane lets a PE run one call ahead of a slow
+//   owner in reduce-scatter mode.
+//
+// workspace (symmetric when n_pes > 1): receive slots
+//   slot[p][src][j] = one tile_m x tile_n partial tile of PE `src`, j = the
+//   tile's index among the receiver's tiles (two-shot / RS) or its raster
+//   index (one-shot). Inside a slot, 16-byte vectors are stored column-major
+//   over rows: vector (v, row) at byte (v * tile_m + row) * 16, which is the
+//   order the TMEM epilogue produces them in (one warp store = 512 B).
+#pragma once
+
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define MEGACU_B200_LAYOUT_HD __host__ __device__
+#else
+#define MEGACU_B200_LAYOUT_HD
+#endif
+
+namespace megacu_b200 {
+
+inline constexpr std::int64_t kControlBytes = 256;
+inline constexpr std::int32_t kQuarters = 4;  // 32-row quarters of a 128-row tile
+
+struct control_block {
+  std::uint32_t gemm_ticket;    // next GEMM raster index to hand out
+  std::uint32_t reduce_ticket;  // next reduce sub-task to hand out
+  std::uint32_t done_ctas;      // CTAs finished in this launch
+  std::uint32_t launch_count;   // completed launches on this buffer
+  std::uint32_t error_code;     // 0 = ok; non-zero = first error seen
+  std::uint32_t error_info[3];  // tile, peer, site of that error
+  std::uint32_t trace_count;    // trace records written
+  std::uint32_t reserved[7];
+  unsigned long long counters[8];
+};
+static_assert(sizeof(control_block) <= kControlBytes, "control block too large");
+
+enum : std::uint32_t {
+  err_none = 0,
+  err_remote_timeout = 40,  // a cross-GPU flag never arrived
+  err_local_timeout = 41,   // an on-chip pipeline wait timed out
+};
+
+enum : std::int32_t {
+  ctr_gemm_tasks = 0,
+  ctr_reduce_tasks = 1,
+  ctr_partial_publish = 2,
+  ctr_partial_acquire = 3,
+  ctr_final_publish = 4,
+  ctr_final_acquire = 5,
+  ctr_launches = 6,
+  ctr_errors = 7,
+};
+
+// Word index of arrive[p][src][t][q] inside the event tensor.
+MEGACU_B200_LAYOUT_HD inline std::int64_t event_index(std::int32_t parity, std::int32_t src,
+                                                    std::int32_t tile, std::int32_t quarter,
+                                                    std::int32_t n_pes, std::int32_t tiles) {
+  return ((static_cast<std::int64_t>(parity) * (n_pes + 1) + src) * tiles + tile) * kQuarters +
+         quarter;
+}
+
+inline std::int64_t events_bytes_for(std::int32_t n_pes, std::int32_t tiles) {
+  return kControlBytes +
+         static_cast<std::int64_t>(2) * (n_pes + 1) * tiles * kQuarters * 4;
+}
+
+}  // namespace megacu_b200

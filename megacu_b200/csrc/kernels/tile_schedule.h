@@ -1,0 +1,87 @@
+// Tile schedule of the fused GEMM + allreduce / reduce-scatter megakernel.
+//
+// The output [m, n] is cut into tile_m x tile_n tiles, tile id
+// t = tile_row * n_tiles + tile_col (megacu's decomposition,
+// megacu_gemm_allreduce_phased.cu:64-80). Tiles are handed out in "raster
+// order": raster index r = 0, 1, ... is what the device task queue hands to
+// the next free CTA. The raster order walks bands of `group_m` tile rows
+// column by column, so the CTAs working at the same time share A row panels
+// and B column panels in L2.
+//
+// Ownership (who reduces a tile) rotates with the raster index, r % n_pes,
+// so every PE receives reducible tiles from the start of the GEMM. For
+// reduce-scatter the owner is fixed by the output rows instead: PE q owns
+// tile rows [q * mq, (q + 1) * mq); raster index r then walks PE (r % n_pes)'s
+// block, so ownership still rotates in time.
+//
+// The same arithmetic is restated in C in oracle/oracle.c (oracle_locate).
+#pragma once
+
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define MEGACU_B200_HD __host__ __device__ __forceinline__
+#else
+#define MEGACU_B200_HD inline
+#endif
+
+namespace megacu_b200 {
+
+enum : std::int32_t { mode_allreduce = 0, mode_reduce_scatter = 1 };
+
+struct tile_schedule {
+  std::int32_t m_tiles = 0;
+  std::int32_t n_tiles = 0;
+  std::int32_t n_pes = 1;
+  std::int32_t mode = mode_allreduce;
+  std::int32_t group_m = 16;
+
+  MEGACU_B200_HD std::int32_t tiles() const { return m_tiles * n_tiles; }
+};
+
+struct tile_coord {
+  std::int32_t tile_row = 0;
+  std::int32_t tile_col = 0;
+  std::int32_t owner = 0;  // PE that reduces this tile (two-shot / RS)
+  std::int32_t local = 0;  // index of this tile among its owner's tiles
+};
+
+// Grouped raster walk of an (rows x cols) tile grid: r -> (row, col).
+MEGACU_B200_HD void grouped_raster(std::int32_t r, std::int32_t rows, std::int32_t cols,
+                                   std::int32_t group, std::int32_t &row,
+                                   std::int32_t &col) {
+  std::int32_t const band_tiles = group * cols;
+  std::int32_t const band = r / band_tiles;
+  std::int32_t const first_row = band * group;
+  std::int32_t const left = rows - first_row;
+  std::int32_t const band_rows = left < group ? left : group;
+  std::int32_t const within = r - band * band_tiles;
+  row = first_row + within % band_rows;
+  col = within / band_rows;
+}
+
+MEGACU_B200_HD tile_coord locate(tile_schedule const &s, std::int32_t r) {
+  tile_coord c;
+  c.owner = r % s.n_pes;
+  c.local = r / s.n_pes;
+  if (s.mode == mode_reduce_scatter) {
+    std::int32_t const mq = s.m_tiles / s.n_pes;
+    std::int32_t row = 0;
+    grouped_raster(c.local, mq, s.n_tiles, s.group_m < mq ? s.group_m : mq, row,
+                   c.tile_col);
+    c.tile_row = c.owner * mq + row;
+  } else {
+    grouped_raster(r, s.m_tiles, s.n_tiles, s.group_m, c.tile_row, c.tile_col);
+  }
+  return c;
+}
+
+// Number of tiles PE q reduces under the two-shot / reduce-scatter split.
+MEGACU_B200_HD std::int32_t owned_tiles(tile_schedule const &s, std::int32_t q) {
+  std::int32_t const t = s.tiles();
+  return t > q ? (t - q + s.n_pes - 1) / s.n_pes : 0;
+}
+
+}  // namespace megacu_b200
+
+#undef MEGACU_B200_HD

@@ -1,0 +1,361 @@
+/*
+ * TEST INFRASTRUCTURE ONLY — CPU oracle of the fused GEMM + allreduce /
+ * reduce-scatter path (see oracle.h for what it restates and where each
+ * part comes from in the reference). Nothing in the product links this.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---- fp32 GEMM, k ascending, one fmaf per step ---------------------------
+ * Restates golden/golden_gemm_allreduce.cu:85-96 and
+ * megacu_gemm_allreduce_phased.cu:82-87 (`value += a * b`, which nvcc
+ * contracts to a fused multiply-add). Iterating k in the outer loop of a row
+ * block keeps that per-element order while streaming b rows. */
+void oracle_gemm_block(const float *a, const float *b, float *c, int64_t m, int64_t n,
+                       int64_t k, int64_t r0, int64_t r1, int64_t c0, int64_t c1) {
+  (void)m;
+  enum { kColBlock = 512, kDepthBlock = 128 };
+  for (int64_t r = r0; r < r1; ++r) {
+    for (int64_t j = c0; j < c1; ++j) c[r * n + j] = 0.0f;
+  }
+  /* Blocked over columns and k so the b panel stays in cache; every element
+   * still accumulates k = 0, 1, ..., k-1 in that order. */
+  for (int64_t cb = c0; cb < c1; cb += kColBlock) {
+    int64_t const ce = cb + kColBlock < c1 ? cb + kColBlock : c1;
+    int64_t const w = ce - cb;
+    for (int64_t k0 = 0; k0 < k; k0 += kDepthBlock) {
+      int64_t const k1 = k0 + kDepthBlock < k ? k0 + kDepthBlock : k;
+      for (int64_t r = r0; r < r1; ++r) {
+        float *crow = c + r * n + cb;
+        const float *arow = a + r * k;
+        for (int64_t kk = k0; kk < k1; ++kk) {
+          float const av = arow[kk];
+          const float *brow = b + kk * n + cb;
+          for (int64_t j = 0; j < w; ++j) crow[j] = fmaf(av, brow[j], crow[j]);
+        }
+      }
+    }
+  }
+}
+
+typedef struct gemm_job {
+  const float *a, *b;
+  float *c;
+  int64_t m, n, k, r0, r1;
+} gemm_job;
+
+static void *gemm_worker(void *arg) {
+  gemm_job *j = (gemm_job *)arg;
+  oracle_gemm_block(j->a, j->b, j->c, j->m, j->n, j->k, j->r0, j->r1, 0, j->n);
+  return NULL;
+}
+
+void oracle_gemm_f32(const float *a, const float *b, float *c, int64_t m, int64_t n, int64_t k,
+                     int32_t threads) {
+  if (threads <= 1 || m < 2) {
+    oracle_gemm_block(a, b, c, m, n, k, 0, m, 0, n);
+    return;
+  }
+  if (threads > m) threads = (int32_t)m;
+  pthread_t *tid = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)threads);
+  gemm_job *jobs = (gemm_job *)malloc(sizeof(gemm_job) * (size_t)threads);
+  for (int32_t t = 0; t < threads; ++t) {
+    jobs[t].a = a;
+    jobs[t].b = b;
+    jobs[t].c = c;
+    jobs[t].m = m;
+    jobs[t].n = n;
+    jobs[t].k = k;
+    jobs[t].r0 = m * t / threads;
+    jobs[t].r1 = m * (t + 1) / threads;
+    pthread_create(&tid[t], NULL, gemm_worker, &jobs[t]);
+  }
+  for (int32_t t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+  free(jobs);
+  free(tid);
+}
+
+float oracle_round_bf16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) {
+    if (u & 0x007fffffu) u |= 0x00400000u; /* quiet NaN */
+    u &= 0xffff0000u;
+  } else {
+    uint32_t const lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    u &= 0xffff0000u;
+  }
+  memcpy(&x, &u, 4);
+  return x;
+}
+
+/* ---- megacu's phased fp32 graph -------------------------------------------- */
+
+int oracle_phased_f32(int64_t m, int64_t n, int64_t k, int32_t tile_m, int32_t tile_n,
+                      int32_t n_pes, const float *const *a, const float *const *b,
+                      float *const *out, int32_t *const *events) {
+  int64_t const n_tiles = (n + tile_n - 1) / tile_n;
+  int64_t const tiles = ((m + tile_m - 1) / tile_m) * n_tiles;
+  float **partial = (float **)calloc((size_t)n_pes, sizeof(float *));
+  int rc = 0;
+  for (int32_t pe = 0; pe < n_pes; ++pe) {
+    memset(events[pe], 0, sizeof(int32_t) * (size_t)(tiles * n_pes));
+  }
+  /* Task 0 on every PE, tile by tile, then publish tile + 1 into every PE's
+   * slot [pe][tile] (cuda_event_tensor.cuh:19-31). */
+  for (int32_t pe = 0; pe < n_pes; ++pe) {
+    partial[pe] = (float *)calloc((size_t)(m * n), sizeof(float));
+    for (int64_t t = 0; t < tiles; ++t) {
+      int64_t const r0 = (t / n_tiles) * tile_m, c0 = (t % n_tiles) * tile_n;
+      int64_t const r1 = r0 + tile_m < m ? r0 + tile_m : m;
+      int64_t const c1 = c0 + tile_n < n ? c0 + tile_n : n;
+      oracle_gemm_block(a[pe], b[pe], partial[pe], m, n, k, r0, r1, c0, c1);
+      for (int32_t dst = 0; dst < n_pes; ++dst) events[dst][pe * tiles + t] = (int32_t)(t + 1);
+    }
+  }
+  /* Task 2 on every PE: acquire all slots of the tile, then sum in PE order
+   * (megacu_gemm_allreduce_phased.cu:118-130). */
+  for (int32_t pe = 0; pe < n_pes && rc == 0; ++pe) {
+    for (int64_t t = 0; t < tiles && rc == 0; ++t) {
+      for (int32_t src = 0; src < n_pes; ++src) {
+        if (events[pe][src * tiles + t] != (int32_t)(t + 1)) rc = -1;
+      }
+      int64_t const r0 = (t / n_tiles) * tile_m, c0 = (t % n_tiles) * tile_n;
+      for (int64_t r = r0; r < r0 + tile_m && r < m; ++r) {
+        for (int64_t c = c0; c < c0 + tile_n && c < n; ++c) {
+          float s = 0.0f;
+          for (int32_t src = 0; src < n_pes; ++src) s += partial[src][r * n + c];
+          out[pe][r * n + c] = s;
+        }
+      }
+    }
+  }
+  for (int32_t pe = 0; pe < n_pes; ++pe) free(partial[pe]);
+  free(partial);
+  return rc;
+}
+
+/* ---- B200 megakernel schedule (restates tile_schedule.h) ------------------- */
+
+static void grouped_raster(int32_t r, int32_t rows, int32_t cols, int32_t group, int32_t *row,
+                           int32_t *col) {
+  int32_t const band_tiles = group * cols;
+  int32_t const band = r / band_tiles;
+  int32_t const first = band * group;
+  int32_t const left = rows - first;
+  int32_t const band_rows = left < group ? left : group;
+  int32_t const within = r - band * band_tiles;
+  *row = first + within % band_rows;
+  *col = within / band_rows;
+}
+
+void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode,
+                   int32_t group_m, int32_t r, int32_t out[4]) {
+  out[2] = r % n_pes;
+  out[3] = r / n_pes;
+  if (mode == 1) {
+    int32_t const mq = m_tiles / n_pes;
+    int32_t row, col;
+    grouped_raster(out[3], mq, n_tiles, group_m < mq ? group_m : mq, &row, &col);
+    out[0] = out[2] * mq + row;
+    out[1] = col;
+  } else {
+    grouped_raster(r, m_tiles, n_tiles, group_m, &out[0], &out[1]);
+  }
+}
+
+static int64_t ev_index(int32_t parity, int32_t src, int32_t tile, int32_t quarter, int32_t n_pes,
+                        int32_t tiles) {
+  return (((int64_t)parity * (n_pes + 1) + src) * tiles + tile) * 4 + quarter;
+}
+
+int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
+                     const float *const *b, float *const *out, uint32_t *const *events,
+                     uint64_t *counters, int32_t *gemm_order, int32_t *const *reduce_order) {
+  int32_t const np = p->n_pes;
+  int64_t const m = p->m, n = p->n;
+  int32_t const mt = (int32_t)((m + p->tile_m - 1) / p->tile_m);
+  int32_t const nt = (int32_t)((n + p->tile_n - 1) / p->tile_n);
+  int32_t const tiles = mt * nt;
+  uint32_t const epoch = p->epoch;
+  int32_t const parity = (int32_t)(epoch & 1u);
+  int const two_shot_ar = p->mode == 0 && !p->one_shot && np > 1;
+  int rc = 0;
+  uint64_t local_counters[8 * 8];
+  uint64_t *cnt = counters != NULL ? counters : local_counters;
+  memset(cnt, 0, sizeof(uint64_t) * 8 * (size_t)np);
+
+  /* Every PE's full partial product (what its GEMM tiles produce). */
+  float **part = (float **)calloc((size_t)np, sizeof(float *));
+  for (int32_t pe = 0; pe < np; ++pe) {
+    part[pe] = (float *)malloc(sizeof(float) * (size_t)(m * n));
+    oracle_gemm_f32(a[pe], b[pe], part[pe], m, n, p->k, p->threads);
+    if (np > 1 && p->wire_bytes == 2) {
+      for (int64_t i = 0; i < m * n; ++i) part[pe][i] = oracle_round_bf16(part[pe][i]);
+    }
+  }
+
+  /* Task 0 (GEMM tile) + its publish, in queue (raster) order. */
+  for (int32_t r = 0; r < tiles; ++r) {
+    int32_t c[4];
+    oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
+    int32_t const t = c[0] * nt + c[1];
+    if (gemm_order) gemm_order[r] = t;
+    for (int32_t pe = 0; pe < np; ++pe) {
+      cnt[pe * 8 + 0] += 1;
+      for (int32_t q = 0; q < 4; ++q) {
+        if ((int64_t)c[0] * p->tile_m + q * 32 >= m) continue;
+        if (np == 1) {
+          if (events) {
+            events[0][ev_index(parity, 0, t, q, 1, tiles)] = epoch;
+            events[0][ev_index(parity, 1, t, q, 1, tiles)] = epoch;
+          }
+          cnt[pe * 8 + 2] += 1;
+        } else {
+          int32_t const first = p->one_shot ? 0 : c[2];
+          int32_t const n_dst = p->one_shot ? np : 1;
+          for (int32_t d = 0; d < n_dst; ++d) {
+            if (events) events[first + d][ev_index(parity, pe, t, q, np, tiles)] = epoch;
+          }
+          cnt[pe * 8 + 2] += (uint64_t)n_dst;
+        }
+      }
+    }
+  }
+
+  if (np == 1) {
+    memcpy(out[0], part[0], sizeof(float) * (size_t)(m * n));
+  } else {
+    int64_t const rows_per_pe = m / np;
+    for (int32_t me = 0; me < np && rc == 0; ++me) {
+      int32_t owned = p->one_shot ? tiles : (tiles > me ? (tiles - me + np - 1) / np : 0);
+      for (int32_t ticket = 0; ticket < owned * 4 && rc == 0; ++ticket) {
+        int32_t const j = ticket / 4, q = ticket % 4;
+        int32_t const r = p->one_shot ? j : j * np + me;
+        int32_t c[4];
+        oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
+        int32_t const t = c[0] * nt + c[1];
+        int64_t const row0 = (int64_t)c[0] * p->tile_m + q * 32;
+        if (row0 >= m) {
+          if (reduce_order) reduce_order[me][ticket] = -1;
+          continue;
+        }
+        if (reduce_order) reduce_order[me][ticket] = t;
+        /* Task 2 "before": acquire every PE's quarter. */
+        if (events) {
+          for (int32_t src = 0; src < np; ++src) {
+            if (events[me][ev_index(parity, src, t, q, np, tiles)] != epoch) rc = -2;
+          }
+        }
+        cnt[me * 8 + 1] += 1;
+        cnt[me * 8 + 3] += (uint64_t)np;
+        int64_t const c0 = (int64_t)c[1] * p->tile_n;
+        for (int64_t row = row0; row < row0 + 32 && row < m; ++row) {
+          for (int64_t col = c0; col < c0 + p->tile_n && col < n; ++col) {
+            float s = 0.0f;
+            for (int32_t src = 0; src < np; ++src) s += part[src][row * n + col];
+            if (p->mode == 1) {
+              out[me][(row - me * rows_per_pe) * n + col] = s;
+            } else if (p->one_shot) {
+              out[me][row * n + col] = s;
+            } else {
+              for (int32_t pe = 0; pe < np; ++pe) out[pe][row * n + col] = s;
+            }
+          }
+        }
+        if (two_shot_ar) {
+          for (int32_t pe = 0; pe < np; ++pe) {
+            if (events) events[pe][ev_index(parity, np, t, q, np, tiles)] = epoch;
+          }
+          cnt[me * 8 + 4] += (uint64_t)np;
+        }
+      }
+    }
+    if (two_shot_ar) {
+      /* Every PE waits for every final quarter before its call completes. */
+      for (int32_t pe = 0; pe < np; ++pe) {
+        for (int32_t t = 0; t < tiles; ++t) {
+          for (int32_t q = 0; q < 4; ++q) {
+            if ((int64_t)(t / nt) * p->tile_m + q * 32 >= m) continue;
+            if (events && events[pe][ev_index(parity, np, t, q, np, tiles)] != epoch) rc = -3;
+            cnt[pe * 8 + 5] += 1;
+          }
+        }
+      }
+    }
+  }
+  for (int32_t pe = 0; pe < np; ++pe) {
+    cnt[pe * 8 + 6] += 1;
+    free(part[pe]);
+  }
+  free(part);
+  return rc;
+}
+
+/* ---- CPU-baseline sample: a list of output tiles -------------------------- */
+
+typedef struct tile_job {
+  const oracle_bf16_problem *p;
+  const float *const *a;
+  const float *const *b;
+  const int32_t *tile_ids;
+  int32_t first, last;
+  float *out;
+} tile_job;
+
+static void *tile_worker(void *arg) {
+  tile_job *j = (tile_job *)arg;
+  const oracle_bf16_problem *p = j->p;
+  int64_t const n = p->n, m = p->m;
+  int32_t const nt = (int32_t)((n + p->tile_n - 1) / p->tile_n);
+  float *scratch = (float *)malloc(sizeof(float) * (size_t)(p->tile_m * n));
+  for (int32_t i = j->first; i < j->last; ++i) {
+    int32_t const t = j->tile_ids[i];
+    int64_t const r0 = (int64_t)(t / nt) * p->tile_m, c0 = (int64_t)(t % nt) * p->tile_n;
+    int64_t const r1 = r0 + p->tile_m < m ? r0 + p->tile_m : m;
+    int64_t const c1 = c0 + p->tile_n < n ? c0 + p->tile_n : n;
+    for (int64_t r = r0; r < r1; ++r)
+      for (int64_t c = c0; c < c1; ++c) j->out[r * n + c] = 0.0f;
+    for (int32_t pe = 0; pe < p->n_pes; ++pe) {
+      /* Partial rows [r0, r1) of PE pe, computed into a row-offset scratch. */
+      oracle_gemm_block(j->a[pe] + r0 * p->k, j->b[pe], scratch, r1 - r0, n, p->k, 0, r1 - r0, c0,
+                        c1);
+      for (int64_t r = r0; r < r1; ++r) {
+        for (int64_t c = c0; c < c1; ++c) {
+          float v = scratch[(r - r0) * n + c];
+          if (p->n_pes > 1 && p->wire_bytes == 2) v = oracle_round_bf16(v);
+          j->out[r * n + c] += v;
+        }
+      }
+    }
+  }
+  free(scratch);
+  return NULL;
+}
+
+void oracle_bf16_tiles(const oracle_bf16_problem *p, const float *const *a,
+                       const float *const *b, const int32_t *tile_ids, int32_t n_listed,
+                       float *out_full) {
+  int32_t threads = p->threads > 0 ? p->threads : 1;
+  if (threads > n_listed) threads = n_listed > 0 ? n_listed : 1;
+  pthread_t *tid = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)threads);
+  tile_job *jobs = (tile_job *)malloc(sizeof(tile_job) * (size_t)threads);
+  for (int32_t t = 0; t < threads; ++t) {
+    jobs[t].p = p;
+    jobs[t].a = a;
+    jobs[t].b = b;
+    jobs[t].tile_ids = tile_ids;
+    jobs[t].first = n_listed * t / threads;
+    jobs[t].last = n_listed * (t + 1) / threads;
+    jobs[t].out = out_full;
+    pthread_create(&tid[t], NULL, tile_worker, &jobs[t]);
+  }
+  for (int32_t t = 0; t < threads; ++t) pthread_join(tid[t], NULL);
+  free(jobs);
+  free(tid);
+}

@@ -1,0 +1,106 @@
+/*
+ * TEST INFRASTRUCTURE ONLY — the CPU oracle of the fused GEMM + allreduce /
+ * reduce-scatter path. Only tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline legs may load it, and only as the checker or the timed CPU
+ * baseline; the product path never calls it.
+ *
+ * It restates, in plain C, megacu's tile-task graph:
+ *   - the fp32 tile GEMM with k ascending, one fused multiply-add per step
+ *     (golden/golden_gemm_allreduce.cu:65-98,
+ *      phased/megacu/megacu_gemm_allreduce_phased.cu:56-89);
+ *   - the reduction out = sum over PEs in PE order 0..n-1, fp32
+ *     (golden_gemm_allreduce.cu:192-240, megacu_gemm_allreduce_phased.cu:91-133);
+ *   - the event tensor int32 [n_pes][tiles], slot = pe * tiles + tile, ready
+ *     value tile + 1 (backends/nvshmem/cuda_event_tensor.cuh:13-58);
+ * and, for the B200 megakernel, the same graph with the device task queue's
+ * raster order, the tile ownership of two-shot / one-shot allreduce and
+ * reduce-scatter, and the epoch-tagged quarter-tile event tensor (restated
+ * from megacu_b200/csrc/kernels/tile_schedule.h and layout.h).
+ *
+ * Parity pins: the reference's known-answer tests
+ * (tests/runtime/cuda_gemm_allreduce_correctness.cc:92-99 and
+ *  tests/runtime/nvshmem_two_rank_smoke.cc:101-102) are committed as
+ * fixtures in tests/golden/ and checked by tests/test_oracle.py.
+ */
+#ifndef MEGACU_B200_ORACLE_H_
+#define MEGACU_B200_ORACLE_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* c[m, n] = a[m, k] @ b[k, n], fp32, k ascending with fmaf per step, rows
+ * split over `threads` POSIX threads (the order per element is unchanged). */
+void oracle_gemm_f32(const float *a, const float *b, float *c, int64_t m, int64_t n,
+                     int64_t k, int32_t threads);
+
+/* The same for the sub-block rows [r0, r1) x cols [c0, c1) of c (ldc = n). */
+void oracle_gemm_block(const float *a, const float *b, float *c, int64_t m, int64_t n,
+                       int64_t k, int64_t r0, int64_t r1, int64_t c0, int64_t c1);
+
+/* Round-to-nearest-even fp32 -> bf16 -> fp32. */
+float oracle_round_bf16(float x);
+
+/*
+ * megacu's phased fp32 graph on n_pes logical PEs (one call):
+ * per PE: GEMM tiles in tile-id order publish events[pe][tile] = tile + 1 on
+ * every PE; every PE then acquires all PEs' slot of each tile and sums the
+ * partials in PE order into its out. a[pe]: [m, k], b[pe]: [k, n],
+ * out[pe]: [m, n]; events[pe]: int32 [n_pes][tiles] (reset by the call).
+ * Returns 0, or a negative number if an acquire found a slot unset.
+ */
+int oracle_phased_f32(int64_t m, int64_t n, int64_t k, int32_t tile_m, int32_t tile_n,
+                      int32_t n_pes, const float *const *a, const float *const *b,
+                      float *const *out, int32_t *const *events);
+
+/* Tile schedule restatement: raster index r -> out[0] tile row, out[1] tile
+ * column, out[2] owner PE, out[3] index among the owner's tiles. */
+void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode,
+                   int32_t group_m, int32_t r, int32_t out[4]);
+
+typedef struct oracle_bf16_problem {
+  int64_t m, n, k;       /* k = per-PE slice */
+  int32_t tile_m;        /* 128 */
+  int32_t tile_n;        /* 64 / 128 / 256 */
+  int32_t n_pes;
+  int32_t mode;          /* 0 allreduce, 1 reduce-scatter */
+  int32_t one_shot;
+  int32_t group_m;       /* raster band height */
+  int32_t wire_bytes;    /* 2: partials rounded to bf16 before the sum; 4: fp32 */
+  int32_t threads;       /* CPU threads for the GEMMs */
+  uint32_t epoch;        /* the call's epoch tag (launch count + 1) */
+} oracle_bf16_problem;
+
+/*
+ * The B200 megakernel's tile-task graph for one call on n_pes logical PEs.
+ * a[pe], b[pe]: bf16 values held in fp32. out[pe]: fp32 result, [m, n] for
+ * allreduce, [m / n_pes, n] for reduce-scatter (not rounded to bf16).
+ * events[pe] (optional): the event tensor words after the control block,
+ * uint32 [2][n_pes + 1][tiles][4], updated in place exactly as the device
+ * does. counters[pe * 8 + i] (optional) receive the per-call deltas of the
+ * device counters. gemm_order (optional, [tiles]) receives the tile id of
+ * each GEMM ticket; reduce_order[pe] (optional, [tiles * 4]) the tile id of
+ * each reduce ticket of PE pe, or -1 where the ticket is skipped (a 32-row
+ * quarter that lies wholly below m). Returns 0, or a negative number if the
+ * graph was inconsistent (an acquire found a flag unset).
+ */
+int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
+                     const float *const *b, float *const *out, uint32_t *const *events,
+                     uint64_t *counters, int32_t *gemm_order, int32_t *const *reduce_order);
+
+/*
+ * CPU-baseline sample: the summed output of the listed tiles only (full K
+ * on every PE, PE-order fp32 sum), written into out_full[m, n] at the tiles'
+ * positions. Uses `threads` POSIX threads across the listed tiles.
+ */
+void oracle_bf16_tiles(const oracle_bf16_problem *p, const float *const *a,
+                       const float *const *b, const int32_t *tile_ids, int32_t n_tiles_listed,
+                       float *out_full);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEGACU_B200_ORACLE_H_ */

@@ -1,0 +1,73 @@
+"""Helpers shared by the GPU tests: seeded inputs, one-call runners, checks."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+import megacu_b200 as mb
+import oracle_lib
+
+# Tolerance of the bf16 path (north star: max relative error 1e-2, bf16 inputs,
+# fp32 accumulate), applied per element against the fp32 oracle with a floor
+# of 1% of the output's RMS so that near-zero outputs are judged on scale.
+REL_TOL = 1e-2
+
+
+def rel_error(got: np.ndarray, want: np.ndarray) -> float:
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    rms = float(np.sqrt(np.mean(want ** 2))) if want.size else 0.0
+    denom = np.abs(want) + 0.01 * rms + 1e-30
+    return float(np.max(np.abs(got - want) / denom)) if want.size else 0.0
+
+
+def seeded_bf16(seed: int, shape, std: float) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def inputs(seed: int, n_pes: int, m: int, n: int, k: int, std_a: float = 1.0,
+           std_b: float = 0.02):
+    """Per-PE bf16 A [m, k] and B [k, n] (host tensors) from per-(PE, tensor) seeds."""
+    a = [seeded_bf16(seed * 100 + 10 * pe + 0, (m, k), std_a) for pe in range(n_pes)]
+    b = [seeded_bf16(seed * 100 + 10 * pe + 1, (k, n), std_b) for pe in range(n_pes)]
+    return a, b
+
+
+def f32(t: torch.Tensor) -> np.ndarray:
+    return np.ascontiguousarray(t.float().cpu().numpy())
+
+
+class SinglePE:
+    """Device buffers for one-PE calls of the bf16 path on cuda:0."""
+
+    def __init__(self, problem: mb.Problem, device: int = 0):
+        self.problem = problem
+        self.device = device
+        self.plan = mb.plan(problem, 1)
+        ev_bytes = mb.events_bytes(problem, 1)
+        self.events = torch.zeros(ev_bytes // 4, dtype=torch.int32, device=f"cuda:{device}")
+        self.out = torch.empty(problem.m, problem.n, dtype=torch.bfloat16,
+                               device=f"cuda:{device}")
+
+    def run(self, a: torch.Tensor, b: torch.Tensor, trace=None, orchestrate=True):
+        stream = torch.cuda.current_stream(self.device)
+        mb.gemm_allreduce(a, b, self.out, workspace=None, events=self.events,
+                          problem=self.problem, stream=stream, device=self.device, trace=trace,
+                          orchestrate=orchestrate)
+        mb.events_status(self.events, stream)
+        return self.out
+
+    def event_words(self) -> np.ndarray:
+        return self.events[64:].cpu().numpy().view(np.uint32).copy()
+
+
+def trace_records(trace: torch.Tensor):
+    rec = trace.view(-1, 4).cpu().numpy().astype(np.uint64)
+    rec = rec[rec[:, 3] != 0]
+    kind = (rec[:, 0] & 0xFF).astype(np.int64)
+    sub = ((rec[:, 0] >> 8) & 0xFF).astype(np.int64)
+    cta = ((rec[:, 0] >> 16) & 0xFFFF).astype(np.int64)
+    ticket = (rec[:, 0] >> 32).astype(np.int64)
+    return dict(kind=kind, sub=sub, cta=cta, ticket=ticket, tile=rec[:, 1].astype(np.int64),
+                t0=rec[:, 2], t1=rec[:, 3])

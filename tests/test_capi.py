@@ -1,0 +1,117 @@
+"""The C ABI library: loads, exports what include/megacu_b200.h declares, and
+validates arguments the way megacu's launcher does (no GPU needed: a null
+stream means "validate only", megacu_gemm_allreduce_phased.cu:160-165)."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+
+import megacu_b200 as mb
+from megacu_b200 import _capi
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _capi.load()
+    names = _capi.declared_functions()
+    assert len(names) >= 24
+    for name in names:
+        assert hasattr(lib, name), name
+    assert lib.megacu_b200_version().startswith(b"megacu_b200")
+
+
+def test_component_link_anchors():
+    """tests/build/runtime_components_contracts.cc:60-64."""
+    lib = _capi.load()
+    for name in ("megacu_dispatcher_explicit_attrs_component",
+                 "megacu_scheduler_explicit_asap_component", "megacu_platform_cuda_component",
+                 "megacu_backend_nvshmem_component", "megacu_target_runtime_component"):
+        assert getattr(lib, name)() == 1
+
+
+def _status(fn, *args):
+    s = fn(*args)
+    return s.code, s.detail
+
+
+FAKE = 0x100000  # never dereferenced: validation-only calls
+
+
+def test_f32_validation_only():
+    """direct_orchestrate_smoke.cc: null stream + team of 2 -> ok, no launch."""
+    d = mb.driver_view(None, 0)
+    d.team.team_n_pes, d.team.world_n_pes = 2, 2
+    p = _capi.GemmArProblem(m=1, n=1, k=1, tile_m=1, tile_n=1)
+    lib = _capi.load()
+    assert _status(lib.megacu_cuda_gemm_allreduce_f32_orchestrate, d, FAKE, FAKE, FAKE, FAKE,
+                   FAKE, p) == (0, 0)
+    assert _status(lib.megacu_cuda_gemm_allreduce_phased_f32, d, FAKE, FAKE, FAKE, FAKE, FAKE,
+                   p) == (0, 0)
+    bad = _capi.GemmArProblem(m=0, n=1, k=1, tile_m=1, tile_n=1)
+    assert _status(lib.megacu_cuda_gemm_allreduce_phased_f32, d, FAKE, FAKE, FAKE, FAKE, FAKE,
+                   bad) == (1, 1)
+    assert _status(lib.megacu_cuda_gemm_allreduce_phased_f32, d, None, FAKE, FAKE, FAKE, FAKE,
+                   p) == (1, 2)
+
+
+def test_bf16_validation_only():
+    lib = _capi.load()
+    d = mb.driver_view(None, 0)
+    good = mb.Problem(256, 512, 128).to_c()
+    for fn in (lib.megacu_cuda_gemm_allreduce_bf16, lib.megacu_cuda_gemm_allreduce_bf16_orchestrate,
+               lib.megacu_cuda_gemm_reduce_scatter_bf16):
+        assert _status(fn, d, FAKE, FAKE, FAKE, FAKE, FAKE, good) == (0, 0)
+    cases = [
+        (mb.Problem(0, 512, 128), (1, 1)),
+        (mb.Problem(256, 510, 128), (1, 21)),
+        (mb.Problem(256, 512, 100), (1, 21)),
+        (mb.Problem(256, 512, 128, tile_n=96), (2, 22)),
+        (mb.Problem(256, 512, 128, mode=7), (1, 1)),
+    ]
+    for prob, want in cases:
+        assert _status(lib.megacu_cuda_gemm_allreduce_bf16_orchestrate, d, FAKE, FAKE, FAKE, FAKE,
+                       FAKE, prob.to_c()) == want
+    p = mb.Problem(256, 512, 128).to_c()
+    p.dtype = 3
+    assert _status(lib.megacu_cuda_gemm_allreduce_bf16, d, FAKE, FAKE, FAKE, FAKE, FAKE, p) == (2, 20)
+    # missing storage / misaligned
+    assert _status(lib.megacu_cuda_gemm_allreduce_bf16, d, None, FAKE, FAKE, FAKE, FAKE,
+                   good) == (1, 2)
+    assert _status(lib.megacu_cuda_gemm_allreduce_bf16, d, FAKE + 2, FAKE, FAKE, FAKE, FAKE,
+                   good) == (1, 21)
+    # remote PEs without a team backend (megacu's detail 13)
+    d2 = mb.driver_view(None, 0)
+    d2.team.team_n_pes = 2
+    assert _status(lib.megacu_cuda_gemm_allreduce_bf16, d2, FAKE, FAKE, FAKE, FAKE, FAKE,
+                   good) == (2, 13)
+    # reduce-scatter needs m divisible by tp * 128
+    rs = mb.Problem(300, 512, 128).to_c()
+    assert _status(lib.megacu_cuda_gemm_reduce_scatter_bf16, d, FAKE, FAKE, FAKE, FAKE, FAKE,
+                   rs) == (2, 26)
+
+
+@pytest.mark.parametrize("m,n,k,n_pes,mode", [(4096, 8192, 8192, 1, 0), (4096, 8192, 1024, 8, 0),
+                                              (8192, 8192, 3584, 8, 1), (16, 8192, 3584, 8, 0),
+                                              (2048, 4096, 1024, 2, 0)])
+def test_plan_sizes(m, n, k, n_pes, mode):
+    prob = mb.Problem(m, n, k, mode=mode)
+    pl = mb.plan(prob, n_pes)
+    assert pl.tile_m == 128 and pl.tile_n in (64, 128, 256)
+    assert pl.m_tiles == -(-m // 128) and pl.n_tiles == -(-n // pl.tile_n)
+    ws = mb.workspace_bytes(prob, n_pes)
+    ev = mb.events_bytes(prob, n_pes)
+    assert ev == 256 + 2 * (n_pes + 1) * pl.tiles * 4 * 4
+    if n_pes == 1:
+        assert ws == 0
+    else:
+        assert ws == 2 * n_pes * pl.slots_per_src * 128 * pl.tile_n * pl.wire_bytes
+        if mode == 0 and m <= 128:
+            assert pl.one_shot
+    if mode == 1 or (n_pes > 1 and not pl.one_shot):
+        assert pl.slots_per_src == -(-pl.tiles // n_pes)
+
+
+def test_status_layout_matches_cpp():
+    assert ctypes.sizeof(_capi.Status) == 16
+    assert ctypes.sizeof(_capi.DriverView) == 64
+    assert ctypes.sizeof(_capi.GemmArProblem) == 32

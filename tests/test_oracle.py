@@ -1,0 +1,160 @@
+"""The CPU oracle against the reference's golden vectors and its own invariants.
+
+Pins: the reference's known-answer tests (tests/golden/kat_gemm_allreduce.json,
+transcribed from its test sources by tests/golden/make_golden.py) and BASELINE
+config 1 (512^3 fp32, 128x128 tiles = 16 tile tasks, 2 logical ranks).
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle_lib
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "kat_gemm_allreduce.json")
+
+
+@pytest.fixture(scope="module")
+def kat():
+    with open(GOLDEN) as f:
+        return json.load(f)
+
+
+def test_kat_single_pe(kat):
+    """cuda_gemm_allreduce_correctness.cc: 2x4 @ 4x3, tile 1x2, tol 1e-4."""
+    k = kat["single_pe"]
+    a = np.array(k["a"], np.float32).reshape(k["m"], k["k"])
+    b = np.array(k["b"], np.float32).reshape(k["k"], k["n"])
+    outs, events = oracle_lib.phased_f32([a], [b], k["m"], k["n"], k["k"], k["tile_m"],
+                                         k["tile_n"])
+    want = np.array(k["expected"], np.float32).reshape(k["m"], k["n"])
+    assert np.max(np.abs(outs[0] - want)) < k["tolerance"]
+    tiles = events[0].shape[1]
+    assert events[0].tolist() == [[t + 1 for t in range(tiles)]]
+
+
+def test_kat_two_pe(kat):
+    """nvshmem_two_rank_smoke.cc: A = pe + 1, B = 1, K = 4 -> 12 everywhere."""
+    k = kat["two_pe"]
+    a = [np.full((k["m"], k["k"]), v, np.float32) for v in k["a_value_per_pe"]]
+    b = [np.full((k["k"], k["n"]), k["b_value"], np.float32) for _ in a]
+    outs, events = oracle_lib.phased_f32(a, b, k["m"], k["n"], k["k"], k["tile_m"], k["tile_n"])
+    for pe, out in enumerate(outs):
+        assert np.all(np.abs(out - k["expected_value"]) < k["tolerance"]), pe
+        assert np.all(events[pe] == 1)  # one tile, ready value tile + 1
+
+
+def test_config1_host_plumbing():
+    """512^3 fp32, N(0,1) seed 0, 16 tile tasks, 2 ranks x K/2."""
+    rng = np.random.default_rng(0)
+    m = n = k = 512
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((k, n), dtype=np.float32)
+    halves_a = [np.ascontiguousarray(a[:, :256]), np.ascontiguousarray(a[:, 256:])]
+    halves_b = [np.ascontiguousarray(b[:256]), np.ascontiguousarray(b[256:])]
+    outs, events = oracle_lib.phased_f32(halves_a, halves_b, m, n, k // 2, 128, 128)
+    want = a.astype(np.float64) @ b.astype(np.float64)
+    for out in outs:
+        rel = np.max(np.abs(out - want)) / np.max(np.abs(want))
+        assert rel < 1e-5
+    assert outs[0].tobytes() == outs[1].tobytes()  # same PE-order sum on every rank
+    for ev in events:
+        assert ev.shape == (2, 16)
+        assert np.all(ev == np.arange(1, 17)[None, :])
+
+
+def test_gemm_matches_float64():
+    rng = np.random.default_rng(7)
+    a = rng.standard_normal((67, 45), dtype=np.float32)
+    b = rng.standard_normal((45, 33), dtype=np.float32)
+    c = oracle_lib.gemm_f32(a, b, threads=3)
+    assert np.allclose(c, a.astype(np.float64) @ b, rtol=1e-5, atol=1e-4)
+    # thread count does not change a single bit (k order is per element)
+    assert oracle_lib.gemm_f32(a, b, threads=1).tobytes() == c.tobytes()
+
+
+def test_round_bf16_matches_c():
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.standard_normal(4096).astype(np.float32) * 10,
+                        np.array([0.0, -0.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -9, np.inf, -np.inf],
+                                 np.float32)])
+    lib = oracle_lib.load()
+    want = np.array([lib.oracle_round_bf16(float(v)) for v in x], np.float32)
+    got = oracle_lib.round_bf16(x)
+    assert got.tobytes() == want.tobytes()
+    assert oracle_lib.round_bf16(np.array([1.0 + 2 ** -8], np.float32))[0] == 1.0  # tie to even
+
+
+def _bf16_inputs(rng, n_pes, m, n, k):
+    a = [oracle_lib.round_bf16(rng.normal(0, 1, (m, k)).astype(np.float32)) for _ in range(n_pes)]
+    b = [oracle_lib.round_bf16(rng.normal(0, 0.5, (k, n)).astype(np.float32)) for _ in range(n_pes)]
+    return a, b
+
+
+@pytest.mark.parametrize("n_pes,mode,one_shot,m,n,tile_n", [
+    (1, 0, False, 200, 136, 64),
+    (2, 0, False, 300, 520, 128),
+    (2, 0, True, 96, 256, 64),
+    (4, 0, False, 512, 384, 128),
+    (4, 1, False, 1024, 200, 64),
+    (3, 0, True, 130, 64, 64),
+])
+def test_bf16_graph_counts_and_events(n_pes, mode, one_shot, m, n, tile_n):
+    """The task graph's output, completion counts and event tensor are consistent."""
+    rng = np.random.default_rng(11)
+    k = 40
+    a, b = _bf16_inputs(rng, n_pes, m, n, k)
+    m_tiles, n_tiles = -(-m // 128), -(-n // tile_n)
+    tiles = m_tiles * n_tiles
+    events = [np.zeros(oracle_lib.event_tensor_words(n_pes, tiles), np.uint32)
+              for _ in range(n_pes)]
+    r = oracle_lib.bf16_call(a, b, m=m, n=n, k=k, tile_n=tile_n, mode=mode, one_shot=one_shot,
+                             wire_bytes=4, epoch=5, events=events)
+    full = sum(x.astype(np.float64) @ y for x, y in zip(a, b))
+    for pe in range(n_pes):
+        want = full[pe * (m // n_pes):(pe + 1) * (m // n_pes)] if mode == 1 else full
+        assert np.allclose(r["out"][pe], want, rtol=1e-4, atol=1e-3)
+    # every raster index maps to a distinct tile
+    assert sorted(r["gemm_order"].tolist()) == list(range(tiles))
+    active = sum(1 for t in range(tiles) for q in range(4) if (t // n_tiles) * 128 + q * 32 < m)
+    c = r["counters"]
+    assert np.all(c[:, 0] == tiles) and np.all(c[:, 6] == 1) and np.all(c[:, 7] == 0)
+    reduced = [sum(1 for t in ro if t >= 0) for ro in r["reduce_order"]]
+    if n_pes == 1:
+        assert c[0, 2] == active and c[0, 1] == 0
+    elif one_shot:
+        assert all(x == active for x in reduced)
+        assert np.all(c[:, 2] == active * n_pes)
+    else:
+        assert sum(reduced) == active  # every active quarter reduced exactly once
+        assert np.all(c[:, 2] == active)
+    assert c[:, 1].tolist() == reduced
+    assert np.all(c[:, 3] == np.array(reduced) * n_pes)
+    two_shot_ar = n_pes > 1 and mode == 0 and not one_shot
+    assert np.all(c[:, 5] == (active if two_shot_ar else 0))
+    # the event tensor holds the epoch exactly where the graph published
+    for pe in range(n_pes):
+        ev = r["events"][pe].reshape(2, n_pes + 1, tiles, 4)
+        assert np.all(ev[0] == 0)  # epoch 5 -> parity plane 1 only
+        assert set(np.unique(ev[1]).tolist()) <= {0, 5}
+
+
+def test_locate_matches_product_schedule():
+    """oracle_locate restates the device queue's raster order exactly."""
+    import megacu_b200 as mb
+    cases = [(4096, 8192, 1, 0), (4096, 8192, 8, 0), (8192, 8192, 8, 1), (16, 8192, 8, 0),
+             (1000, 2000, 3, 0), (2048, 512, 4, 1), (130, 72, 2, 0)]
+    for m, n, n_pes, mode in cases:
+        prob = mb.Problem(m, n, 64, mode=mode)
+        pl = mb.plan(prob, n_pes)
+        seen = set()
+        for r in range(pl.tiles):
+            got = mb.plan_tile(prob, n_pes, r)
+            assert got == oracle_lib.locate(pl.m_tiles, pl.n_tiles, n_pes, mode, pl.group_m, r)
+            seen.add(got[0] * pl.n_tiles + got[1])
+            if mode == 1:  # reduce-scatter: the owner holds the tile's rows
+                assert got[0] // (pl.m_tiles // n_pes) == got[2]
+        assert len(seen) == pl.tiles
