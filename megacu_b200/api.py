@@ -52,12 +52,17 @@ def _ptr(x) -> Optional[int]:
     return x.data_ptr()
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy: the legacy default stream, named explicitly
+
+
 def _stream_handle(stream) -> Optional[int]:
+    """Raw cudaStream_t of ``stream``. None stays None (megacu: validate only);
+    torch's default stream (handle 0) is passed as cudaStreamLegacy so that it
+    is not mistaken for "no stream"."""
     if stream is None:
         return None
-    if isinstance(stream, int):
-        return stream
-    return stream.cuda_stream
+    handle = stream if isinstance(stream, int) else stream.cuda_stream
+    return handle if handle != 0 else CUDA_STREAM_LEGACY
 
 
 # ---- team ----------------------------------------------------------------------

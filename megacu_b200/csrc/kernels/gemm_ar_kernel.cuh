@@ -278,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        kLocalTimeoutNs);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------- tcgen05.mma issuer ----------------
     if (lane == 0) {
@@ -337,25 +338,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::umma_commit(mma_done);
       ptx::mbar_wait(mma_done, 0, nullptr, kLocalTimeoutNs);
     }
+    __syncwarp();
   } else if (warp < kReduceWarp0) {
     // ---------------- epilogue: TMEM -> destination, publish ----------------
     std::int32_t const quarter = warp % 4;  // TMEM lanes [32q, 32q+32)
     std::int32_t const row_in_tile = quarter * 32 + static_cast<std::int32_t>(lane);
     for (std::uint32_t n = 0;; ++n) {
       std::uint32_t const slot = n % kTaskRing;
-      if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word,
-                          kLocalTimeoutNs)) {
+      // Warp-uniform decision: every lane waits, the warp acts on the vote.
+      if (!__all_sync(0xffffffffu, ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u,
+                                                  abort_word, kLocalTimeoutNs))) {
         if (lane == 0) detail::record_error(p, err_local_timeout, 0, 0, 6);
         break;
       }
-      std::int32_t const r = ring[slot];
-      __syncwarp();
+      std::int32_t const r = __shfl_sync(0xffffffffu, ring[slot], 0);
       if (lane == 0) ptx::mbar_arrive(&task_empty[slot]);
       if (r < 0) {
         break;
       }
       std::uint32_t const buf = n & 1u;
-      if (!ptx::mbar_wait(&acc_full[buf], (n >> 1) & 1u, abort_word, kLocalTimeoutNs)) {
+      if (!__all_sync(0xffffffffu,
+                      ptx::mbar_wait(&acc_full[buf], (n >> 1) & 1u, abort_word, kLocalTimeoutNs))) {
         if (lane == 0) detail::record_error(p, err_local_timeout, r, 0, 7);
         break;
       }
@@ -626,6 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- teardown ----------------
+  __syncwarp();
   ptx::tc_fence_before_sync();
   __syncthreads();
   ptx::tc_fence_after_sync();
