@@ -181,6 +181,25 @@ megacu_status megacu_cuda_gemm_allreduce_f32_orchestrate(
     megacu_driver_view driver, const float *a, const float *b, float *partial,
     float *out, void *events, megacu_gemm_ar_problem problem);
 
+/*
+ * Allocation-free single-PE form of megacu_cuda_gemm_allreduce_bf16 (no
+ * counterpart in megacu). For callers that cannot allocate device memory for
+ * the kernel's scratch: plugin hosts that pass an operator only its inputs
+ * and outputs, processes whose device memory belongs to another allocator,
+ * and latency-critical loops that must not call cudaMalloc. The caller still
+ * passes a, b and out; the scratch (task-queue control block and event
+ * tensor) lives in a 256 KiB array built into the library, one per GPU, held
+ * until the process exits. Limits: team_n_pes must be 1 (unsupported/51);
+ * at most 4092 output tiles (invalid_argument/52). Every call on a GPU shares
+ * that array, so calls that overlap on the GPU race — issue them in stream
+ * order. The first call on a device looks up the array's address with that
+ * device current; make it before any stream capture.
+ */
+megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver,
+                                            const void *a, const void *b,
+                                            void *out,
+                                            megacu_gemm_ar_problem_v2 problem);
+
 /* Bytes of workspace / events a bf16 call needs for `problem` on n_pes PEs. */
 megacu_status megacu_b200_workspace_bytes(megacu_gemm_ar_problem_v2 problem,
                                           int32_t n_pes, int64_t *bytes);

@@ -39,7 +39,7 @@ def _nvcc() -> str:
 
 
 def _sources() -> list[str]:
-    src = [os.path.join(PKG, "csrc", "capi.cu")]
+    src = sorted(glob.glob(os.path.join(PKG, "csrc", "*.cu")))
     src += sorted(glob.glob(os.path.join(PKG, "csrc", "runtime", "*.cc")))
     return src
 

@@ -1,0 +1,197 @@
+// Allocation-free entry point of the single-PE bf16 megakernel.
+//
+// Some callers cannot allocate device memory for us: a plugin host that
+// hands an operator only its input and output buffers (the host owns every
+// byte of device memory and exposes no workspace), a process whose device
+// memory is entirely managed by another allocator, or a latency-critical
+// serving loop where a cudaMalloc call (which may synchronise the device) is
+// not acceptable. For them, `megacu_cuda_gemm_bf16_noalloc` runs the same
+// kernel as `megacu_cuda_gemm_allreduce_bf16` on one PE, with the kernel's
+// scratch (the control block with the device task-queue tickets, and the
+// event tensor) in a fixed array compiled into this library.
+//
+// Limits and sharing rules:
+//  * scratch is `kNoAllocScratchBytes` (256 KiB) per GPU, held by every GPU
+//    that loads the library until the process exits; problems whose tile
+//    grid needs more (more than 4092 output tiles) are rejected;
+//  * every call on a GPU shares that one array: calls that overlap on the
+//    GPU (on different streams, or from different threads) race and must
+//    not be issued; calls in stream order are fine;
+//  * the first call on a device looks up the array's device address (with
+//    that device current); make that first call before any stream capture.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include <megacu_b200.h>
+
+#include "kernels/gemm_ar_kernel.cuh"
+
+namespace {
+
+using namespace megacu_b200;
+
+constexpr std::int64_t kNoAllocScratchBytes = 256 * 1024;
+constexpr int kNoAllocMaxDevices = 64;
+
+// The scratch itself. In host code this name is only a handle for the
+// runtime: its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_addr[kNoAllocMaxDevices] = {};
+bool g_noalloc_configured[kNoAllocMaxDevices][3] = {};
+
+megacu_status na_ok() { return {MEGACU_OK, 0, nullptr}; }
+
+megacu_status na_fail(megacu_status_code code, std::uint16_t detail, char const *msg) {
+  return {static_cast<std::uint8_t>(code), detail, msg};
+}
+
+megacu_status na_cuda(cudaError_t e, std::uint16_t detail) {
+  return {MEGACU_LAUNCH_ERROR, detail, cudaGetErrorString(e)};
+}
+
+// Device address of this GPU's scratch; looked up once per device with that
+// device current.
+megacu_status scratch_address(int device, void **out) {
+  if (device < 0 || device >= kNoAllocMaxDevices) {
+    return na_fail(MEGACU_INVALID_ARGUMENT, 10, "device ordinal out of range");
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[device] == nullptr) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return na_cuda(e, 50);
+    g_noalloc_addr[device] = ptr;
+  }
+  *out = g_noalloc_addr[device];
+  return na_ok();
+}
+
+bool na_encode(CUtensorMap *map, void const *base, std::int64_t rows, std::int64_t cols,
+               std::uint32_t box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+cudaError_t na_launch(int device, int slot, int grid, cudaStream_t stream, CUtensorMap const &ma,
+                      CUtensorMap const &mb, gemm_ar_params const &prm) {
+  auto kernel = &gemm_ar_megakernel<BN, false>;
+  if (!g_noalloc_configured[device][slot]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm_config<BN>::smem_bytes);
+    if (e != cudaSuccess) return e;
+    g_noalloc_configured[device][slot] = true;
+  }
+  kernel<<<grid, kThreads, gemm_config<BN>::smem_bytes, stream>>>(ma, mb, prm);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver, void const *a,
+                                                       void const *b, void *out,
+                                                       megacu_gemm_ar_problem_v2 problem) {
+  if (driver.team.team_n_pes != 1) {
+    return na_fail(MEGACU_UNSUPPORTED, 51,
+                   "the allocation-free entry runs on one PE only (team_n_pes must be 1)");
+  }
+  problem.mode = MEGACU_MODE_ALLREDUCE;
+  std::int32_t info[8];
+  megacu_status st = megacu_b200_plan_info(problem, 1, info);
+  if (st.code != MEGACU_OK) return st;
+  if (a == nullptr || b == nullptr || out == nullptr) {
+    return na_fail(MEGACU_INVALID_ARGUMENT, 2, "missing storage");
+  }
+  auto aligned = [](void const *p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; };
+  if (!aligned(a) || !aligned(b) || !aligned(out)) {
+    return na_fail(MEGACU_INVALID_ARGUMENT, 21, "buffers must be 16-byte aligned");
+  }
+  std::int32_t const tile_n = info[1], m_tiles = info[2], n_tiles = info[3];
+  std::int64_t const tiles = static_cast<std::int64_t>(m_tiles) * n_tiles;
+  if (events_bytes_for(1, static_cast<std::int32_t>(tiles)) > kNoAllocScratchBytes) {
+    return na_fail(MEGACU_INVALID_ARGUMENT, 52,
+                   "problem too large for the allocation-free entry: its tile grid needs more "
+                   "than the 256 KiB of built-in scratch (at most 4092 output tiles)");
+  }
+  if (driver.launch.stream == nullptr) {
+    return na_ok();
+  }
+  int const device = driver.launch.device_ordinal;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return na_cuda(e, 10);
+  void *scratch = nullptr;
+  st = scratch_address(device, &scratch);
+  if (st.code != MEGACU_OK) return st;
+
+  CUtensorMap map_a, map_b;
+  if (!na_encode(&map_a, a, problem.m, problem.k, kBlockM) ||
+      !na_encode(&map_b, b, problem.k, problem.n, kBlockK)) {
+    return na_fail(MEGACU_BACKEND_ERROR, 30, "cuTensorMapEncodeTiled failed");
+  }
+  auto stream = static_cast<cudaStream_t>(driver.launch.stream);
+  // The device task-queue words must start at zero: clear them (the array
+  // keeps whatever the previous call left).
+  e = cudaMemsetAsync(scratch, 0, 3 * sizeof(std::uint32_t), stream);
+  if (e != cudaSuccess) return na_cuda(e, 11);
+
+  gemm_ar_params prm{};
+  prm.m = static_cast<std::int32_t>(problem.m);
+  prm.n = static_cast<std::int32_t>(problem.n);
+  prm.k = static_cast<std::int32_t>(problem.k);
+  prm.m_tiles = m_tiles;
+  prm.n_tiles = n_tiles;
+  prm.tiles = static_cast<std::int32_t>(tiles);
+  prm.n_pes = 1;
+  prm.my_pe = 0;
+  prm.mode = mode_allreduce;
+  prm.group_m = info[6];
+  prm.rows_per_pe = prm.m;
+  prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
+  prm.out = static_cast<__nv_bfloat16 *>(out);
+  prm.events = static_cast<std::uint32_t *>(scratch);
+  prm.peers.n_pes = 1;
+  prm.trace = reinterpret_cast<unsigned long long *>(problem.trace);
+  prm.trace_capacity = problem.trace != nullptr ? problem.trace_capacity : 0;
+
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return na_cuda(e, 10);
+  int const grid = problem.num_ctas > 0 ? problem.num_ctas : sms;
+  switch (tile_n) {
+    case 256:
+      e = na_launch<256>(device, 2, grid, stream, map_a, map_b, prm);
+      break;
+    case 128:
+      e = na_launch<128>(device, 1, grid, stream, map_a, map_b, prm);
+      break;
+    default:
+      e = na_launch<64>(device, 0, grid, stream, map_a, map_b, prm);
+      break;
+  }
+  if (e != cudaSuccess) return na_cuda(e, 14);
+  return na_ok();
+}
