@@ -309,7 +309,7 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, prm.mode, pl.group_m};
   std::int32_t const reduce_tiles =
       n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
-  prm.n_reduce = reduce_tiles * kQuarters;
+  prm.n_reduce = reduce_tiles * kQuarters * (pl.tile_n / 64);
   prm.slots_per_src = pl.slots_per_src;
   prm.rows_per_pe = static_cast<std::int32_t>(problem.m / n_pes);
   prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;

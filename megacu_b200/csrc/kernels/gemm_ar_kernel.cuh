@@ -47,6 +47,9 @@ inline constexpr int kTaskRing = 4;
 inline constexpr int kEpilogueWarp0 = 2;
 inline constexpr int kReduceWarp0 = 6;
 inline constexpr int kReduceWarps = 4;
+// Warps that may run reduce sub-tasks: the reduce warps from the start, the
+// epilogue warps once the GEMM queue is drained.
+inline constexpr int kWorkerWarps = 8;
 inline constexpr std::uint64_t kLocalTimeoutNs = 4000000000ull;
 
 template <int BN>
@@ -57,7 +60,8 @@ struct gemm_config {
   static constexpr int b_bytes = kBlockK * BN * 2;
   static constexpr int stage_bytes = a_bytes + b_bytes;
   static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8
-  static constexpr int reduce_bytes = kReduceWarps * 32 * 128; // transpose tiles
+  static constexpr int col_blocks = BN / 64;                   // reduce sub-tasks per quarter
+  static constexpr int reduce_bytes = kWorkerWarps * 32 * 128; // transpose tiles
   static constexpr int n_barriers = 2 * stages + 4 + 2 * kTaskRing + 1;
   static constexpr int aux_bytes = n_barriers * 8 + kTaskRing * 4 + 16;
   static constexpr int smem_bytes = 1024 + stages * stage_bytes + reduce_bytes + aux_bytes;
@@ -160,6 +164,220 @@ __device__ __forceinline__ std::int64_t slot_offset(gemm_ar_params const &p, std
                                                     std::int64_t slot_bytes) {
   return ((static_cast<std::int64_t>(parity) * p.n_pes + src) * p.slots_per_src + j) *
          slot_bytes;
+}
+
+// Does the 32-row quarter q x 64-column block c of tile (row, col) hold any
+// output element?
+template <int BN>
+__device__ __forceinline__ bool block_exists(gemm_ar_params const &p, std::int32_t tile_row,
+                                             std::int32_t tile_col, std::int32_t quarter,
+                                             std::int32_t block) {
+  return tile_row * kBlockM + quarter * 32 < p.m && tile_col * BN + block * 64 < p.n;
+}
+
+// Reduce worker (task 2): one warp pulls sub-tasks = (owned tile, 32-row
+// quarter, 64-column block) from the reduce queue until it is empty. For each:
+// acquire every PE's arrive flag of the quarter, sum the PE partials in PE
+// order 0..n_pes-1 in fp32 (two PEs' loads in flight at a time), round to
+// bf16, transpose 32 x 64 through `xpose` (4 KiB of shared memory) and store
+// row-major into this PE's out, or — two-shot allreduce — into every PE's out
+// followed by the final flags.
+template <int BN, bool kWireF32>
+__device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_schedule const &sched,
+                                             std::uint32_t parity, std::uint32_t epoch,
+                                             std::uint32_t *my_events,
+                                             std::uint32_t const *abort_word, std::uint8_t *xpose,
+                                             std::uint32_t lane) {
+  constexpr int kWireBytes = kWireF32 ? 4 : 2;
+  constexpr int kBlocks = BN / 64;
+  constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
+  control_block *ctrl = control(p);
+  bool const push_all = p.mode == mode_allreduce && !p.one_shot;
+  std::int64_t const src_stride = static_cast<std::int64_t>(p.slots_per_src) * kSlotBytes;
+  for (;;) {
+    std::uint32_t ticket = 0;
+    if (lane == 0) ticket = atomicAdd(&ctrl->reduce_ticket, 1u);
+    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    if (ticket >= static_cast<std::uint32_t>(p.n_reduce)) {
+      break;
+    }
+    std::int32_t const j = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
+    std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks);
+    std::int32_t const quarter = rem / kBlocks;
+    std::int32_t const cb = rem % kBlocks;
+    std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
+    tile_coord const c = locate(sched, r);
+    std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+    if (!block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
+      continue;  // no output element lives in this block
+    }
+
+    // Task 2 "before": every PE's partial of this quarter has arrived.
+    bool ok = true;
+    if (static_cast<std::int32_t>(lane) < p.n_pes) {
+      ok = wait_flag(my_events + arrive_index(parity, lane, tile, quarter, p.n_pes, p.tiles),
+                     epoch, abort_word, p.timeout_ns);
+      if (!ok) record_error(p, err_remote_timeout, tile, lane, 8);
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      break;
+    }
+    std::uint64_t const t0 = ptx::now_ns();
+
+    float acc[8][8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+    }
+    // Lane = row; vector (v, row) of a slot sits at (v * 128 + row) * 16.
+    char const *base = p.workspace + slot_offset(p, parity, 0, j, kSlotBytes) +
+                       (static_cast<std::int64_t>(quarter) * 32 + lane) * 16;
+    if constexpr (kWireF32) {
+#pragma unroll 1
+      for (std::int32_t src = 0; src < p.n_pes; ++src) {
+        uint4 w[16];
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          w[h] = ptx::ld_cg_v4(base + src * src_stride + (cb * 16 + h) * (kBlockM * 16));
+        }
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          acc[h / 2][(h % 2) * 4 + 0] += __uint_as_float(w[h].x);
+          acc[h / 2][(h % 2) * 4 + 1] += __uint_as_float(w[h].y);
+          acc[h / 2][(h % 2) * 4 + 2] += __uint_as_float(w[h].z);
+          acc[h / 2][(h % 2) * 4 + 3] += __uint_as_float(w[h].w);
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (std::int32_t src = 0; src < p.n_pes; src += 2) {
+        bool const pair = src + 1 < p.n_pes;
+        uint4 w0[8], w1[8];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          w0[g] = ptx::ld_cg_v4(base + src * src_stride + (cb * 8 + g) * (kBlockM * 16));
+        }
+        if (pair) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            w1[g] = ptx::ld_cg_v4(base + (src + 1) * src_stride + (cb * 8 + g) * (kBlockM * 16));
+          }
+        }
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          acc[g][0] += ptx::bf16_lo(w0[g].x);
+          acc[g][1] += ptx::bf16_hi(w0[g].x);
+          acc[g][2] += ptx::bf16_lo(w0[g].y);
+          acc[g][3] += ptx::bf16_hi(w0[g].y);
+          acc[g][4] += ptx::bf16_lo(w0[g].z);
+          acc[g][5] += ptx::bf16_hi(w0[g].z);
+          acc[g][6] += ptx::bf16_lo(w0[g].w);
+          acc[g][7] += ptx::bf16_hi(w0[g].w);
+        }
+        if (pair) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            acc[g][0] += ptx::bf16_lo(w1[g].x);
+            acc[g][1] += ptx::bf16_hi(w1[g].x);
+            acc[g][2] += ptx::bf16_lo(w1[g].y);
+            acc[g][3] += ptx::bf16_hi(w1[g].y);
+            acc[g][4] += ptx::bf16_lo(w1[g].z);
+            acc[g][5] += ptx::bf16_hi(w1[g].z);
+            acc[g][6] += ptx::bf16_lo(w1[g].w);
+            acc[g][7] += ptx::bf16_hi(w1[g].w);
+          }
+        }
+      }
+    }
+    // Row `lane` of the 32 x 64 block -> shared, 16 B per 8 columns,
+    // XOR-swizzled so that both the write and the read are conflict-free.
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint4 q;
+      q.x = ptx::pack_bf16x2(acc[g][0], acc[g][1]);
+      q.y = ptx::pack_bf16x2(acc[g][2], acc[g][3]);
+      q.z = ptx::pack_bf16x2(acc[g][4], acc[g][5]);
+      q.w = ptx::pack_bf16x2(acc[g][6], acc[g][7]);
+      *reinterpret_cast<uint4 *>(xpose + lane * 128 + ((g ^ (lane & 7)) * 16)) = q;
+    }
+    __syncwarp();
+    // Read back row-major: 8 lanes cover one 128 B row segment.
+    std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
+    std::int32_t const out_row0 =
+        p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
+    std::int32_t const g = lane % 8;
+    std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
+      uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
+      if (row0 + rr < p.m && col < p.n) {
+        std::int64_t const off = static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
+        if (push_all) {
+          for (std::int32_t pe = 0; pe < p.n_pes; ++pe) {
+            ptx::st_v4(p.peers.translate(p.out, pe) + off, q);
+          }
+        } else {
+          ptx::st_v4(p.out + off, q);
+        }
+      }
+    }
+    __syncwarp();
+
+    if (push_all) {
+      // All-gather publish: this block of the summed tile is in every PE's out.
+      ptx::fence_acq_rel_sys();
+      __syncwarp();
+      if (static_cast<std::int32_t>(lane) < p.n_pes) {
+        std::uint32_t *flags = p.peers.translate(my_events, lane);
+        ptx::st_release_sys(flags + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles),
+                            epoch);
+      }
+    }
+    if (lane == 0) {
+      count(p, ctr_reduce_tasks, 1);
+      count(p, ctr_partial_acquire, p.n_pes);
+      if (push_all) count(p, ctr_final_publish, p.n_pes);
+      trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
+    }
+  }
+}
+
+// Two-shot allreduce: this PE's output is complete once every final flag of
+// every existing (tile, quarter, column block) is set. Worker `worker` of
+// `workers` polls its share, 32 flags per warp step.
+template <int BN>
+__device__ __forceinline__ void wait_final(gemm_ar_params const &p, std::uint32_t parity,
+                                           std::uint32_t epoch, std::uint32_t *my_events,
+                                           std::uint32_t const *abort_word, std::int32_t worker,
+                                           std::int32_t workers, std::uint32_t lane) {
+  constexpr int kBlocks = BN / 64;
+  std::int32_t const total = p.tiles * kQuarters * kBlocks;
+  std::uint32_t seen = 0;
+  for (std::int32_t first = worker * 32; first < total; first += workers * 32) {
+    std::int32_t const idx = first + static_cast<std::int32_t>(lane);
+    bool ok = true;
+    if (idx < total) {
+      std::int32_t const tile = idx / (kQuarters * kBlocks);
+      std::int32_t const quarter = (idx / kBlocks) % kQuarters;
+      std::int32_t const cb = idx % kBlocks;
+      if (block_exists<BN>(p, tile / p.n_tiles, tile % p.n_tiles, quarter, cb)) {
+        ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
+                       abort_word, p.timeout_ns);
+        if (!ok) {
+          record_error(p, err_remote_timeout, tile, 0xffffffffu, 9);
+        } else {
+          ++seen;
+        }
+      }
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      break;
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) seen += __shfl_xor_sync(0xffffffffu, seen, off);
+  if (lane == 0 && seen != 0) count(p, ctr_final_acquire, seen);
 }
 
 }  // namespace detail
@@ -445,189 +663,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (p.n_pes == 1) {
+        // One PE: the tile is final as written; mark its quarter arrived and
+        // its existing 64-column blocks final.
         if (lane == 0) {
-          ptx::st_release_sys(my_events + event_index(parity, 0, tile, quarter, 1, p.tiles), epoch);
-          ptx::st_release_sys(my_events + event_index(parity, 1, tile, quarter, 1, p.tiles), epoch);
+          ptx::st_release_sys(my_events + arrive_index(parity, 0, tile, quarter, 1, p.tiles), epoch);
+        } else if (static_cast<std::int32_t>(lane) <= cfg::col_blocks &&
+                   detail::block_exists<BN>(p, c.tile_row, c.tile_col, quarter, lane - 1)) {
+          ptx::st_release_sys(
+              my_events + final_index(parity, tile, quarter, lane - 1, 1, p.tiles), epoch);
         }
       } else if (static_cast<std::int32_t>(lane) < n_dst) {
         std::int32_t const pe = first_dst + static_cast<std::int32_t>(lane);
         std::uint32_t *flags = p.peers.translate(my_events, pe);
-        ptx::st_release_sys(flags + event_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles),
+        ptx::st_release_sys(flags + arrive_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles),
                             epoch);
       }
       if (lane == 0) {
         detail::count(p, ctr_partial_publish, p.n_pes == 1 ? 1 : n_dst);
       }
     }
-  } else if (p.n_pes > 1) {
-    // ---------------- reduce workers (task 2) ----------------
-    int const rw = warp - kReduceWarp0;
-    std::uint8_t *xpose = reduce_smem + rw * (32 * 128);
-    for (;;) {
-      std::uint32_t ticket = 0;
-      if (lane == 0) ticket = atomicAdd(&ctrl->reduce_ticket, 1u);
-      ticket = __shfl_sync(0xffffffffu, ticket, 0);
-      if (ticket >= static_cast<std::uint32_t>(p.n_reduce)) {
-        break;
-      }
-      std::int32_t const j = static_cast<std::int32_t>(ticket) / kQuarters;
-      std::int32_t const quarter = static_cast<std::int32_t>(ticket) % kQuarters;
-      std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
-      tile_coord const c = locate(sched, r);
-      std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
-      if (c.tile_row * kBlockM + quarter * 32 >= p.m) {
-        continue;  // no rows of this quarter exist
-      }
-
-      // Acquire: every PE's partial of this quarter has arrived (task 2
-      // "before" hook).
-      bool ok = true;
-      if (static_cast<std::int32_t>(lane) < p.n_pes) {
-        ok = detail::wait_flag(
-            my_events + event_index(parity, lane, tile, quarter, p.n_pes, p.tiles), epoch,
-            abort_word, p.timeout_ns);
-        if (!ok) detail::record_error(p, err_remote_timeout, tile, lane, 8);
-      }
-      if (!__all_sync(0xffffffffu, ok)) {
-        break;
-      }
-      std::uint64_t const t0 = ptx::now_ns();
-
-      std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
-      char const *slots0 = p.workspace + detail::slot_offset(p, parity, 0, j, kSlotBytes);
-      std::int64_t const src_stride = static_cast<std::int64_t>(p.slots_per_src) * kSlotBytes;
-      std::int32_t const out_row0 =
-          p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
-      bool const push_all = p.mode == mode_allreduce && !p.one_shot;
-
-      // 64-column blocks: sum the PE partials of rows [row0, row0 + 32) in
-      // PE order, transpose through shared memory, store row-major.
-#pragma unroll 1
-      for (int cb = 0; cb < BN / 64; ++cb) {
-        float acc[8][8];
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
-        }
-#pragma unroll 1
-        for (std::int32_t src = 0; src < p.n_pes; ++src) {
-          char const *slot = slots0 + src * src_stride;
-          if constexpr (kWireF32) {
-            uint4 w[16];
-#pragma unroll
-            for (int h = 0; h < 16; ++h) {
-              std::int64_t const vec = cb * 16 + h;
-              w[h] = ptx::ld_cg_v4(slot + (vec * kBlockM + quarter * 32 + lane) * 16);
-            }
-#pragma unroll
-            for (int h = 0; h < 16; ++h) {
-              acc[h / 2][(h % 2) * 4 + 0] += __uint_as_float(w[h].x);
-              acc[h / 2][(h % 2) * 4 + 1] += __uint_as_float(w[h].y);
-              acc[h / 2][(h % 2) * 4 + 2] += __uint_as_float(w[h].z);
-              acc[h / 2][(h % 2) * 4 + 3] += __uint_as_float(w[h].w);
-            }
-          } else {
-            uint4 w[8];
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              std::int64_t const vec = cb * 8 + g;
-              w[g] = ptx::ld_cg_v4(slot + (vec * kBlockM + quarter * 32 + lane) * 16);
-            }
-#pragma unroll
-            for (int g = 0; g < 8; ++g) {
-              acc[g][0] += ptx::bf16_lo(w[g].x);
-              acc[g][1] += ptx::bf16_hi(w[g].x);
-              acc[g][2] += ptx::bf16_lo(w[g].y);
-              acc[g][3] += ptx::bf16_hi(w[g].y);
-              acc[g][4] += ptx::bf16_lo(w[g].z);
-              acc[g][5] += ptx::bf16_hi(w[g].z);
-              acc[g][6] += ptx::bf16_lo(w[g].w);
-              acc[g][7] += ptx::bf16_hi(w[g].w);
-            }
-          }
-        }
-        // Row `lane` of the 32 x 64 block -> shared, 16 B per 8 columns,
-        // XOR-swizzled so that both the write and the read are conflict-free.
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          uint4 q;
-          q.x = ptx::pack_bf16x2(acc[g][0], acc[g][1]);
-          q.y = ptx::pack_bf16x2(acc[g][2], acc[g][3]);
-          q.z = ptx::pack_bf16x2(acc[g][4], acc[g][5]);
-          q.w = ptx::pack_bf16x2(acc[g][6], acc[g][7]);
-          *reinterpret_cast<uint4 *>(xpose + lane * 128 + ((g ^ (lane & 7)) * 16)) = q;
-        }
-        __syncwarp();
-        // Read back row-major: 8 lanes cover one 128 B row segment.
-        std::int32_t const g = lane % 8;
-        std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
-          uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
-          if (row0 + rr < p.m && col < p.n) {
-            std::int64_t const off = static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
-            if (push_all) {
-              for (std::int32_t pe = 0; pe < p.n_pes; ++pe) {
-                ptx::st_v4(p.peers.translate(p.out, pe) + off, q);
-              }
-            } else {
-              ptx::st_v4(p.out + off, q);
-            }
-          }
-        }
-        __syncwarp();
-      }
-
-      if (push_all) {
-        // All-gather publish: this quarter of the summed tile is in every
-        // PE's output.
-        ptx::fence_acq_rel_sys();
-        __syncwarp();
-        if (static_cast<std::int32_t>(lane) < p.n_pes) {
-          std::uint32_t *flags = p.peers.translate(my_events, lane);
-          ptx::st_release_sys(flags + event_index(parity, p.n_pes, tile, quarter, p.n_pes, p.tiles),
-                              epoch);
-        }
-      }
-      if (lane == 0) {
-        detail::count(p, ctr_reduce_tasks, 1);
-        detail::count(p, ctr_partial_acquire, p.n_pes);
-        if (push_all) detail::count(p, ctr_final_publish, p.n_pes);
-        detail::trace(p, 2, quarter, ticket, tile, t0);
-      }
-    }
-
-    if (p.mode == mode_allreduce && !p.one_shot) {
-      // This PE's output is complete once every quarter's final flag is set.
-      std::int32_t const total = p.tiles * kQuarters;
-      std::int32_t const workers = gridDim.x * kReduceWarps;
-      std::int32_t const worker = blockIdx.x * kReduceWarps + rw;
-      std::uint32_t seen = 0;
-      for (std::int32_t base = worker * 32; base < total; base += workers * 32) {
-        std::int32_t const idx = base + static_cast<std::int32_t>(lane);
-        bool ok = true;
-        bool const active = idx < total && (idx / kQuarters / p.n_tiles) * kBlockM +
-                                                   (idx % kQuarters) * 32 < p.m;
-        if (active) {
-          ok = detail::wait_flag(my_events + event_index(parity, p.n_pes, 0, 0, p.n_pes, p.tiles) + idx,
-                                 epoch, abort_word, p.timeout_ns);
-          if (!ok) {
-            detail::record_error(p, err_remote_timeout, idx / kQuarters, 0xffffffffu, 9);
-          } else {
-            ++seen;
-          }
-        }
-        if (!__all_sync(0xffffffffu, ok)) {
-          break;
-        }
-      }
-      for (int off = 16; off > 0; off >>= 1) seen += __shfl_xor_sync(0xffffffffu, seen, off);
-      if (lane == 0 && seen != 0) detail::count(p, ctr_final_acquire, seen);
-    }
   }
 
+  // ---------------- reduce workers (task 2) and the final wait ----------------
+  // Reduce warps work from the start; epilogue warps join once the GEMM queue
+  // is drained, so the reductions of the last GEMM wave use both groups.
+  if (p.n_pes > 1 && warp >= kEpilogueWarp0) {
+    int const worker = warp - kEpilogueWarp0;  // 0..7
+    std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
+    detail::reduce_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
+    if (p.mode == mode_allreduce && !p.one_shot) {
+      detail::wait_final<BN>(p, parity, epoch, my_events, abort_word,
+                             static_cast<std::int32_t>(blockIdx.x) * kWorkerWarps + worker,
+                             static_cast<std::int32_t>(gridDim.x) * kWorkerWarps, lane);
+    }
+  }
   // ---------------- teardown ----------------
   __syncwarp();
   ptx::tc_fence_before_sync();

@@ -5,19 +5,19 @@
 //   [0, 256 B)  control block: device task-queue tickets, the launch counter
 //               that tags every flag with the call's epoch, the error word
 //               and cumulative completion counters.
-//   [256 B, …)  event tensor, uint32 [2 parity][n_pes + 1][tiles][4 quarters]
-//     arrive[p][src][t][q] = epoch once PE `src` has delivered rows
-//                            [32q, 32q + 32) of its partial tile t;
-//     final [p][t][q]      = arrive[p][n_pes][t][q] = epoch once rows
-//                            [32q, 32q + 32) of the summed tile t are in this
-//                            PE's `out` (two-shot allreduce; written by the
-//                            owner on every PE).
+//   then the event tensor, two regions of uint32 flags:
+//     arrive[p][src][t][q]  (p < 2, src < n_pes, q < 4) = epoch once PE `src`
+//         has delivered rows [32q, 32q + 32) of its partial of tile t;
+//     final[p][t][q][c]     (c < 4) = epoch once rows [32q, 32q + 32) x columns
+//         [64c, 64c + 64) of the summed tile t are in this PE's `out`
+//         (two-shot allreduce: written by the owner into every PE; one PE:
+//         written by the epilogue).
 //   This is megacu's event tensor int32 [n_pes][tiles]
 //   (backends/nvshmem/cuda_event_tensor.cuh:13-39) refined to quarter tiles
-//   and tagged with the epoch (the golden's ready_base idiom,
-//   golden_gemm_allreduce.cu:384-385) so consecutive calls need no memset and
-//   no host barrier; the parity plane lets a PE run one call ahead of a slow
-//   owner in reduce-scatter mode.
+//   (and 64-column blocks for the result) and tagged with the epoch (the
+//   golden's ready_base idiom, golden_gemm_allreduce.cu:384-385), so
+//   consecutive calls need no memset and no host barrier; the parity plane
+//   lets a PE run one call ahead of a slow owner in reduce-scatter mode.
 //
 // workspace (symmetric when n_pes > 1): receive slots
 //   slot[p][src][j] = one tile_m x tile_n partial tile of PE `src`, j = the
@@ -38,7 +38,8 @@
 namespace megacu_b200 {
 
 inline constexpr std::int64_t kControlBytes = 256;
-inline constexpr std::int32_t kQuarters = 4;  // 32-row quarters of a 128-row tile
+inline constexpr std::int32_t kQuarters = 4;   // 32-row quarters of a 128-row tile
+inline constexpr std::int32_t kColBlocks = 4;  // 64-column blocks of a tile (at most)
 
 struct control_block {
   std::uint32_t gemm_ticket;    // next GEMM raster index to hand out
@@ -70,17 +71,29 @@ enum : std::int32_t {
   ctr_errors = 7,
 };
 
-// Word index of arrive[p][src][t][q] inside the event tensor.
-MEGACU_B200_LAYOUT_HD inline std::int64_t event_index(std::int32_t parity, std::int32_t src,
-                                                    std::int32_t tile, std::int32_t quarter,
+// Word index (after the control block) of arrive[p][src][t][q].
+MEGACU_B200_LAYOUT_HD inline std::int64_t arrive_index(std::int32_t parity, std::int32_t src,
+                                                     std::int32_t tile, std::int32_t quarter,
+                                                     std::int32_t n_pes, std::int32_t tiles) {
+  return ((static_cast<std::int64_t>(parity) * n_pes + src) * tiles + tile) * kQuarters + quarter;
+}
+
+// Word index (after the control block) of final[p][t][q][c].
+MEGACU_B200_LAYOUT_HD inline std::int64_t final_index(std::int32_t parity, std::int32_t tile,
+                                                    std::int32_t quarter, std::int32_t block,
                                                     std::int32_t n_pes, std::int32_t tiles) {
-  return ((static_cast<std::int64_t>(parity) * (n_pes + 1) + src) * tiles + tile) * kQuarters +
-         quarter;
+  std::int64_t const arrive_words = static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters;
+  return arrive_words +
+         ((static_cast<std::int64_t>(parity) * tiles + tile) * kQuarters + quarter) * kColBlocks +
+         block;
 }
 
 inline std::int64_t events_bytes_for(std::int32_t n_pes, std::int32_t tiles) {
-  return kControlBytes +
-         static_cast<std::int64_t>(2) * (n_pes + 1) * tiles * kQuarters * 4;
+  std::int64_t const words = static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters +
+                             static_cast<std::int64_t>(2) * tiles * kQuarters * kColBlocks;
+  return kControlBytes + 4 * words;
 }
 
 }  // namespace megacu_b200
+
+#undef MEGACU_B200_LAYOUT_HD

@@ -169,9 +169,23 @@ void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode
   }
 }
 
-static int64_t ev_index(int32_t parity, int32_t src, int32_t tile, int32_t quarter, int32_t n_pes,
-                        int32_t tiles) {
-  return (((int64_t)parity * (n_pes + 1) + src) * tiles + tile) * 4 + quarter;
+/* Event tensor words after the control block (restates layout.h):
+ * arrive[p][src][t][q] then final[p][t][q][c], q < 4 quarters, c < 4 blocks. */
+static int64_t arrive_idx(int32_t parity, int32_t src, int32_t tile, int32_t quarter,
+                          int32_t n_pes, int32_t tiles) {
+  return (((int64_t)parity * n_pes + src) * tiles + tile) * 4 + quarter;
+}
+
+static int64_t final_idx(int32_t parity, int32_t tile, int32_t quarter, int32_t block,
+                         int32_t n_pes, int32_t tiles) {
+  return (int64_t)2 * n_pes * tiles * 4 + (((int64_t)parity * tiles + tile) * 4 + quarter) * 4 +
+         block;
+}
+
+/* Does quarter q x 64-column block c of tile (row, col) hold an output element? */
+static int block_exists(const oracle_bf16_problem *p, int32_t row, int32_t col, int32_t q,
+                        int32_t c) {
+  return (int64_t)row * p->tile_m + q * 32 < p->m && (int64_t)col * p->tile_n + c * 64 < p->n;
 }
 
 int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
@@ -200,6 +214,8 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
     }
   }
 
+  int32_t const blocks = p->tile_n / 64;
+
   /* Task 0 (GEMM tile) + its publish, in queue (raster) order. */
   for (int32_t r = 0; r < tiles; ++r) {
     int32_t c[4];
@@ -211,16 +227,21 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
       for (int32_t q = 0; q < 4; ++q) {
         if ((int64_t)c[0] * p->tile_m + q * 32 >= m) continue;
         if (np == 1) {
+          /* One PE: the quarter is arrived and its existing blocks final. */
           if (events) {
-            events[0][ev_index(parity, 0, t, q, 1, tiles)] = epoch;
-            events[0][ev_index(parity, 1, t, q, 1, tiles)] = epoch;
+            events[0][arrive_idx(parity, 0, t, q, 1, tiles)] = epoch;
+            for (int32_t cb = 0; cb < blocks; ++cb) {
+              if (block_exists(p, c[0], c[1], q, cb)) {
+                events[0][final_idx(parity, t, q, cb, 1, tiles)] = epoch;
+              }
+            }
           }
           cnt[pe * 8 + 2] += 1;
         } else {
           int32_t const first = p->one_shot ? 0 : c[2];
           int32_t const n_dst = p->one_shot ? np : 1;
           for (int32_t d = 0; d < n_dst; ++d) {
-            if (events) events[first + d][ev_index(parity, pe, t, q, np, tiles)] = epoch;
+            if (events) events[first + d][arrive_idx(parity, pe, t, q, np, tiles)] = epoch;
           }
           cnt[pe * 8 + 2] += (uint64_t)n_dst;
         }
@@ -232,16 +253,19 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
     memcpy(out[0], part[0], sizeof(float) * (size_t)(m * n));
   } else {
     int64_t const rows_per_pe = m / np;
+    int32_t const per_tile = 4 * blocks;
     for (int32_t me = 0; me < np && rc == 0; ++me) {
       int32_t owned = p->one_shot ? tiles : (tiles > me ? (tiles - me + np - 1) / np : 0);
-      for (int32_t ticket = 0; ticket < owned * 4 && rc == 0; ++ticket) {
-        int32_t const j = ticket / 4, q = ticket % 4;
+      /* Task 2 sub-tasks: (owned tile, 32-row quarter, 64-column block). */
+      for (int32_t ticket = 0; ticket < owned * per_tile && rc == 0; ++ticket) {
+        int32_t const j = ticket / per_tile;
+        int32_t const q = (ticket % per_tile) / blocks;
+        int32_t const cb = ticket % blocks;
         int32_t const r = p->one_shot ? j : j * np + me;
         int32_t c[4];
         oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
         int32_t const t = c[0] * nt + c[1];
-        int64_t const row0 = (int64_t)c[0] * p->tile_m + q * 32;
-        if (row0 >= m) {
+        if (!block_exists(p, c[0], c[1], q, cb)) {
           if (reduce_order) reduce_order[me][ticket] = -1;
           continue;
         }
@@ -249,14 +273,15 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
         /* Task 2 "before": acquire every PE's quarter. */
         if (events) {
           for (int32_t src = 0; src < np; ++src) {
-            if (events[me][ev_index(parity, src, t, q, np, tiles)] != epoch) rc = -2;
+            if (events[me][arrive_idx(parity, src, t, q, np, tiles)] != epoch) rc = -2;
           }
         }
         cnt[me * 8 + 1] += 1;
         cnt[me * 8 + 3] += (uint64_t)np;
-        int64_t const c0 = (int64_t)c[1] * p->tile_n;
+        int64_t const row0 = (int64_t)c[0] * p->tile_m + q * 32;
+        int64_t const c0 = (int64_t)c[1] * p->tile_n + cb * 64;
         for (int64_t row = row0; row < row0 + 32 && row < m; ++row) {
-          for (int64_t col = c0; col < c0 + p->tile_n && col < n; ++col) {
+          for (int64_t col = c0; col < c0 + 64 && col < n; ++col) {
             float s = 0.0f;
             for (int32_t src = 0; src < np; ++src) s += part[src][row * n + col];
             if (p->mode == 1) {
@@ -270,20 +295,22 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
         }
         if (two_shot_ar) {
           for (int32_t pe = 0; pe < np; ++pe) {
-            if (events) events[pe][ev_index(parity, np, t, q, np, tiles)] = epoch;
+            if (events) events[pe][final_idx(parity, t, q, cb, np, tiles)] = epoch;
           }
           cnt[me * 8 + 4] += (uint64_t)np;
         }
       }
     }
     if (two_shot_ar) {
-      /* Every PE waits for every final quarter before its call completes. */
+      /* Every PE waits for every final block before its call completes. */
       for (int32_t pe = 0; pe < np; ++pe) {
         for (int32_t t = 0; t < tiles; ++t) {
           for (int32_t q = 0; q < 4; ++q) {
-            if ((int64_t)(t / nt) * p->tile_m + q * 32 >= m) continue;
-            if (events && events[pe][ev_index(parity, np, t, q, np, tiles)] != epoch) rc = -3;
-            cnt[pe * 8 + 5] += 1;
+            for (int32_t cb = 0; cb < blocks; ++cb) {
+              if (!block_exists(p, t / nt, t % nt, q, cb)) continue;
+              if (events && events[pe][final_idx(parity, t, q, cb, np, tiles)] != epoch) rc = -3;
+              cnt[pe * 8 + 5] += 1;
+            }
           }
         }
       }

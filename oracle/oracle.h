@@ -77,14 +77,16 @@ typedef struct oracle_bf16_problem {
  * The B200 megakernel's tile-task graph for one call on n_pes logical PEs.
  * a[pe], b[pe]: bf16 values held in fp32. out[pe]: fp32 result, [m, n] for
  * allreduce, [m / n_pes, n] for reduce-scatter (not rounded to bf16).
- * events[pe] (optional): the event tensor words after the control block,
- * uint32 [2][n_pes + 1][tiles][4], updated in place exactly as the device
- * does. counters[pe * 8 + i] (optional) receive the per-call deltas of the
- * device counters. gemm_order (optional, [tiles]) receives the tile id of
- * each GEMM ticket; reduce_order[pe] (optional, [tiles * 4]) the tile id of
- * each reduce ticket of PE pe, or -1 where the ticket is skipped (a 32-row
- * quarter that lies wholly below m). Returns 0, or a negative number if the
- * graph was inconsistent (an acquire found a flag unset).
+ * events[pe] (optional): the event tensor words after the control block —
+ * arrive uint32 [2][n_pes][tiles][4] then final uint32 [2][tiles][4][4] —
+ * updated in place exactly as the device does. counters[pe * 8 + i]
+ * (optional) receive the per-call deltas of the device counters. gemm_order
+ * (optional, [tiles]) receives the tile id of each GEMM ticket;
+ * reduce_order[pe] (optional, [tiles * 4 * tile_n / 64]) the tile id of each
+ * reduce ticket (owned tile, 32-row quarter, 64-column block) of PE pe, or -1
+ * where the ticket is skipped (a block that holds no output element).
+ * Returns 0, or a negative number if the graph was inconsistent (an acquire
+ * found a flag unset).
  */
 int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
                      const float *const *b, float *const *out, uint32_t *const *events,

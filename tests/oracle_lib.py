@@ -132,7 +132,7 @@ def bf16_call(a_list, b_list, *, m, n, k, tile_n, mode=0, one_shot=False, group_
             *[e.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)) for e in events])
     counters = np.zeros((n_pes, 8), np.uint64)
     gemm_order = np.zeros(tiles, np.int32)
-    reduce_orders = [np.full(tiles * 4, -1, np.int32) for _ in range(n_pes)]
+    reduce_orders = [np.full(tiles * 4 * (tile_n // 64), -1, np.int32) for _ in range(n_pes)]
     rop = (ctypes.POINTER(ctypes.c_int32) * n_pes)(
         *[r.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) for r in reduce_orders])
     rc = load().oracle_bf16_call(ctypes.byref(p), _fp_array(a_list), _fp_array(b_list),
@@ -158,5 +158,6 @@ def bf16_tiles(a_list, b_list, tile_ids, *, m, n, k, tile_n, wire_bytes=2, threa
 
 
 def event_tensor_words(n_pes: int, tiles: int) -> int:
-    """uint32 words of the event tensor after the control block."""
-    return 2 * (n_pes + 1) * tiles * 4
+    """uint32 words of the event tensor after the control block
+    (arrive [2][n_pes][tiles][4], then final [2][tiles][4][4])."""
+    return 2 * n_pes * tiles * 4 + 2 * tiles * 16

@@ -120,26 +120,34 @@ def test_bf16_graph_counts_and_events(n_pes, mode, one_shot, m, n, tile_n):
     # every raster index maps to a distinct tile
     assert sorted(r["gemm_order"].tolist()) == list(range(tiles))
     active = sum(1 for t in range(tiles) for q in range(4) if (t // n_tiles) * 128 + q * 32 < m)
+    blocks = [(t, q, cb) for t in range(tiles) for q in range(4) for cb in range(tile_n // 64)
+              if (t // n_tiles) * 128 + q * 32 < m and (t % n_tiles) * tile_n + cb * 64 < n]
     c = r["counters"]
     assert np.all(c[:, 0] == tiles) and np.all(c[:, 6] == 1) and np.all(c[:, 7] == 0)
     reduced = [sum(1 for t in ro if t >= 0) for ro in r["reduce_order"]]
     if n_pes == 1:
         assert c[0, 2] == active and c[0, 1] == 0
     elif one_shot:
-        assert all(x == active for x in reduced)
+        assert all(x == len(blocks) for x in reduced)
         assert np.all(c[:, 2] == active * n_pes)
     else:
-        assert sum(reduced) == active  # every active quarter reduced exactly once
+        assert sum(reduced) == len(blocks)  # every existing block reduced exactly once
         assert np.all(c[:, 2] == active)
     assert c[:, 1].tolist() == reduced
     assert np.all(c[:, 3] == np.array(reduced) * n_pes)
     two_shot_ar = n_pes > 1 and mode == 0 and not one_shot
-    assert np.all(c[:, 5] == (active if two_shot_ar else 0))
+    assert np.all(c[:, 5] == (len(blocks) if two_shot_ar else 0))
     # the event tensor holds the epoch exactly where the graph published
     for pe in range(n_pes):
-        ev = r["events"][pe].reshape(2, n_pes + 1, tiles, 4)
-        assert np.all(ev[0] == 0)  # epoch 5 -> parity plane 1 only
-        assert set(np.unique(ev[1]).tolist()) <= {0, 5}
+        words = r["events"][pe]
+        arrive = words[:2 * n_pes * tiles * 4].reshape(2, n_pes, tiles, 4)
+        final = words[2 * n_pes * tiles * 4:].reshape(2, tiles, 4, 4)
+        assert np.all(arrive[0] == 0) and np.all(final[0] == 0)  # epoch 5: parity plane 1
+        assert set(np.unique(arrive[1]).tolist()) <= {0, 5}
+        if n_pes == 1 or two_shot_ar:
+            assert int((final[1] == 5).sum()) == len(blocks)
+        else:
+            assert np.all(final[1] == 0)
 
 
 def test_locate_matches_product_schedule():
