@@ -208,7 +208,7 @@ megacu_status megacu_b200_events_bytes(megacu_gemm_ar_problem_v2 problem,
 
 /*
  * Tile plan of a bf16 call (host only, no GPU): info[0] tile_m, [1] tile_n,
- * [2] m_tiles, [3] n_tiles, [4] one_shot, [5] receive slots per (parity, PE),
+ * [2] m_tiles, [3] n_tiles, [4] one_shot, [5] partial slots per parity plane,
  * [6] raster band height in tile rows, [7] bytes per element on the wire.
  */
 megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem,

@@ -210,15 +210,11 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
     pl.one_shot = pl.m_tiles == 1 ? 1 : 0;  // latency-bound shapes: one hop
   }
   pl.wire_bytes = p.deterministic ? 4 : 2;
-  if (n_pes == 1) {
-    pl.slots_per_src = 0;
-  } else if (pl.one_shot) {
-    pl.slots_per_src = pl.tiles;
-  } else {
-    pl.slots_per_src = (pl.tiles + n_pes - 1) / n_pes;
-  }
-  pl.workspace_bytes = static_cast<std::int64_t>(2) * n_pes * pl.slots_per_src * kBlockM *
-                       pl.tile_n * pl.wire_bytes;
+  // Each PE keeps its own partial of every tile (two parity planes); the
+  // tile's reducers read it over NVLink.
+  pl.slots_per_src = n_pes == 1 ? 0 : pl.tiles;
+  pl.workspace_bytes =
+      static_cast<std::int64_t>(2) * pl.slots_per_src * kBlockM * pl.tile_n * pl.wire_bytes;
   pl.events_bytes = events_bytes_for(n_pes, pl.tiles);
   out = pl;
   return ok_status();
@@ -310,7 +306,9 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   std::int32_t const reduce_tiles =
       n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
   prm.n_reduce = reduce_tiles * kQuarters * (pl.tile_n / 64);
-  prm.slots_per_src = pl.slots_per_src;
+  // Two-shot allreduce: every PE copies the other owners' finished blocks.
+  bool const gathers = n_pes > 1 && prm.mode == mode_allreduce && !pl.one_shot;
+  prm.n_gather = gathers ? pl.tiles * kQuarters * (pl.tile_n / 64) : 0;
   prm.rows_per_pe = static_cast<std::int32_t>(problem.m / n_pes);
   prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
   prm.out = static_cast<__nv_bfloat16 *>(out);

@@ -10,20 +10,22 @@
 //  * one CTA per SM, 10 warps with fixed roles
 //      warp 0      task fetcher + TMA producer (GEMM task queue)
 //      warp 1      TMEM allocator + tcgen05.mma issuer (one thread)
-//      warps 2..5  epilogue: TMEM -> registers -> bf16/fp32 -> destination,
-//                  then publish (task 0's "after" hook)
-//      warps 6..9  reduce workers (task 2): each warp independently pulls
-//                  quarter-tile sub-tasks from the reduce queue, acquires
-//                  the event tensor, sums the PE partials in PE order in
-//                  fp32 and writes the result (plus the all-gather push)
+//      warps 2..5  epilogue: TMEM -> registers -> bf16/fp32 -> this PE's own
+//                  partial slot, then publish (task 0's "after" hook); once
+//                  the GEMM queue is drained they join the workers below
+//      warps 6..9  workers: reduce sub-tasks (task 2: acquire, PE-order fp32
+//                  sum of every PE's partial read over NVLink, store into this
+//                  PE's out), then gather sub-tasks (copy finished blocks of
+//                  tiles owned by other PEs from the owner's out)
 //  * the static tile_grid dispatcher (tile = blockIdx + i * gridDim,
 //    tile_grid_device.cuh:13-23) is replaced by device task queues: an
 //    atomic ticket per queue, tickets mapped to tiles by tile_schedule.h;
-//  * the event tensor is per (PE, tile, 32-row quarter), tagged with the
-//    call's epoch, published with st.release.sys after a sys-scope fence and
-//    acquired with ld.acquire.sys under a bounded wait;
-//  * partial tiles are pushed (not pulled): each epilogue warp stores its 32
-//    rows straight into the owner's receive slot over NVLink.
+//  * the event tensor is per (PE, tile, 32-row quarter) for partials and per
+//    (tile, quarter, 64-column block) for results, tagged with the call's
+//    epoch, published with st.release.sys after a fence and acquired with
+//    ld.acquire.sys under a bounded wait;
+//  * every byte crosses NVLink as a load by the consumer: producers write only
+//    their own memory (so their fences are cheap) and push 4-byte flags.
 //
 // No loads here use cluster multicast.
 #pragma once
@@ -47,8 +49,8 @@ inline constexpr int kTaskRing = 4;
 inline constexpr int kEpilogueWarp0 = 2;
 inline constexpr int kReduceWarp0 = 6;
 inline constexpr int kReduceWarps = 4;
-// Warps that may run reduce sub-tasks: the reduce warps from the start, the
-// epilogue warps once the GEMM queue is drained.
+// Warps that may run reduce / gather sub-tasks: the worker warps from the
+// start, the epilogue warps once the GEMM queue is drained.
 inline constexpr int kWorkerWarps = 8;
 inline constexpr std::uint64_t kLocalTimeoutNs = 4000000000ull;
 
@@ -60,7 +62,7 @@ struct gemm_config {
   static constexpr int b_bytes = kBlockK * BN * 2;
   static constexpr int stage_bytes = a_bytes + b_bytes;
   static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8
-  static constexpr int col_blocks = BN / 64;                   // reduce sub-tasks per quarter
+  static constexpr int col_blocks = BN / 64;                   // sub-tasks per quarter
   static constexpr int reduce_bytes = kWorkerWarps * 32 * 128; // transpose tiles
   static constexpr int n_barriers = 2 * stages + 4 + 2 * kTaskRing + 1;
   static constexpr int aux_bytes = n_barriers * 8 + kTaskRing * 4 + 16;
@@ -75,12 +77,12 @@ struct gemm_ar_params {
   std::int32_t mode;          // mode_allreduce / mode_reduce_scatter
   std::int32_t one_shot;      // 1: every PE reduces every tile
   std::int32_t group_m;
-  std::int32_t n_reduce;      // reduce sub-tasks on this PE (quarters)
-  std::int32_t slots_per_src; // receive slots per (parity, src)
+  std::int32_t n_reduce;      // reduce sub-tasks on this PE
+  std::int32_t n_gather;      // gather sub-tasks on this PE (two-shot allreduce)
   std::int32_t rows_per_pe;   // reduce-scatter: output rows per PE
   std::uint64_t timeout_ns;   // bound of cross-GPU waits
   __nv_bfloat16 *out;         // this PE's output
-  char *workspace;            // this PE's receive slots (symmetric)
+  char *workspace;            // this PE's partial slots (symmetric)
   std::uint32_t *events;      // this PE's events buffer (symmetric)
   megacu::nvshmem::peer_table peers;
   unsigned long long *trace;
@@ -158,12 +160,10 @@ __device__ __forceinline__ bool wait_flag(std::uint32_t const *flag, std::uint32
   }
 }
 
-// Byte offset of receive slot (parity, src, j).
-__device__ __forceinline__ std::int64_t slot_offset(gemm_ar_params const &p, std::uint32_t parity,
-                                                    std::int32_t src, std::int32_t j,
-                                                    std::int64_t slot_bytes) {
-  return ((static_cast<std::int64_t>(parity) * p.n_pes + src) * p.slots_per_src + j) *
-         slot_bytes;
+// Byte offset of this PE's partial slot (parity, tile) in its workspace.
+__device__ __forceinline__ std::int64_t slot_offset(std::uint32_t parity, std::int32_t tile,
+                                                    std::int32_t tiles, std::int64_t slot_bytes) {
+  return (static_cast<std::int64_t>(parity) * tiles + tile) * slot_bytes;
 }
 
 // Does the 32-row quarter q x 64-column block c of tile (row, col) hold any
@@ -175,13 +175,31 @@ __device__ __forceinline__ bool block_exists(gemm_ar_params const &p, std::int32
   return tile_row * kBlockM + quarter * 32 < p.m && tile_col * BN + block * 64 < p.n;
 }
 
-// Reduce worker (task 2): one warp pulls sub-tasks = (owned tile, 32-row
+__device__ __forceinline__ std::uint32_t draw_ticket(std::uint32_t *counter, std::uint32_t lane) {
+  std::uint32_t ticket = 0;
+  if (lane == 0) ticket = atomicAdd(counter, 1u);
+  return __shfl_sync(0xffffffffu, ticket, 0);
+}
+
+__device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 w) {
+  acc[0] += ptx::bf16_lo(w.x);
+  acc[1] += ptx::bf16_hi(w.x);
+  acc[2] += ptx::bf16_lo(w.y);
+  acc[3] += ptx::bf16_hi(w.y);
+  acc[4] += ptx::bf16_lo(w.z);
+  acc[5] += ptx::bf16_hi(w.z);
+  acc[6] += ptx::bf16_lo(w.w);
+  acc[7] += ptx::bf16_hi(w.w);
+}
+
+// Reduce worker (task 2): one warp takes sub-tasks = (reduced tile, 32-row
 // quarter, 64-column block) from the reduce queue until it is empty. For each:
-// acquire every PE's arrive flag of the quarter, sum the PE partials in PE
+// acquire every PE's arrive flag of the quarter, load the block of every PE's
+// partial slot (its own memory for this PE, NVLink for the others), sum in PE
 // order 0..n_pes-1 in fp32 (two PEs' loads in flight at a time), round to
 // bf16, transpose 32 x 64 through `xpose` (4 KiB of shared memory) and store
-// row-major into this PE's out, or — two-shot allreduce — into every PE's out
-// followed by the final flags.
+// row-major into this PE's out. Two-shot allreduce then publishes the block's
+// final flag on every PE, which copy it from here (gather_tasks).
 template <int BN, bool kWireF32>
 __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_schedule const &sched,
                                              std::uint32_t parity, std::uint32_t epoch,
@@ -191,13 +209,11 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
   constexpr int kWireBytes = kWireF32 ? 4 : 2;
   constexpr int kBlocks = BN / 64;
   constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
+  constexpr std::int64_t kVecStride = kBlockM * 16;  // bytes between wire vectors of a row
   control_block *ctrl = control(p);
-  bool const push_all = p.mode == mode_allreduce && !p.one_shot;
-  std::int64_t const src_stride = static_cast<std::int64_t>(p.slots_per_src) * kSlotBytes;
+  bool const publish_final = p.mode == mode_allreduce && !p.one_shot;
   for (;;) {
-    std::uint32_t ticket = 0;
-    if (lane == 0) ticket = atomicAdd(&ctrl->reduce_ticket, 1u);
-    ticket = __shfl_sync(0xffffffffu, ticket, 0);
+    std::uint32_t const ticket = draw_ticket(&ctrl->reduce_ticket, lane);
     if (ticket >= static_cast<std::uint32_t>(p.n_reduce)) {
       break;
     }
@@ -212,7 +228,7 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
       continue;  // no output element lives in this block
     }
 
-    // Task 2 "before": every PE's partial of this quarter has arrived.
+    // Task 2 "before": every PE's partial of this quarter is ready.
     bool ok = true;
     if (static_cast<std::int32_t>(lane) < p.n_pes) {
       ok = wait_flag(my_events + arrive_index(parity, lane, tile, quarter, p.n_pes, p.tiles),
@@ -222,6 +238,7 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
     if (!__all_sync(0xffffffffu, ok)) {
       break;
     }
+    __syncwarp();  // orders every lane's loads after the lanes' acquires
     std::uint64_t const t0 = ptx::now_ns();
 
     float acc[8][8];
@@ -230,17 +247,16 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
     }
-    // Lane = row; vector (v, row) of a slot sits at (v * 128 + row) * 16.
-    char const *base = p.workspace + slot_offset(p, parity, 0, j, kSlotBytes) +
-                       (static_cast<std::int64_t>(quarter) * 32 + lane) * 16;
+    // Lane = row of the quarter; vector (v, row) of a slot at (v * 128 + row) * 16.
+    std::int64_t const in_slot = slot_offset(parity, tile, p.tiles, kSlotBytes) +
+                                 (static_cast<std::int64_t>(quarter) * 32 + lane) * 16;
     if constexpr (kWireF32) {
 #pragma unroll 1
       for (std::int32_t src = 0; src < p.n_pes; ++src) {
+        char const *base = p.peers.translate(p.workspace, src) + in_slot;
         uint4 w[16];
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          w[h] = ptx::ld_cg_v4(base + src * src_stride + (cb * 16 + h) * (kBlockM * 16));
-        }
+        for (int h = 0; h < 16; ++h) w[h] = ptx::ld_cg_v4(base + (cb * 16 + h) * kVecStride);
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
           acc[h / 2][(h % 2) * 4 + 0] += __uint_as_float(w[h].x);
@@ -253,40 +269,20 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
 #pragma unroll 1
       for (std::int32_t src = 0; src < p.n_pes; src += 2) {
         bool const pair = src + 1 < p.n_pes;
+        char const *base0 = p.peers.translate(p.workspace, src) + in_slot;
         uint4 w0[8], w1[8];
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          w0[g] = ptx::ld_cg_v4(base + src * src_stride + (cb * 8 + g) * (kBlockM * 16));
+        for (int g = 0; g < 8; ++g) w0[g] = ptx::ld_cg_v4(base0 + (cb * 8 + g) * kVecStride);
+        if (pair) {
+          char const *base1 = p.peers.translate(p.workspace, src + 1) + in_slot;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) w1[g] = ptx::ld_cg_v4(base1 + (cb * 8 + g) * kVecStride);
         }
+#pragma unroll
+        for (int g = 0; g < 8; ++g) add_bf16x8(acc[g], w0[g]);
         if (pair) {
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            w1[g] = ptx::ld_cg_v4(base + (src + 1) * src_stride + (cb * 8 + g) * (kBlockM * 16));
-          }
-        }
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          acc[g][0] += ptx::bf16_lo(w0[g].x);
-          acc[g][1] += ptx::bf16_hi(w0[g].x);
-          acc[g][2] += ptx::bf16_lo(w0[g].y);
-          acc[g][3] += ptx::bf16_hi(w0[g].y);
-          acc[g][4] += ptx::bf16_lo(w0[g].z);
-          acc[g][5] += ptx::bf16_hi(w0[g].z);
-          acc[g][6] += ptx::bf16_lo(w0[g].w);
-          acc[g][7] += ptx::bf16_hi(w0[g].w);
-        }
-        if (pair) {
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            acc[g][0] += ptx::bf16_lo(w1[g].x);
-            acc[g][1] += ptx::bf16_hi(w1[g].x);
-            acc[g][2] += ptx::bf16_lo(w1[g].y);
-            acc[g][3] += ptx::bf16_hi(w1[g].y);
-            acc[g][4] += ptx::bf16_lo(w1[g].z);
-            acc[g][5] += ptx::bf16_hi(w1[g].z);
-            acc[g][6] += ptx::bf16_lo(w1[g].w);
-            acc[g][7] += ptx::bf16_hi(w1[g].w);
-          }
+          for (int g = 0; g < 8; ++g) add_bf16x8(acc[g], w1[g]);
         }
       }
     }
@@ -313,20 +309,13 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
       std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
       uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
       if (row0 + rr < p.m && col < p.n) {
-        std::int64_t const off = static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
-        if (push_all) {
-          for (std::int32_t pe = 0; pe < p.n_pes; ++pe) {
-            ptx::st_v4(p.peers.translate(p.out, pe) + off, q);
-          }
-        } else {
-          ptx::st_v4(p.out + off, q);
-        }
+        ptx::st_v4(p.out + static_cast<std::int64_t>(out_row0 + rr) * p.n + col, q);
       }
     }
     __syncwarp();
 
-    if (push_all) {
-      // All-gather publish: this block of the summed tile is in every PE's out.
+    if (publish_final) {
+      // The block is in this PE's out: every PE may copy it from here.
       ptx::fence_acq_rel_sys();
       __syncwarp();
       if (static_cast<std::int32_t>(lane) < p.n_pes) {
@@ -338,46 +327,66 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
     if (lane == 0) {
       count(p, ctr_reduce_tasks, 1);
       count(p, ctr_partial_acquire, p.n_pes);
-      if (push_all) count(p, ctr_final_publish, p.n_pes);
+      if (publish_final) count(p, ctr_final_publish, p.n_pes);
       trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
     }
   }
 }
 
-// Two-shot allreduce: this PE's output is complete once every final flag of
-// every existing (tile, quarter, column block) is set. Worker `worker` of
-// `workers` polls its share, 32 flags per warp step.
+// Gather worker (two-shot allreduce, task 2's second half): copies every
+// existing 32 x 64 block of the tiles other PEs own from the owner's out
+// (NVLink loads) into this PE's out, once the owner's final flag is set.
 template <int BN>
-__device__ __forceinline__ void wait_final(gemm_ar_params const &p, std::uint32_t parity,
-                                           std::uint32_t epoch, std::uint32_t *my_events,
-                                           std::uint32_t const *abort_word, std::int32_t worker,
-                                           std::int32_t workers, std::uint32_t lane) {
+__device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, tile_schedule const &sched,
+                                             std::uint32_t parity, std::uint32_t epoch,
+                                             std::uint32_t *my_events,
+                                             std::uint32_t const *abort_word, std::uint32_t lane) {
   constexpr int kBlocks = BN / 64;
-  std::int32_t const total = p.tiles * kQuarters * kBlocks;
-  std::uint32_t seen = 0;
-  for (std::int32_t first = worker * 32; first < total; first += workers * 32) {
-    std::int32_t const idx = first + static_cast<std::int32_t>(lane);
-    bool ok = true;
-    if (idx < total) {
-      std::int32_t const tile = idx / (kQuarters * kBlocks);
-      std::int32_t const quarter = (idx / kBlocks) % kQuarters;
-      std::int32_t const cb = idx % kBlocks;
-      if (block_exists<BN>(p, tile / p.n_tiles, tile % p.n_tiles, quarter, cb)) {
-        ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
-                       abort_word, p.timeout_ns);
-        if (!ok) {
-          record_error(p, err_remote_timeout, tile, 0xffffffffu, 9);
-        } else {
-          ++seen;
-        }
-      }
-    }
-    if (!__all_sync(0xffffffffu, ok)) {
+  control_block *ctrl = control(p);
+  for (;;) {
+    std::uint32_t const ticket = draw_ticket(&ctrl->gather_ticket, lane);
+    if (ticket >= static_cast<std::uint32_t>(p.n_gather)) {
       break;
     }
+    std::int32_t const r = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
+    std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks);
+    std::int32_t const quarter = rem / kBlocks;
+    std::int32_t const cb = rem % kBlocks;
+    tile_coord const c = locate(sched, r);
+    if (c.owner == p.my_pe || !block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
+      continue;
+    }
+    std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+    bool ok = true;
+    if (lane == 0) {
+      ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
+                     abort_word, p.timeout_ns);
+      if (!ok) record_error(p, err_remote_timeout, tile, c.owner, 9);
+    }
+    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+      break;
+    }
+    __syncwarp();  // orders every lane's loads after lane 0's acquire
+    std::uint64_t const t0 = ptx::now_ns();
+    std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
+    std::int32_t const col = c.tile_col * BN + cb * 64 + static_cast<std::int32_t>(lane % 8) * 8;
+    __nv_bfloat16 const *src = p.peers.translate(p.out, c.owner);
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
+      if (row < p.m && col < p.n) v[i] = ptx::ld_cg_v4(src + static_cast<std::int64_t>(row) * p.n + col);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
+      if (row < p.m && col < p.n) ptx::st_v4(p.out + static_cast<std::int64_t>(row) * p.n + col, v[i]);
+    }
+    if (lane == 0) {
+      count(p, ctr_final_acquire, 1);
+      trace(p, 3, quarter * kBlocks + cb, ticket, tile, t0);
+    }
   }
-  for (int off = 16; off > 0; off >>= 1) seen += __shfl_xor_sync(0xffffffffu, seen, off);
-  if (lane == 0 && seen != 0) count(p, ctr_final_acquire, seen);
 }
 
 }  // namespace detail
@@ -588,12 +597,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       std::int32_t const gcol0 = c.tile_col * BN;
       std::uint32_t const t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) +
                                   buf * BN;
-      // Destinations of this tile's partial (n_pes > 1).
+      // Who reduces this tile: its owner (two-shot / RS) or every PE (one-shot).
       std::int32_t const first_dst = p.one_shot ? 0 : c.owner;
       std::int32_t const n_dst = p.n_pes == 1 ? 0 : (p.one_shot ? p.n_pes : 1);
-      std::int32_t const slot_j = p.one_shot ? r : c.local;
-      // A 32-row quarter wholly below m carries no data: it is neither sent
-      // nor published, and no reduce task exists for it.
+      char *const slot_base = p.workspace + detail::slot_offset(parity, tile, p.tiles, kSlotBytes);
+      // A 32-row quarter wholly below m carries no data: it is neither
+      // written nor published, and no reduce task exists for it.
       bool const active = c.tile_row * kBlockM + quarter * 32 < p.m;
 
 #pragma unroll 1
@@ -618,28 +627,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         } else {
+          // This PE's own partial slot (local memory); reducers read it over NVLink.
           constexpr int kVecs = 32 / kVecCols;  // wire vectors per 32-column chunk
-          uint4 q[kVecs];
 #pragma unroll
           for (int j = 0; j < kVecs; ++j) {
+            uint4 q;
             if constexpr (kWireF32) {
-              q[j] = make_uint4(v[4 * j + 0], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              q = make_uint4(v[4 * j + 0], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             } else {
-              q[j].x = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 0]), __uint_as_float(v[8 * j + 1]));
-              q[j].y = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
-              q[j].z = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
-              q[j].w = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
+              q.x = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 0]), __uint_as_float(v[8 * j + 1]));
+              q.y = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3]));
+              q.z = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5]));
+              q.w = ptx::pack_bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7]));
             }
-          }
-          for (std::int32_t d = 0; d < n_dst; ++d) {
-            std::int32_t const pe = first_dst + d;
-            char *slot_base = p.peers.translate(p.workspace, pe) +
-                              detail::slot_offset(p, parity, p.my_pe, slot_j, kSlotBytes);
-#pragma unroll
-            for (int j = 0; j < kVecs; ++j) {
-              std::int64_t const vec = ch * kVecs + j;
-              ptx::st_v4(slot_base + (vec * kBlockM + row_in_tile) * 16, q[j]);
-            }
+            std::int64_t const vec = ch * kVecs + j;
+            ptx::st_v4(slot_base + (vec * kBlockM + row_in_tile) * 16, q);
           }
         }
       }
@@ -655,7 +657,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!active) {
         continue;
       }
-      // Publish this quarter (task 0 "after" hook).
+      // Publish this quarter (task 0 "after" hook). The data is in this PE's
+      // own memory, so the fence only waits for local writes.
       if (p.n_pes > 1) {
         ptx::fence_acq_rel_sys();
       } else {
@@ -684,19 +687,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---------------- reduce workers (task 2) and the final wait ----------------
-  // Reduce warps work from the start; epilogue warps join once the GEMM queue
-  // is drained, so the reductions of the last GEMM wave use both groups.
+  // ---------------- workers: reduce, then gather (task 2) ----------------
+  // Worker warps start at once; epilogue warps join once the GEMM queue is
+  // drained, so the last GEMM wave's reductions use both groups.
   if (p.n_pes > 1 && warp >= kEpilogueWarp0) {
     int const worker = warp - kEpilogueWarp0;  // 0..7
     std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
     detail::reduce_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
-    if (p.mode == mode_allreduce && !p.one_shot) {
-      detail::wait_final<BN>(p, parity, epoch, my_events, abort_word,
-                             static_cast<std::int32_t>(blockIdx.x) * kWorkerWarps + worker,
-                             static_cast<std::int32_t>(gridDim.x) * kWorkerWarps, lane);
-    }
+    detail::gather_tasks<BN>(p, sched, parity, epoch, my_events, abort_word, lane);
   }
+
   // ---------------- teardown ----------------
   __syncwarp();
   ptx::tc_fence_before_sync();
@@ -713,6 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       ctrl->gemm_ticket = 0;
       ctrl->reduce_ticket = 0;
+      ctrl->gather_ticket = 0;
       ctrl->trace_count = 0;
       ctrl->launch_count = epoch;
       atomicAdd(&ctrl->counters[ctr_launches], 1ull);

@@ -9,9 +9,9 @@
 //     arrive[p][src][t][q]  (p < 2, src < n_pes, q < 4) = epoch once PE `src`
 //         has delivered rows [32q, 32q + 32) of its partial of tile t;
 //     final[p][t][q][c]     (c < 4) = epoch once rows [32q, 32q + 32) x columns
-//         [64c, 64c + 64) of the summed tile t are in this PE's `out`
-//         (two-shot allreduce: written by the owner into every PE; one PE:
-//         written by the epilogue).
+//         [64c, 64c + 64) of the summed tile t are in the owner's `out`
+//         (two-shot allreduce: set by the owner on every PE, which then copies
+//         the block from the owner; one PE: set by the epilogue).
 //   This is megacu's event tensor int32 [n_pes][tiles]
 //   (backends/nvshmem/cuda_event_tensor.cuh:13-39) refined to quarter tiles
 //   (and 64-column blocks for the result) and tagged with the epoch (the
@@ -19,12 +19,12 @@
 //   consecutive calls need no memset and no host barrier; the parity plane
 //   lets a PE run one call ahead of a slow owner in reduce-scatter mode.
 //
-// workspace (symmetric when n_pes > 1): receive slots
-//   slot[p][src][j] = one tile_m x tile_n partial tile of PE `src`, j = the
-//   tile's index among the receiver's tiles (two-shot / RS) or its raster
-//   index (one-shot). Inside a slot, 16-byte vectors are stored column-major
+// workspace (symmetric when n_pes > 1): this PE's own partial tiles,
+//   slot[p][t] = the tile_m x tile_n partial of tile t (wire dtype), written
+//   by this PE's epilogue into its own memory and read over NVLink by the
+//   tile's reducers. Inside a slot, 16-byte vectors are stored column-major
 //   over rows: vector (v, row) at byte (v * tile_m + row) * 16, which is the
-//   order the TMEM epilogue produces them in (one warp store = 512 B).
+//   order the TMEM epilogue produces them in (one warp access = 512 B).
 #pragma once
 
 #include <cstdint>
@@ -49,7 +49,8 @@ struct control_block {
   std::uint32_t error_code;     // 0 = ok; non-zero = first error seen
   std::uint32_t error_info[3];  // tile, peer, site of that error
   std::uint32_t trace_count;    // trace records written
-  std::uint32_t reserved[7];
+  std::uint32_t gather_ticket;  // next gather sub-task to hand out
+  std::uint32_t reserved[6];
   unsigned long long counters[8];
 };
 static_assert(sizeof(control_block) <= kControlBytes, "control block too large");

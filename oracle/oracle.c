@@ -302,12 +302,17 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
       }
     }
     if (two_shot_ar) {
-      /* Every PE waits for every final block before its call completes. */
+      /* Gather: every PE copies each existing block of the tiles other PEs
+       * own, after acquiring the owner's final flag. */
       for (int32_t pe = 0; pe < np; ++pe) {
-        for (int32_t t = 0; t < tiles; ++t) {
+        for (int32_t r = 0; r < tiles; ++r) {
+          int32_t c[4];
+          oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
+          if (c[2] == pe) continue;
+          int32_t const t = c[0] * nt + c[1];
           for (int32_t q = 0; q < 4; ++q) {
             for (int32_t cb = 0; cb < blocks; ++cb) {
-              if (!block_exists(p, t / nt, t % nt, q, cb)) continue;
+              if (!block_exists(p, c[0], c[1], q, cb)) continue;
               if (events && events[pe][final_idx(parity, t, q, cb, np, tiles)] != epoch) rc = -3;
               cnt[pe * 8 + 5] += 1;
             }

@@ -102,13 +102,13 @@ def test_plan_sizes(m, n, k, n_pes, mode):
     ev = mb.events_bytes(prob, n_pes)
     assert ev == 256 + 4 * (2 * n_pes * pl.tiles * 4 + 2 * pl.tiles * 16)
     if n_pes == 1:
-        assert ws == 0
+        assert ws == 0 and pl.slots_per_src == 0
     else:
-        assert ws == 2 * n_pes * pl.slots_per_src * 128 * pl.tile_n * pl.wire_bytes
+        # each PE keeps its own partial of every tile, two parity planes
+        assert pl.slots_per_src == pl.tiles
+        assert ws == 2 * pl.tiles * 128 * pl.tile_n * pl.wire_bytes
         if mode == 0 and m <= 128:
             assert pl.one_shot
-    if mode == 1 or (n_pes > 1 and not pl.one_shot):
-        assert pl.slots_per_src == -(-pl.tiles // n_pes)
 
 
 def test_status_layout_matches_cpp():

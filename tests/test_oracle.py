@@ -125,6 +125,7 @@ def test_bf16_graph_counts_and_events(n_pes, mode, one_shot, m, n, tile_n):
     c = r["counters"]
     assert np.all(c[:, 0] == tiles) and np.all(c[:, 6] == 1) and np.all(c[:, 7] == 0)
     reduced = [sum(1 for t in ro if t >= 0) for ro in r["reduce_order"]]
+    reduced_tiles = [sorted(set(int(t) for t in ro if t >= 0)) for ro in r["reduce_order"]]
     if n_pes == 1:
         assert c[0, 2] == active and c[0, 1] == 0
     elif one_shot:
@@ -136,7 +137,12 @@ def test_bf16_graph_counts_and_events(n_pes, mode, one_shot, m, n, tile_n):
     assert c[:, 1].tolist() == reduced
     assert np.all(c[:, 3] == np.array(reduced) * n_pes)
     two_shot_ar = n_pes > 1 and mode == 0 and not one_shot
-    assert np.all(c[:, 5] == (len(blocks) if two_shot_ar else 0))
+    if two_shot_ar:  # gathers: the blocks of tiles some other PE owns
+        for pe in range(n_pes):
+            owned_blocks = sum(1 for t, q, cb in blocks if reduced_tiles[pe].count(t))
+            assert c[pe, 5] == len(blocks) - owned_blocks
+    else:
+        assert np.all(c[:, 5] == 0)
     # the event tensor holds the epoch exactly where the graph published
     for pe in range(n_pes):
         words = r["events"][pe]
