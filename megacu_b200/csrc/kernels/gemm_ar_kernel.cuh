@@ -135,8 +135,9 @@ __device__ __forceinline__ void trace(gemm_ar_params const &p, std::uint32_t kin
   rec[3] = ptx::now_ns();
 }
 
-// Waits until `*flag == want`, polling with a short back-off. Gives up when
-// the abort word is set or `timeout_ns` elapses.
+// Waits until `*flag == want`, polling relaxed with a short back-off and
+// finishing with one system-scope acquire load. Gives up when the abort word
+// is set or `timeout_ns` elapses.
 __device__ __forceinline__ bool wait_flag(std::uint32_t const *flag, std::uint32_t want,
                                           std::uint32_t const *abort_word,
                                           std::uint64_t timeout_ns) {
@@ -146,7 +147,7 @@ __device__ __forceinline__ bool wait_flag(std::uint32_t const *flag, std::uint32
   std::uint64_t const start = ptx::now_ns();
   for (std::uint32_t spin = 1;; ++spin) {
     __nanosleep(spin < 64 ? 32 : 256);
-    if (ptx::ld_acquire_sys(flag) == want) {
+    if (ptx::ld_relaxed_sys(flag) == want && ptx::ld_acquire_sys(flag) == want) {
       return true;
     }
     if ((spin & 15u) == 0) {
@@ -315,13 +316,13 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
     __syncwarp();
 
     if (publish_final) {
-      // The block is in this PE's out: every PE may copy it from here.
-      ptx::fence_acq_rel_sys();
+      // The block is in this PE's own out: every PE may copy it from here.
+      ptx::fence_acq_rel_gpu();
       __syncwarp();
       if (static_cast<std::int32_t>(lane) < p.n_pes) {
         std::uint32_t *flags = p.peers.translate(my_events, lane);
-        ptx::st_release_sys(flags + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles),
-                            epoch);
+        ptx::publish_local_data(flags + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles),
+                                epoch);
       }
     }
     if (lane == 0) {
@@ -658,28 +659,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       // Publish this quarter (task 0 "after" hook). The data is in this PE's
-      // own memory, so the fence only waits for local writes.
-      if (p.n_pes > 1) {
-        ptx::fence_acq_rel_sys();
-      } else {
-        __threadfence();
-      }
+      // own memory (its out, or its partial slot that reducers load over
+      // NVLink), so a GPU-scope fence suffices.
+      ptx::fence_acq_rel_gpu();
       __syncwarp();
       if (p.n_pes == 1) {
         // One PE: the tile is final as written; mark its quarter arrived and
         // its existing 64-column blocks final.
         if (lane == 0) {
-          ptx::st_release_sys(my_events + arrive_index(parity, 0, tile, quarter, 1, p.tiles), epoch);
+          ptx::publish_local_data(my_events + arrive_index(parity, 0, tile, quarter, 1, p.tiles),
+                                  epoch);
         } else if (static_cast<std::int32_t>(lane) <= cfg::col_blocks &&
                    detail::block_exists<BN>(p, c.tile_row, c.tile_col, quarter, lane - 1)) {
-          ptx::st_release_sys(
+          ptx::publish_local_data(
               my_events + final_index(parity, tile, quarter, lane - 1, 1, p.tiles), epoch);
         }
       } else if (static_cast<std::int32_t>(lane) < n_dst) {
         std::int32_t const pe = first_dst + static_cast<std::int32_t>(lane);
         std::uint32_t *flags = p.peers.translate(my_events, pe);
-        ptx::st_release_sys(flags + arrive_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles),
-                            epoch);
+        ptx::publish_local_data(
+            flags + arrive_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles), epoch);
       }
       if (lane == 0) {
         detail::count(p, ctr_partial_publish, p.n_pes == 1 ? 1 : n_dst);

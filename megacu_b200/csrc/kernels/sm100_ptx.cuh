@@ -44,12 +44,37 @@ __device__ __forceinline__ std::uint32_t ld_relaxed_gpu(std::uint32_t const *p) 
   return v;
 }
 
+__device__ __forceinline__ std::uint32_t ld_relaxed_sys(std::uint32_t const *p) {
+  std::uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_release_sys(std::uint32_t *p, std::uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ void st_relaxed_sys(std::uint32_t *p, std::uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_acq_rel_sys() {
   asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// Publishes a flag for data this thread (or its warp, after a __syncwarp)
+// wrote into THIS GPU's own memory. The GPU-scope fence makes those writes
+// visible at this GPU's L2, which is where every peer's NVLink load of that
+// memory is served; the flag itself is a relaxed system-scope store. On a
+// B200 under NVLink load a system-scope fence costs several microseconds per
+// call (it orders against all of the SM's outstanding peer traffic), this
+// costs none; readers acquire at system scope (wait_flag).
+__device__ __forceinline__ void publish_local_data(std::uint32_t *flag, std::uint32_t v) {
+  st_relaxed_sys(flag, v);
 }
 
 __device__ __forceinline__ void named_barrier_sync(std::uint32_t id, std::uint32_t threads) {
