@@ -13,10 +13,11 @@
 //      warps 2..5  epilogue: TMEM -> registers -> bf16/fp32 -> this PE's own
 //                  partial slot, then publish (task 0's "after" hook); once
 //                  the GEMM queue is drained they join the workers below
-//      warps 6..9  workers: reduce sub-tasks (task 2: acquire, PE-order fp32
-//                  sum of every PE's partial read over NVLink, store into this
-//                  PE's out), then gather sub-tasks (copy finished blocks of
-//                  tiles owned by other PEs from the owner's out)
+//      warps 6..9  workers: one raster-ordered queue of task-2 sub-tasks —
+//                  reduces (acquire, PE-order fp32 sum of every PE's partial
+//                  read over NVLink, store into this PE's out) and gathers
+//                  (copy finished blocks of tiles other PEs own from the
+//                  owner's out)
 //  * the static tile_grid dispatcher (tile = blockIdx + i * gridDim,
 //    tile_grid_device.cuh:13-23) is replaced by device task queues: an
 //    atomic ticket per queue, tickets mapped to tiles by tile_schedule.h;
@@ -77,8 +78,8 @@ struct gemm_ar_params {
   std::int32_t mode;          // mode_allreduce / mode_reduce_scatter
   std::int32_t one_shot;      // 1: every PE reduces every tile
   std::int32_t group_m;
-  std::int32_t n_reduce;      // reduce sub-tasks on this PE
-  std::int32_t n_gather;      // gather sub-tasks on this PE (two-shot allreduce)
+  std::int32_t n_comm;        // communication sub-tasks (tiles x quarters x blocks)
+  std::int32_t reserved;
   std::int32_t rows_per_pe;   // reduce-scatter: output rows per PE
   std::uint64_t timeout_ns;   // bound of cross-GPU waits
   __nv_bfloat16 *out;         // this PE's output
@@ -193,20 +194,68 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 w) {
   acc[7] += ptx::bf16_hi(w.w);
 }
 
-// Reduce worker (task 2): one warp takes sub-tasks = (reduced tile, 32-row
-// quarter, 64-column block) from the reduce queue until it is empty. For each:
-// acquire every PE's arrive flag of the quarter, load the block of every PE's
-// partial slot (its own memory for this PE, NVLink for the others), sum in PE
-// order 0..n_pes-1 in fp32 (two PEs' loads in flight at a time), round to
-// bf16, transpose 32 x 64 through `xpose` (4 KiB of shared memory) and store
-// row-major into this PE's out. Two-shot allreduce then publishes the block's
-// final flag on every PE, which copy it from here (gather_tasks).
-template <int BN, bool kWireF32>
-__device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_schedule const &sched,
+// Gather sub-task (two-shot allreduce, the second half of task 2): copy the
+// 32 x 64 block (quarter, cb) of a tile another PE owns from the owner's out
+// (NVLink loads) into this PE's out, once the owner's final flag is set.
+// Returns false if the wait gave up.
+template <int BN>
+__device__ __forceinline__ bool gather_block(gemm_ar_params const &p, tile_coord const &c,
+                                             std::int32_t tile, std::int32_t quarter,
+                                             std::int32_t cb, std::uint32_t ticket,
                                              std::uint32_t parity, std::uint32_t epoch,
                                              std::uint32_t *my_events,
-                                             std::uint32_t const *abort_word, std::uint8_t *xpose,
-                                             std::uint32_t lane) {
+                                             std::uint32_t const *abort_word, std::uint32_t lane) {
+  constexpr int kBlocks = BN / 64;
+  bool ok = true;
+  if (lane == 0) {
+    ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
+                   abort_word, p.timeout_ns);
+    if (!ok) record_error(p, err_remote_timeout, tile, c.owner, 9);
+  }
+  if (!__shfl_sync(0xffffffffu, ok, 0)) {
+    return false;
+  }
+  __syncwarp();  // orders every lane's loads after lane 0's acquire
+  std::uint64_t const t0 = ptx::now_ns();
+  std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
+  std::int32_t const col = c.tile_col * BN + cb * 64 + static_cast<std::int32_t>(lane % 8) * 8;
+  __nv_bfloat16 const *src = p.peers.translate(p.out, c.owner);
+  uint4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
+    if (row < p.m && col < p.n) v[i] = ptx::ld_cg_v4(src + static_cast<std::int64_t>(row) * p.n + col);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
+    if (row < p.m && col < p.n) ptx::st_v4(p.out + static_cast<std::int64_t>(row) * p.n + col, v[i]);
+  }
+  if (lane == 0) {
+    count(p, ctr_final_acquire, 1);
+    trace(p, 3, quarter * kBlocks + cb, ticket, tile, t0);
+  }
+  return true;
+}
+
+// Communication worker (task 2): one warp takes sub-tasks = (tile, 32-row
+// quarter, 64-column block) in raster order from one queue until it is
+// empty. A block of a tile this PE reduces (every tile in one-shot mode, the
+// owned ones otherwise) is a reduce: acquire every PE's arrive flag of the
+// quarter, load the block of every PE's partial slot (its own memory for this
+// PE, NVLink for the others), sum in PE order 0..n_pes-1 in fp32 (two PEs'
+// loads in flight at a time), round to bf16, transpose 32 x 64 through
+// `xpose` (4 KiB of shared memory) and store row-major into this PE's out;
+// two-shot allreduce then publishes the block's final flag on every PE. A
+// block of a tile another PE owns is, in two-shot allreduce, a gather
+// (gather_block); in reduce-scatter it is skipped. One raster-ordered queue
+// lets each tile's gathers follow its reduction while the GEMM still runs.
+template <int BN, bool kWireF32>
+__device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedule const &sched,
+                                           std::uint32_t parity, std::uint32_t epoch,
+                                           std::uint32_t *my_events,
+                                           std::uint32_t const *abort_word, std::uint8_t *xpose,
+                                           std::uint32_t lane) {
   constexpr int kWireBytes = kWireF32 ? 4 : 2;
   constexpr int kBlocks = BN / 64;
   constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
@@ -215,18 +264,25 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
   bool const publish_final = p.mode == mode_allreduce && !p.one_shot;
   for (;;) {
     std::uint32_t const ticket = draw_ticket(&ctrl->reduce_ticket, lane);
-    if (ticket >= static_cast<std::uint32_t>(p.n_reduce)) {
+    if (ticket >= static_cast<std::uint32_t>(p.n_comm)) {
       break;
     }
-    std::int32_t const j = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
+    std::int32_t const r = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
     std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks);
     std::int32_t const quarter = rem / kBlocks;
     std::int32_t const cb = rem % kBlocks;
-    std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
     tile_coord const c = locate(sched, r);
     std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
     if (!block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
       continue;  // no output element lives in this block
+    }
+    if (!p.one_shot && c.owner != p.my_pe) {
+      if (publish_final &&
+          !gather_block<BN>(p, c, tile, quarter, cb, ticket, parity, epoch, my_events, abort_word,
+                            lane)) {
+        break;
+      }
+      continue;
     }
 
     // Task 2 "before": every PE's partial of this quarter is ready.
@@ -330,62 +386,6 @@ __device__ __forceinline__ void reduce_tasks(gemm_ar_params const &p, tile_sched
       count(p, ctr_partial_acquire, p.n_pes);
       if (publish_final) count(p, ctr_final_publish, p.n_pes);
       trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
-    }
-  }
-}
-
-// Gather worker (two-shot allreduce, task 2's second half): copies every
-// existing 32 x 64 block of the tiles other PEs own from the owner's out
-// (NVLink loads) into this PE's out, once the owner's final flag is set.
-template <int BN>
-__device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, tile_schedule const &sched,
-                                             std::uint32_t parity, std::uint32_t epoch,
-                                             std::uint32_t *my_events,
-                                             std::uint32_t const *abort_word, std::uint32_t lane) {
-  constexpr int kBlocks = BN / 64;
-  control_block *ctrl = control(p);
-  for (;;) {
-    std::uint32_t const ticket = draw_ticket(&ctrl->gather_ticket, lane);
-    if (ticket >= static_cast<std::uint32_t>(p.n_gather)) {
-      break;
-    }
-    std::int32_t const r = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
-    std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks);
-    std::int32_t const quarter = rem / kBlocks;
-    std::int32_t const cb = rem % kBlocks;
-    tile_coord const c = locate(sched, r);
-    if (c.owner == p.my_pe || !block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
-      continue;
-    }
-    std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
-    bool ok = true;
-    if (lane == 0) {
-      ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
-                     abort_word, p.timeout_ns);
-      if (!ok) record_error(p, err_remote_timeout, tile, c.owner, 9);
-    }
-    if (!__shfl_sync(0xffffffffu, ok, 0)) {
-      break;
-    }
-    __syncwarp();  // orders every lane's loads after lane 0's acquire
-    std::uint64_t const t0 = ptx::now_ns();
-    std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
-    std::int32_t const col = c.tile_col * BN + cb * 64 + static_cast<std::int32_t>(lane % 8) * 8;
-    __nv_bfloat16 const *src = p.peers.translate(p.out, c.owner);
-    uint4 v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
-      if (row < p.m && col < p.n) v[i] = ptx::ld_cg_v4(src + static_cast<std::int64_t>(row) * p.n + col);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
-      if (row < p.m && col < p.n) ptx::st_v4(p.out + static_cast<std::int64_t>(row) * p.n + col, v[i]);
-    }
-    if (lane == 0) {
-      count(p, ctr_final_acquire, 1);
-      trace(p, 3, quarter * kBlocks + cb, ticket, tile, t0);
     }
   }
 }
@@ -686,14 +686,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---------------- workers: reduce, then gather (task 2) ----------------
+  // ---------------- workers: reduce and gather (task 2) ----------------
   // Worker warps start at once; epilogue warps join once the GEMM queue is
   // drained, so the last GEMM wave's reductions use both groups.
   if (p.n_pes > 1 && warp >= kEpilogueWarp0) {
     int const worker = warp - kEpilogueWarp0;  // 0..7
     std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
-    detail::reduce_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
-    detail::gather_tasks<BN>(p, sched, parity, epoch, my_events, abort_word, lane);
+    detail::comm_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
   }
 
   // ---------------- teardown ----------------

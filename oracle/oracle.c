@@ -255,17 +255,17 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
     int64_t const rows_per_pe = m / np;
     int32_t const per_tile = 4 * blocks;
     for (int32_t me = 0; me < np && rc == 0; ++me) {
-      int32_t owned = p->one_shot ? tiles : (tiles > me ? (tiles - me + np - 1) / np : 0);
-      /* Task 2 sub-tasks: (owned tile, 32-row quarter, 64-column block). */
-      for (int32_t ticket = 0; ticket < owned * per_tile && rc == 0; ++ticket) {
-        int32_t const j = ticket / per_tile;
+      /* Task 2 queue: every (tile, 32-row quarter, 64-column block) in raster
+       * order; this PE reduces the blocks of the tiles it owns (all of them in
+       * one-shot mode); the others are gathers (two-shot) or skipped (RS). */
+      for (int32_t ticket = 0; ticket < tiles * per_tile && rc == 0; ++ticket) {
+        int32_t const r = ticket / per_tile;
         int32_t const q = (ticket % per_tile) / blocks;
         int32_t const cb = ticket % blocks;
-        int32_t const r = p->one_shot ? j : j * np + me;
         int32_t c[4];
         oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
         int32_t const t = c[0] * nt + c[1];
-        if (!block_exists(p, c[0], c[1], q, cb)) {
+        if (!block_exists(p, c[0], c[1], q, cb) || (!p->one_shot && c[2] != me)) {
           if (reduce_order) reduce_order[me][ticket] = -1;
           continue;
         }

@@ -83,8 +83,9 @@ typedef struct oracle_bf16_problem {
  * (optional) receive the per-call deltas of the device counters. gemm_order
  * (optional, [tiles]) receives the tile id of each GEMM ticket;
  * reduce_order[pe] (optional, [tiles * 4 * tile_n / 64]) the tile id of each
- * reduce ticket (owned tile, 32-row quarter, 64-column block) of PE pe, or -1
- * where the ticket is skipped (a block that holds no output element).
+ * communication ticket (raster tile, 32-row quarter, 64-column block) that PE
+ * pe reduces, or -1 where the ticket is a gather, skipped, or holds no
+ * output element.
  * Returns 0, or a negative number if the graph was inconsistent (an acquire
  * found a flag unset).
  */
