@@ -207,7 +207,9 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
   } else if (p.algo == MEGACU_ALGO_TWO_SHOT) {
     pl.one_shot = 0;
   } else {
-    pl.one_shot = pl.m_tiles == 1 ? 1 : 0;  // latency-bound shapes: one hop
+    // One hop for latency-bound shapes (one tile row) and for two PEs, where
+    // one-shot moves the same NVLink bytes as two-shot without the gather.
+    pl.one_shot = (pl.m_tiles == 1 || n_pes == 2) ? 1 : 0;
   }
   pl.wire_bytes = p.deterministic ? 4 : 2;
   // Each PE keeps its own partial of every tile (two parity planes); the
