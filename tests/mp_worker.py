@@ -22,7 +22,7 @@ sys.path.insert(0, HERE)
 
 import megacu_b200 as mb  # noqa: E402
 import oracle_lib  # noqa: E402
-from gpu_util import REL_TOL, f32, inputs, rel_error  # noqa: E402
+from gpu_util import REL_TOL, f32, inputs, rel_error, wire_scale  # noqa: E402
 
 CASES = [
     # m, n, k, mode, algo, deterministic
@@ -66,7 +66,10 @@ def main() -> int:
         ref2 = oracle_lib.bf16_call([f32(x) for x in a], [f32(x) for x in b], m=m, n=n, k=k,
                                     tile_n=pl.tile_n, mode=mode, one_shot=pl.one_shot,
                                     wire_bytes=pl.wire_bytes, epoch=2, events=ref["events"])
-        err = rel_error(f32(out), ref["out"][rank])
+        rows = (slice(rank * (m // world), (rank + 1) * (m // world))
+                if mode == mb.MODE_REDUCE_SCATTER else None)
+        scale = None if det else wire_scale(a, b, rows)
+        err = rel_error(f32(out), ref["out"][rank], scale)
         if not err < REL_TOL:
             failures.append(f"case {idx}: rel error {err}")
         words = ev[64:].cpu().numpy().view(np.uint32)
