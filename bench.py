@@ -253,15 +253,13 @@ def run_gpu(args, rank, world, local_rank):
         return float(total.item()) / steps, ms
 
     # ---- fused megakernel, inputs resident ----
-    # The clock sampler runs from the warm-up through the timed steps; an
-    # untimed half-second of calls first gives nvidia-smi time to sample the
-    # GPU under this load.
+    # The clock sampler runs from the warm-up through the timed steps; a fixed
+    # number of untimed calls first (the same on every rank: each call is a
+    # collective) gives nvidia-smi time to sample the GPU under this load.
     with ClockSampler(local_rank) as clocks:
-        t_end = time.time() + 0.5
-        while time.time() < t_end:
-            for _ in range(20):
-                call(a, b)
-            torch.cuda.synchronize()
+        for _ in range(args.heat_calls):
+            call(a, b)
+        torch.cuda.synchronize()
         ms_fused, _ = timed_steps(lambda: call(a, b), args.steps, args.warmup)
     mb.events_status(events, stream)
     flops_total = 2.0 * M * N * K_TOTAL
@@ -341,6 +339,8 @@ def main():
     ap.add_argument("--impl", default="megacu_b200", choices=["megacu_b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--heat-calls", type=int, default=1500,
+                    help="untimed calls before the warm-up, while clocks are sampled")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
