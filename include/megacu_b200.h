@@ -190,7 +190,7 @@ megacu_status megacu_cuda_gemm_allreduce_f32_orchestrate(
  * passes a, b and out; the scratch (task-queue control block and event
  * tensor) lives in a 256 KiB array built into the library, one per GPU, held
  * until the process exits. Limits: team_n_pes must be 1 (unsupported/51);
- * at most 1636 output tiles (invalid_argument/52). Every call on a GPU shares
+ * at most 8183 output tiles (invalid_argument/52). Every call on a GPU shares
  * that array, so calls that overlap on the GPU race — issue them in stream
  * order. The first call on a device looks up the array's address with that
  * device current; make it before any stream capture.

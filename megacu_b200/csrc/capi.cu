@@ -304,10 +304,13 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   prm.mode = problem.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter : mode_allreduce;
   prm.one_shot = pl.one_shot;
   prm.group_m = pl.group_m;
-  // One communication queue over every (tile, quarter, 64-column block) in
-  // raster order: reduces of the tiles this PE reduces, gathers of the others
-  // (two-shot allreduce).
-  prm.n_comm = n_pes == 1 ? 0 : pl.tiles * kQuarters * (pl.tile_n / 64);
+  // The reduce queue: every (reduced tile, quarter, 64-column block), the
+  // reduced tiles being this PE's own (two-shot, reduce-scatter) or all
+  // tiles (one-shot), in raster order.
+  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, prm.mode, pl.group_m};
+  std::int32_t const reduced_tiles =
+      n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
+  prm.n_comm = reduced_tiles * kQuarters * (pl.tile_n / 64);
   prm.rows_per_pe = static_cast<std::int32_t>(problem.m / n_pes);
   prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
   prm.out = static_cast<__nv_bfloat16 *>(out);

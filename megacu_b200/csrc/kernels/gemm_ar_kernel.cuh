@@ -194,62 +194,18 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 w) {
   acc[7] += ptx::bf16_hi(w.w);
 }
 
-// Gather sub-task (two-shot allreduce, the second half of task 2): copy the
-// 32 x 64 block (quarter, cb) of a tile another PE owns from the owner's out
-// (NVLink loads) into this PE's out, once the owner's final flag is set.
-// Returns false if the wait gave up.
-template <int BN>
-__device__ __forceinline__ bool gather_block(gemm_ar_params const &p, tile_coord const &c,
-                                             std::int32_t tile, std::int32_t quarter,
-                                             std::int32_t cb, std::uint32_t ticket,
-                                             std::uint32_t parity, std::uint32_t epoch,
-                                             std::uint32_t *my_events,
-                                             std::uint32_t const *abort_word, std::uint32_t lane) {
-  constexpr int kBlocks = BN / 64;
-  bool ok = true;
-  if (lane == 0) {
-    ok = wait_flag(my_events + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles), epoch,
-                   abort_word, p.timeout_ns);
-    if (!ok) record_error(p, err_remote_timeout, tile, c.owner, 9);
-  }
-  if (!__shfl_sync(0xffffffffu, ok, 0)) {
-    return false;
-  }
-  __syncwarp();  // orders every lane's loads after lane 0's acquire
-  std::uint64_t const t0 = ptx::now_ns();
-  std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
-  std::int32_t const col = c.tile_col * BN + cb * 64 + static_cast<std::int32_t>(lane % 8) * 8;
-  __nv_bfloat16 const *src = p.peers.translate(p.out, c.owner);
-  uint4 v[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
-    if (row < p.m && col < p.n) v[i] = ptx::ld_cg_v4(src + static_cast<std::int64_t>(row) * p.n + col);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    std::int32_t const row = row0 + i * 4 + static_cast<std::int32_t>(lane) / 8;
-    if (row < p.m && col < p.n) ptx::st_v4(p.out + static_cast<std::int64_t>(row) * p.n + col, v[i]);
-  }
-  if (lane == 0) {
-    count(p, ctr_final_acquire, 1);
-    trace(p, 3, quarter * kBlocks + cb, ticket, tile, t0);
-  }
-  return true;
-}
-
-// Communication worker (task 2): one warp takes sub-tasks = (tile, 32-row
-// quarter, 64-column block) in raster order from one queue until it is
-// empty. A block of a tile this PE reduces (every tile in one-shot mode, the
-// owned ones otherwise) is a reduce: acquire every PE's arrive flag of the
-// quarter, load the block of every PE's partial slot (its own memory for this
-// PE, NVLink for the others), sum in PE order 0..n_pes-1 in fp32 (two PEs'
-// loads in flight at a time), round to bf16, transpose 32 x 64 through
-// `xpose` (4 KiB of shared memory) and store row-major into this PE's out;
-// two-shot allreduce then publishes the block's final flag on every PE. A
-// block of a tile another PE owns is, in two-shot allreduce, a gather
-// (gather_block); in reduce-scatter it is skipped. One raster-ordered queue
-// lets each tile's gathers follow its reduction while the GEMM still runs.
+// Communication worker (task 2): one warp takes sub-tasks = (reduced tile,
+// 32-row quarter, 64-column block) in raster order from the reduce queue
+// until it is empty; the reduced tiles are this PE's own (two-shot allreduce,
+// reduce-scatter) or all of them (one-shot). For each: acquire every PE's
+// arrive flag of the quarter, load the block of every PE's partial slot (its
+// own memory for this PE, NVLink for the others), sum in PE order
+// 0..n_pes-1 in fp32 (two PEs' loads in flight at a time), round to bf16,
+// transpose 32 x 64 through `xpose` (4 KiB of shared memory) and store it
+// row-major into this PE's out — in two-shot allreduce into every PE's out.
+// Those stores are not flagged one by one: when the queue is empty the warp
+// fences once, and the last worker of this PE announces "all my blocks are
+// written" to every PE (finish_pushes).
 template <int BN, bool kWireF32>
 __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedule const &sched,
                                            std::uint32_t parity, std::uint32_t epoch,
@@ -261,28 +217,21 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
   constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
   constexpr std::int64_t kVecStride = kBlockM * 16;  // bytes between wire vectors of a row
   control_block *ctrl = control(p);
-  bool const publish_final = p.mode == mode_allreduce && !p.one_shot;
+  bool const push_all = p.mode == mode_allreduce && !p.one_shot;
   for (;;) {
     std::uint32_t const ticket = draw_ticket(&ctrl->reduce_ticket, lane);
     if (ticket >= static_cast<std::uint32_t>(p.n_comm)) {
       break;
     }
-    std::int32_t const r = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
+    std::int32_t const j = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks);
     std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks);
     std::int32_t const quarter = rem / kBlocks;
     std::int32_t const cb = rem % kBlocks;
+    std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
     tile_coord const c = locate(sched, r);
     std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
     if (!block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
       continue;  // no output element lives in this block
-    }
-    if (!p.one_shot && c.owner != p.my_pe) {
-      if (publish_final &&
-          !gather_block<BN>(p, c, tile, quarter, cb, ticket, parity, epoch, my_events, abort_word,
-                            lane)) {
-        break;
-      }
-      continue;
     }
 
     // Task 2 "before": every PE's partial of this quarter is ready.
@@ -361,33 +310,71 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
         p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
     std::int32_t const g = lane % 8;
     std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
+    // Every PE's out in two-shot allreduce (starting with the next PE, so the
+    // PEs spread their stores over the links), this PE's out otherwise.
+    std::int32_t const n_out = push_all ? p.n_pes : 1;
+    for (std::int32_t d = 0; d < n_out; ++d) {
+      std::int32_t const pe = push_all ? (p.my_pe + 1 + d) % p.n_pes : p.my_pe;
+      __nv_bfloat16 *dst = push_all ? p.peers.translate(p.out, pe) : p.out;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
-      uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
-      if (row0 + rr < p.m && col < p.n) {
-        ptx::st_v4(p.out + static_cast<std::int64_t>(out_row0 + rr) * p.n + col, q);
+      for (int i = 0; i < 8; ++i) {
+        std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
+        uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
+        if (row0 + rr < p.m && col < p.n) {
+          ptx::st_v4(dst + static_cast<std::int64_t>(out_row0 + rr) * p.n + col, q);
+        }
       }
     }
     __syncwarp();
-
-    if (publish_final) {
-      // The block is in this PE's own out: every PE may copy it from here.
-      ptx::fence_acq_rel_gpu();
-      __syncwarp();
-      if (static_cast<std::int32_t>(lane) < p.n_pes) {
-        std::uint32_t *flags = p.peers.translate(my_events, lane);
-        ptx::publish_local_data(flags + final_index(parity, tile, quarter, cb, p.n_pes, p.tiles),
-                                epoch);
-      }
-    }
     if (lane == 0) {
       count(p, ctr_reduce_tasks, 1);
       count(p, ctr_partial_acquire, p.n_pes);
-      if (publish_final) count(p, ctr_final_publish, p.n_pes);
+      if (push_all) count(p, ctr_final_publish, p.n_pes);
       trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
     }
   }
+}
+
+// Two-shot allreduce completion. Each worker warp, once the reduce queue is
+// empty, fences its stores at system scope (they went to every PE's out) and
+// counts itself done; the last worker of this PE then sets done[p][my_pe] on
+// every PE. One system-scope fence per warp per call instead of one per block.
+__device__ __forceinline__ void finish_pushes(gemm_ar_params const &p, std::uint32_t parity,
+                                              std::uint32_t epoch, std::uint32_t *my_events,
+                                              std::uint32_t lane) {
+  control_block *ctrl = control(p);
+  ptx::fence_acq_rel_sys();
+  __syncwarp();
+  std::uint32_t last = 0;
+  if (lane == 0) {
+    std::uint32_t const total = gridDim.x * kWorkerWarps;
+    last = atomicAdd(&ctrl->workers_done, 1u) == total - 1 ? 1u : 0u;
+  }
+  if (__shfl_sync(0xffffffffu, last, 0) == 0) {
+    return;
+  }
+  ptx::fence_acq_rel_sys();
+  if (static_cast<std::int32_t>(lane) < p.n_pes) {
+    std::uint32_t *flags = p.peers.translate(my_events, lane);
+    ptx::st_relaxed_sys(flags + done_index(parity, p.my_pe, p.n_pes, p.tiles), epoch);
+  }
+}
+
+// Two-shot allreduce: this PE's out is complete once every PE has announced
+// that all of its blocks are written (one waiter per PE suffices: the launch
+// ends only when this warp does).
+__device__ __forceinline__ void wait_all_pushes(gemm_ar_params const &p, std::uint32_t parity,
+                                                std::uint32_t epoch, std::uint32_t *my_events,
+                                                std::uint32_t const *abort_word,
+                                                std::uint32_t lane) {
+  bool ok = true;
+  if (static_cast<std::int32_t>(lane) < p.n_pes) {
+    ok = wait_flag(my_events + done_index(parity, lane, p.n_pes, p.tiles), epoch, abort_word,
+                   p.timeout_ns);
+    if (!ok) record_error(p, err_remote_timeout, 0xffffffffu, lane, 9);
+  }
+  bool const all = __all_sync(0xffffffffu, ok);
+  if (lane == 0 && all) count(p, ctr_final_acquire, p.n_pes);
 }
 
 }  // namespace detail
@@ -664,15 +651,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::fence_acq_rel_gpu();
       __syncwarp();
       if (p.n_pes == 1) {
-        // One PE: the tile is final as written; mark its quarter arrived and
-        // its existing 64-column blocks final.
+        // One PE: the tile is final as written; mark its quarter arrived.
         if (lane == 0) {
           ptx::publish_local_data(my_events + arrive_index(parity, 0, tile, quarter, 1, p.tiles),
                                   epoch);
-        } else if (static_cast<std::int32_t>(lane) <= cfg::col_blocks &&
-                   detail::block_exists<BN>(p, c.tile_row, c.tile_col, quarter, lane - 1)) {
-          ptx::publish_local_data(
-              my_events + final_index(parity, tile, quarter, lane - 1, 1, p.tiles), epoch);
         }
       } else if (static_cast<std::int32_t>(lane) < n_dst) {
         std::int32_t const pe = first_dst + static_cast<std::int32_t>(lane);
@@ -686,13 +668,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---------------- workers: reduce and gather (task 2) ----------------
+  // ---------------- workers: reduce (task 2) ----------------
   // Worker warps start at once; epilogue warps join once the GEMM queue is
   // drained, so the last GEMM wave's reductions use both groups.
   if (p.n_pes > 1 && warp >= kEpilogueWarp0) {
     int const worker = warp - kEpilogueWarp0;  // 0..7
     std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
     detail::comm_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
+    if (p.mode == mode_allreduce && !p.one_shot) {
+      detail::finish_pushes(p, parity, epoch, my_events, lane);
+      if (blockIdx.x == 0 && worker == 0) {
+        detail::wait_all_pushes(p, parity, epoch, my_events, abort_word, lane);
+      }
+    }
   }
 
   // ---------------- teardown ----------------
@@ -711,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __threadfence();
       ctrl->gemm_ticket = 0;
       ctrl->reduce_ticket = 0;
-      ctrl->gather_ticket = 0;
+      ctrl->workers_done = 0;
       ctrl->trace_count = 0;
       ctrl->launch_count = epoch;
       atomicAdd(&ctrl->counters[ctr_launches], 1ull);

@@ -8,16 +8,15 @@
 //   then the event tensor, two regions of uint32 flags:
 //     arrive[p][src][t][q]  (p < 2, src < n_pes, q < 4) = epoch once PE `src`
 //         has delivered rows [32q, 32q + 32) of its partial of tile t;
-//     final[p][t][q][c]     (c < 4) = epoch once rows [32q, 32q + 32) x columns
-//         [64c, 64c + 64) of the summed tile t are in the owner's `out`
-//         (two-shot allreduce: set by the owner on every PE, which then copies
-//         the block from the owner; one PE: set by the epilogue).
+//     done[p][src]          (src < n_pes) = epoch once PE `src` has written
+//         every block it reduced into this PE's `out` (two-shot allreduce,
+//         where each owner stores its summed tiles into every PE's out).
 //   This is megacu's event tensor int32 [n_pes][tiles]
 //   (backends/nvshmem/cuda_event_tensor.cuh:13-39) refined to quarter tiles
-//   (and 64-column blocks for the result) and tagged with the epoch (the
-//   golden's ready_base idiom, golden_gemm_allreduce.cu:384-385), so
-//   consecutive calls need no memset and no host barrier; the parity plane
-//   lets a PE run one call ahead of a slow owner in reduce-scatter mode.
+//   and tagged with the epoch (the golden's ready_base idiom,
+//   golden_gemm_allreduce.cu:384-385), so consecutive calls need no memset
+//   and no host barrier; the parity plane lets a PE run one call ahead of a
+//   slow owner in reduce-scatter mode.
 //
 // workspace (symmetric when n_pes > 1): this PE's own partial tiles,
 //   slot[p][t] = the tile_m x tile_n partial of tile t (wire dtype), written
@@ -49,7 +48,7 @@ struct control_block {
   std::uint32_t error_code;     // 0 = ok; non-zero = first error seen
   std::uint32_t error_info[3];  // tile, peer, site of that error
   std::uint32_t trace_count;    // trace records written
-  std::uint32_t gather_ticket;  // next gather sub-task to hand out
+  std::uint32_t workers_done;   // reduce workers finished in this launch
   std::uint32_t reserved[6];
   unsigned long long counters[8];
 };
@@ -79,19 +78,16 @@ MEGACU_B200_LAYOUT_HD inline std::int64_t arrive_index(std::int32_t parity, std:
   return ((static_cast<std::int64_t>(parity) * n_pes + src) * tiles + tile) * kQuarters + quarter;
 }
 
-// Word index (after the control block) of final[p][t][q][c].
-MEGACU_B200_LAYOUT_HD inline std::int64_t final_index(std::int32_t parity, std::int32_t tile,
-                                                    std::int32_t quarter, std::int32_t block,
-                                                    std::int32_t n_pes, std::int32_t tiles) {
-  std::int64_t const arrive_words = static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters;
-  return arrive_words +
-         ((static_cast<std::int64_t>(parity) * tiles + tile) * kQuarters + quarter) * kColBlocks +
-         block;
+// Word index (after the control block) of done[p][src].
+MEGACU_B200_LAYOUT_HD inline std::int64_t done_index(std::int32_t parity, std::int32_t src,
+                                                   std::int32_t n_pes, std::int32_t tiles) {
+  return static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters +
+         static_cast<std::int64_t>(parity) * n_pes + src;
 }
 
 inline std::int64_t events_bytes_for(std::int32_t n_pes, std::int32_t tiles) {
   std::int64_t const words = static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters +
-                             static_cast<std::int64_t>(2) * tiles * kQuarters * kColBlocks;
+                             static_cast<std::int64_t>(2) * n_pes;
   return kControlBytes + 4 * words;
 }
 

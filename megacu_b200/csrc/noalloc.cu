@@ -13,7 +13,7 @@
 // Limits and sharing rules:
 //  * scratch is `kNoAllocScratchBytes` (256 KiB) per GPU, held by every GPU
 //    that loads the library until the process exits; problems whose tile
-//    grid needs more (more than 1636 output tiles) are rejected;
+//    grid needs more (more than 8183 output tiles) are rejected;
 //  * every call on a GPU shares that one array: calls that overlap on the
 //    GPU (on different streams, or from different threads) race and must
 //    not be issued; calls in stream order are fine;
@@ -135,7 +135,7 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
   if (events_bytes_for(1, static_cast<std::int32_t>(tiles)) > kNoAllocScratchBytes) {
     return na_fail(MEGACU_INVALID_ARGUMENT, 52,
                    "problem too large for the allocation-free entry: its tile grid needs more "
-                   "than the 256 KiB of built-in scratch (at most 1636 output tiles)");
+                   "than the 256 KiB of built-in scratch (at most 8183 output tiles)");
   }
   if (driver.launch.stream == nullptr) {
     return na_ok();

@@ -170,16 +170,14 @@ void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode
 }
 
 /* Event tensor words after the control block (restates layout.h):
- * arrive[p][src][t][q] then final[p][t][q][c], q < 4 quarters, c < 4 blocks. */
+ * arrive[p][src][t][q] (q < 4 quarters), then done[p][src]. */
 static int64_t arrive_idx(int32_t parity, int32_t src, int32_t tile, int32_t quarter,
                           int32_t n_pes, int32_t tiles) {
   return (((int64_t)parity * n_pes + src) * tiles + tile) * 4 + quarter;
 }
 
-static int64_t final_idx(int32_t parity, int32_t tile, int32_t quarter, int32_t block,
-                         int32_t n_pes, int32_t tiles) {
-  return (int64_t)2 * n_pes * tiles * 4 + (((int64_t)parity * tiles + tile) * 4 + quarter) * 4 +
-         block;
+static int64_t done_idx(int32_t parity, int32_t src, int32_t n_pes, int32_t tiles) {
+  return (int64_t)2 * n_pes * tiles * 4 + (int64_t)parity * n_pes + src;
 }
 
 /* Does quarter q x 64-column block c of tile (row, col) hold an output element? */
@@ -227,15 +225,8 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
       for (int32_t q = 0; q < 4; ++q) {
         if ((int64_t)c[0] * p->tile_m + q * 32 >= m) continue;
         if (np == 1) {
-          /* One PE: the quarter is arrived and its existing blocks final. */
-          if (events) {
-            events[0][arrive_idx(parity, 0, t, q, 1, tiles)] = epoch;
-            for (int32_t cb = 0; cb < blocks; ++cb) {
-              if (block_exists(p, c[0], c[1], q, cb)) {
-                events[0][final_idx(parity, t, q, cb, 1, tiles)] = epoch;
-              }
-            }
-          }
+          /* One PE: the quarter is arrived (the tile is final as written). */
+          if (events) events[0][arrive_idx(parity, 0, t, q, 1, tiles)] = epoch;
           cnt[pe * 8 + 2] += 1;
         } else {
           int32_t const first = p->one_shot ? 0 : c[2];
@@ -255,17 +246,19 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
     int64_t const rows_per_pe = m / np;
     int32_t const per_tile = 4 * blocks;
     for (int32_t me = 0; me < np && rc == 0; ++me) {
-      /* Task 2 queue: every (tile, 32-row quarter, 64-column block) in raster
-       * order; this PE reduces the blocks of the tiles it owns (all of them in
-       * one-shot mode); the others are gathers (two-shot) or skipped (RS). */
-      for (int32_t ticket = 0; ticket < tiles * per_tile && rc == 0; ++ticket) {
-        int32_t const r = ticket / per_tile;
+      /* Task 2 queue: every (reduced tile, 32-row quarter, 64-column block),
+       * the reduced tiles being this PE's own (two-shot, reduce-scatter) or
+       * all of them (one-shot), in raster order. */
+      int32_t const reduced = p->one_shot ? tiles : (tiles > me ? (tiles - me + np - 1) / np : 0);
+      for (int32_t ticket = 0; ticket < reduced * per_tile && rc == 0; ++ticket) {
+        int32_t const j = ticket / per_tile;
         int32_t const q = (ticket % per_tile) / blocks;
         int32_t const cb = ticket % blocks;
+        int32_t const r = p->one_shot ? j : j * np + me;
         int32_t c[4];
         oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
         int32_t const t = c[0] * nt + c[1];
-        if (!block_exists(p, c[0], c[1], q, cb) || (!p->one_shot && c[2] != me)) {
+        if (!block_exists(p, c[0], c[1], q, cb)) {
           if (reduce_order) reduce_order[me][ticket] = -1;
           continue;
         }
@@ -289,35 +282,25 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
             } else if (p->one_shot) {
               out[me][row * n + col] = s;
             } else {
-              for (int32_t pe = 0; pe < np; ++pe) out[pe][row * n + col] = s;
+              for (int32_t pe = 0; pe < np; ++pe) out[pe][row * n + col] = s; /* into every out */
             }
           }
         }
-        if (two_shot_ar) {
-          for (int32_t pe = 0; pe < np; ++pe) {
-            if (events) events[pe][final_idx(parity, t, q, cb, np, tiles)] = epoch;
-          }
-          cnt[me * 8 + 4] += (uint64_t)np;
-        }
+        if (two_shot_ar) cnt[me * 8 + 4] += (uint64_t)np;
+      }
+      /* Two-shot completion: PE me announces on every PE that all of its
+       * blocks are written. */
+      if (two_shot_ar && events) {
+        for (int32_t pe = 0; pe < np; ++pe) events[pe][done_idx(parity, me, np, tiles)] = epoch;
       }
     }
     if (two_shot_ar) {
-      /* Gather: every PE copies each existing block of the tiles other PEs
-       * own, after acquiring the owner's final flag. */
+      /* Every PE's call completes once every PE's done flag is set. */
       for (int32_t pe = 0; pe < np; ++pe) {
-        for (int32_t r = 0; r < tiles; ++r) {
-          int32_t c[4];
-          oracle_locate(mt, nt, np, p->mode, p->group_m, r, c);
-          if (c[2] == pe) continue;
-          int32_t const t = c[0] * nt + c[1];
-          for (int32_t q = 0; q < 4; ++q) {
-            for (int32_t cb = 0; cb < blocks; ++cb) {
-              if (!block_exists(p, c[0], c[1], q, cb)) continue;
-              if (events && events[pe][final_idx(parity, t, q, cb, np, tiles)] != epoch) rc = -3;
-              cnt[pe * 8 + 5] += 1;
-            }
-          }
+        for (int32_t src = 0; src < np; ++src) {
+          if (events && events[pe][done_idx(parity, src, np, tiles)] != epoch) rc = -3;
         }
+        cnt[pe * 8 + 5] += (uint64_t)np;
       }
     }
   }

@@ -78,14 +78,13 @@ typedef struct oracle_bf16_problem {
  * a[pe], b[pe]: bf16 values held in fp32. out[pe]: fp32 result, [m, n] for
  * allreduce, [m / n_pes, n] for reduce-scatter (not rounded to bf16).
  * events[pe] (optional): the event tensor words after the control block —
- * arrive uint32 [2][n_pes][tiles][4] then final uint32 [2][tiles][4][4] —
- * updated in place exactly as the device does. counters[pe * 8 + i]
+ * arrive uint32 [2][n_pes][tiles][4] then done uint32 [2][n_pes] — updated in
+ * place exactly as the device does. counters[pe * 8 + i]
  * (optional) receive the per-call deltas of the device counters. gemm_order
  * (optional, [tiles]) receives the tile id of each GEMM ticket;
  * reduce_order[pe] (optional, [tiles * 4 * tile_n / 64]) the tile id of each
- * communication ticket (raster tile, 32-row quarter, 64-column block) that PE
- * pe reduces, or -1 where the ticket is a gather, skipped, or holds no
- * output element.
+ * reduce ticket (reduced tile in raster order, 32-row quarter, 64-column
+ * block) of PE pe, or -1 where the block holds no output element.
  * Returns 0, or a negative number if the graph was inconsistent (an acquire
  * found a flag unset).
  */

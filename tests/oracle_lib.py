@@ -159,5 +159,5 @@ def bf16_tiles(a_list, b_list, tile_ids, *, m, n, k, tile_n, wire_bytes=2, threa
 
 def event_tensor_words(n_pes: int, tiles: int) -> int:
     """uint32 words of the event tensor after the control block
-    (arrive [2][n_pes][tiles][4], then final [2][tiles][4][4])."""
-    return 2 * n_pes * tiles * 4 + 2 * tiles * 16
+    (arrive [2][n_pes][tiles][4], then done [2][n_pes])."""
+    return 2 * n_pes * tiles * 4 + 2 * n_pes

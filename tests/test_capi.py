@@ -100,7 +100,7 @@ def test_plan_sizes(m, n, k, n_pes, mode):
     assert pl.m_tiles == -(-m // 128) and pl.n_tiles == -(-n // pl.tile_n)
     ws = mb.workspace_bytes(prob, n_pes)
     ev = mb.events_bytes(prob, n_pes)
-    assert ev == 256 + 4 * (2 * n_pes * pl.tiles * 4 + 2 * pl.tiles * 16)
+    assert ev == 256 + 4 * (2 * n_pes * pl.tiles * 4 + 2 * n_pes)
     if n_pes == 1:
         assert ws == 0 and pl.slots_per_src == 0
     else:

@@ -137,23 +137,22 @@ def test_bf16_graph_counts_and_events(n_pes, mode, one_shot, m, n, tile_n):
     assert c[:, 1].tolist() == reduced
     assert np.all(c[:, 3] == np.array(reduced) * n_pes)
     two_shot_ar = n_pes > 1 and mode == 0 and not one_shot
-    if two_shot_ar:  # gathers: the blocks of tiles some other PE owns
-        for pe in range(n_pes):
-            owned_blocks = sum(1 for t, q, cb in blocks if reduced_tiles[pe].count(t))
-            assert c[pe, 5] == len(blocks) - owned_blocks
-    else:
-        assert np.all(c[:, 5] == 0)
+    # two-shot: each PE acquires every PE's "all my blocks are written" flag
+    assert np.all(c[:, 5] == (n_pes if two_shot_ar else 0))
+    assert np.all(c[:, 4] == (np.array(reduced) * n_pes if two_shot_ar else 0))
     # the event tensor holds the epoch exactly where the graph published
     for pe in range(n_pes):
         words = r["events"][pe]
         arrive = words[:2 * n_pes * tiles * 4].reshape(2, n_pes, tiles, 4)
-        final = words[2 * n_pes * tiles * 4:].reshape(2, tiles, 4, 4)
-        assert np.all(arrive[0] == 0) and np.all(final[0] == 0)  # epoch 5: parity plane 1
+        done = words[2 * n_pes * tiles * 4:].reshape(2, n_pes)
+        assert np.all(arrive[0] == 0) and np.all(done[0] == 0)  # epoch 5: parity plane 1
         assert set(np.unique(arrive[1]).tolist()) <= {0, 5}
-        if n_pes == 1 or two_shot_ar:
-            assert int((final[1] == 5).sum()) == len(blocks)
-        else:
-            assert np.all(final[1] == 0)
+        assert np.all(done[1] == (5 if two_shot_ar else 0))
+        # every reduced tile's active quarters arrived from every PE
+        for t in reduced_tiles[pe]:
+            for q in range(4):
+                if (t // n_tiles) * 128 + q * 32 < m:
+                    assert np.all(arrive[1, :, t, q] == 5)
 
 
 def test_locate_matches_product_schedule():

@@ -29,7 +29,7 @@ def test_noalloc_rejects_what_it_cannot_hold():
     ok = lib.megacu_cuda_gemm_bf16_noalloc(d, fake, fake, fake, mb.Problem(512, 1024, 256).to_c())
     assert (ok.code, ok.detail) == (0, 0)  # null stream: validate only
     big = lib.megacu_cuda_gemm_bf16_noalloc(d, fake, fake, fake,
-                                            mb.Problem(8192, 16384, 64).to_c())
+                                            mb.Problem(16384, 65536, 64).to_c())
     assert (big.code, big.detail) == (1, 52) and b"256 KiB" in big.message
     d2 = mb.driver_view(None, 0)
     d2.team.team_n_pes = 2
