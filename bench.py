@@ -41,6 +41,7 @@ METRIC = "GEMM+allreduce TFLOP/s (whole job), C2 M4096 N8192 K8192 split over tp
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_TFLOPS = 1590.0
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
 
 
 def env_int(name, default):
@@ -299,6 +300,14 @@ def run_gpu(args, rank, world, local_rank):
 
     peak, peak_src = peaks()
     achieved = flops_rank / (ms_fused * 1e-3) / 1e12
+    # North-star roofline: the slower of the GEMM at the measured peak and the
+    # bytes each PE must send over NVLink (two-shot: 2 (tp-1)/tp of the bf16
+    # output) at the measured 770 GB/s per direction.
+    out_bytes = M * N * 2
+    link_bytes = 2.0 * (tp - 1) / tp * out_bytes
+    t_gemm_us = flops_rank / (peak * 1e12) * 1e6
+    t_link_us = link_bytes / (NVLINK_GBS * 1e9) * 1e6
+    t_roof_us = max(t_gemm_us, t_link_us)
     traffic = traffic_for(f"gemm_ar_megakernel_tp{tp}")
     launches_per_step = 1 + (1 if tp > 1 else 0)
     if rank == 0:
@@ -321,6 +330,12 @@ def run_gpu(args, rank, world, local_rank):
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": peak_src,
                          "traffic": traffic,
                          "kernel": "gemm_ar_megakernel", "per_launch_flops": flops_rank},
+            "roofline_call": {"bound": "nvlink" if t_link_us > t_gemm_us else "tensor",
+                              "gemm_us_at_peak": t_gemm_us, "link_bytes_per_pe": link_bytes,
+                              "link_us_at_770GBps": t_link_us, "roofline_us": t_roof_us,
+                              "frac": t_roof_us / (ms_fused * 1e3),
+                              "note": "slower of GEMM at measured peak and NVLink bytes at the "
+                                      "measured 770 GB/s per direction (900 nominal)"},
             "cpu_baseline": cpu,
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
