@@ -89,6 +89,17 @@ enum megacu_gemm_ar_algo {
                                pushes the sum to every PE */
 };
 
+/* How GEMM tiles map to CTAs. With pairs, the two CTAs of a 2-CTA cluster
+ * (two SMs) compute two vertically adjacent 128-row tiles together with
+ * 256-row tcgen05 MMAs, each SM staging half of the B tile; events,
+ * ownership and partial slots stay per 128-row tile. Pairs need an even
+ * number of tile rows (per PE block in reduce-scatter) and tile_n >= 128. */
+enum megacu_cta_pairs {
+  MEGACU_CTA_PAIRS_AUTO = 0,  /* pairs whenever the tile grid allows them */
+  MEGACU_CTA_PAIRS_OFF = 1,   /* one CTA per tile */
+  MEGACU_CTA_PAIRS_ON = 2     /* pairs, or MEGACU_UNSUPPORTED if not possible */
+};
+
 /* Element type codes, numbered as megacu::dtype (views.h:12-17). */
 enum megacu_dtype {
   MEGACU_DTYPE_UNKNOWN = 0,
@@ -111,8 +122,8 @@ typedef struct megacu_gemm_ar_problem_v2 {
                             bit-reproducible run to run. */
   int32_t dtype;         /* must be MEGACU_DTYPE_BF16 */
   int32_t num_ctas;      /* 0 = one persistent CTA per SM */
-  int32_t reserved;
-  uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 2 s */
+  int32_t cta_pairs;     /* enum megacu_cta_pairs */
+  uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 10 s */
   uint64_t *trace;       /* optional device buffer of trace records
                             (4 x uint64 each), NULL = off */
   int64_t trace_capacity; /* records that fit in `trace` */
@@ -209,10 +220,12 @@ megacu_status megacu_b200_events_bytes(megacu_gemm_ar_problem_v2 problem,
 /*
  * Tile plan of a bf16 call (host only, no GPU): info[0] tile_m, [1] tile_n,
  * [2] m_tiles, [3] n_tiles, [4] one_shot, [5] partial slots per parity plane,
- * [6] raster band height in tile rows, [7] bytes per element on the wire.
+ * [6] raster band height in tile rows, [7] bytes per element on the wire,
+ * [8] 1 if 2-CTA clusters compute 256-row pair tiles (enum megacu_cta_pairs),
+ * [9] GEMM tickets per call (tiles, or pair tiles).
  */
 megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem,
-                                    int32_t n_pes, int32_t info[8]);
+                                    int32_t n_pes, int32_t info[10]);
 
 /*
  * Where the device task queue sends raster index r (host only): out[0] tile
@@ -221,6 +234,15 @@ megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem,
  */
 megacu_status megacu_b200_plan_tile(megacu_gemm_ar_problem_v2 problem,
                                     int32_t n_pes, int32_t r, int32_t out[4]);
+
+/*
+ * Where a CTA pair's GEMM ticket q goes (host only; plans with pairs):
+ * out[0], out[1] = raster indices of the upper and lower 128-row tiles the
+ * two CTAs of the cluster compute (pass them to megacu_b200_plan_tile).
+ * MEGACU_UNSUPPORTED (detail 27) if the plan computes no CTA pairs.
+ */
+megacu_status megacu_b200_plan_pair(megacu_gemm_ar_problem_v2 problem,
+                                    int32_t n_pes, int32_t q, int32_t out[2]);
 
 /*
  * Reads the device status word of `events` after the stream has finished

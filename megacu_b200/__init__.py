@@ -7,15 +7,15 @@ does, and fails loudly if the native library is missing.
 """
 from .api import (MegacuError, Plan, Problem, Team, check, cuda_nvshmem_gemm_allreduce_phased_orchestrate,
                   driver_view, events_bytes, events_counters, events_status, gemm_allreduce,
-                  gemm_reduce_scatter, megacu_cuda_gemm_allreduce_phased_f32, plan, plan_tile,
+                  gemm_reduce_scatter, megacu_cuda_gemm_allreduce_phased_f32, plan, plan_pair, plan_tile,
                   tensor_from_pointer, torch_exchange, workspace_bytes)
-from ._capi import (ALGO_AUTO, ALGO_ONE_SHOT, ALGO_TWO_SHOT, MODE_ALLREDUCE, MODE_REDUCE_SCATTER,
-                    load)
+from ._capi import (ALGO_AUTO, ALGO_ONE_SHOT, ALGO_TWO_SHOT, CTA_PAIRS_AUTO, CTA_PAIRS_OFF,
+                    CTA_PAIRS_ON, MODE_ALLREDUCE, MODE_REDUCE_SCATTER, load)
 
 __all__ = [
     "MegacuError", "Plan", "Problem", "Team", "check", "cuda_nvshmem_gemm_allreduce_phased_orchestrate",
     "driver_view", "events_bytes", "events_counters", "events_status", "gemm_allreduce",
-    "gemm_reduce_scatter", "megacu_cuda_gemm_allreduce_phased_f32", "plan", "plan_tile", "tensor_from_pointer",
+    "gemm_reduce_scatter", "megacu_cuda_gemm_allreduce_phased_f32", "plan", "plan_pair", "plan_tile", "tensor_from_pointer",
     "torch_exchange", "workspace_bytes", "ALGO_AUTO", "ALGO_ONE_SHOT", "ALGO_TWO_SHOT",
-    "MODE_ALLREDUCE", "MODE_REDUCE_SCATTER", "load",
+    "CTA_PAIRS_AUTO", "CTA_PAIRS_OFF", "CTA_PAIRS_ON", "MODE_ALLREDUCE", "MODE_REDUCE_SCATTER", "load",
 ]

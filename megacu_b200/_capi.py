@@ -24,6 +24,7 @@ OK, INVALID_ARGUMENT, UNSUPPORTED, BACKEND_ERROR, LAUNCH_ERROR = range(5)
 STATUS_NAMES = ["ok", "invalid_argument", "unsupported", "backend_error", "launch_error"]
 MODE_ALLREDUCE, MODE_REDUCE_SCATTER = 0, 1
 ALGO_AUTO, ALGO_ONE_SHOT, ALGO_TWO_SHOT = 0, 1, 2
+CTA_PAIRS_AUTO, CTA_PAIRS_OFF, CTA_PAIRS_ON = 0, 1, 2
 DTYPE_BF16 = 2
 
 
@@ -59,7 +60,7 @@ class GemmArProblemV2(ctypes.Structure):
     _fields_ = [("m", c_int64), ("n", c_int64), ("k", c_int64), ("tile_m", c_int32),
                 ("tile_n", c_int32), ("mode", c_int32), ("algo", c_int32),
                 ("deterministic", c_int32), ("dtype", c_int32), ("num_ctas", c_int32),
-                ("reserved", c_int32), ("timeout_ns", c_uint64), ("trace", c_void_p),
+                ("cta_pairs", c_int32), ("timeout_ns", c_uint64), ("trace", c_void_p),
                 ("trace_capacity", c_int64)]
 
 
@@ -82,6 +83,8 @@ _PROTOTYPES = {
     "megacu_b200_events_bytes": (Status, [GemmArProblemV2, c_int32, ctypes.POINTER(c_int64)]),
     "megacu_b200_plan_info": (Status, [GemmArProblemV2, c_int32, ctypes.POINTER(c_int32)]),
     "megacu_b200_plan_tile":
+        (Status, [GemmArProblemV2, c_int32, c_int32, ctypes.POINTER(c_int32)]),
+    "megacu_b200_plan_pair":
         (Status, [GemmArProblemV2, c_int32, c_int32, ctypes.POINTER(c_int32)]),
     "megacu_b200_events_status": (Status, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
     "megacu_b200_events_counters": (Status, [c_void_p, c_void_p, ctypes.POINTER(c_uint64)]),

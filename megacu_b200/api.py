@@ -189,12 +189,14 @@ class Problem:
     tile_n: int = 0
     num_ctas: int = 0
     timeout_ns: int = 0
+    cta_pairs: int = _capi.CTA_PAIRS_AUTO
 
     def to_c(self, trace_ptr: Optional[int] = None, trace_capacity: int = 0) -> GemmArProblemV2:
         return GemmArProblemV2(m=self.m, n=self.n, k=self.k, tile_m=0, tile_n=self.tile_n,
                                mode=self.mode, algo=self.algo,
                                deterministic=1 if self.deterministic else 0,
-                               dtype=_capi.DTYPE_BF16, num_ctas=self.num_ctas, reserved=0,
+                               dtype=_capi.DTYPE_BF16, num_ctas=self.num_ctas,
+                               cta_pairs=self.cta_pairs,
                                timeout_ns=self.timeout_ns, trace=trace_ptr,
                                trace_capacity=trace_capacity)
 
@@ -221,6 +223,8 @@ class Plan:
     slots_per_src: int
     group_m: int
     wire_bytes: int
+    cta_pairs: bool = False  # 2-CTA clusters compute 256-row pair tiles
+    gemm_units: int = 0      # GEMM tickets per call
 
     @property
     def tiles(self) -> int:
@@ -228,15 +232,23 @@ class Plan:
 
 
 def plan(problem: Problem, n_pes: int) -> Plan:
-    info = (ctypes.c_int32 * 8)()
+    info = (ctypes.c_int32 * 10)()
     check(lib().megacu_b200_plan_info(problem.to_c(), n_pes, info))
-    return Plan(info[0], info[1], info[2], info[3], bool(info[4]), info[5], info[6], info[7])
+    return Plan(info[0], info[1], info[2], info[3], bool(info[4]), info[5], info[6], info[7],
+                bool(info[8]), info[9])
 
 
 def plan_tile(problem: Problem, n_pes: int, r: int) -> tuple[int, int, int, int]:
     """(tile_row, tile_col, owner, local index) of raster index ``r``."""
     out = (ctypes.c_int32 * 4)()
     check(lib().megacu_b200_plan_tile(problem.to_c(), n_pes, r, out))
+    return tuple(out)
+
+
+def plan_pair(problem: Problem, n_pes: int, q: int) -> tuple[int, int]:
+    """Raster indices of the two tiles a CTA pair computes for GEMM ticket ``q``."""
+    out = (ctypes.c_int32 * 2)()
+    check(lib().megacu_b200_plan_pair(problem.to_c(), n_pes, q, out))
     return tuple(out)
 
 

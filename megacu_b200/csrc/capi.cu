@@ -30,6 +30,7 @@
 #include <megacu_b200.h>
 
 #include "kernels/gemm_ar_kernel.cuh"
+#include "kernels/launch.cuh"
 #include "team.h"
 
 // ---- the C structs are the C++ types, byte for byte --------------------------
@@ -141,6 +142,8 @@ struct bf16_plan {
   std::int32_t slots_per_src = 0;
   std::int32_t group_m = 16;
   std::int32_t wire_bytes = 2;
+  std::int32_t pairs = 0;       // 1: 2-CTA clusters compute 256-row pair tiles
+  std::int32_t gemm_units = 0;  // GEMM tickets per call (tiles, or pair tiles)
   std::int64_t workspace_bytes = 0;
   std::int64_t events_bytes = 0;
 };
@@ -171,6 +174,9 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
   }
   if (p.algo < MEGACU_ALGO_AUTO || p.algo > MEGACU_ALGO_TWO_SHOT) {
     return fail(MEGACU_INVALID_ARGUMENT, 1, "unknown algo");
+  }
+  if (p.cta_pairs < MEGACU_CTA_PAIRS_AUTO || p.cta_pairs > MEGACU_CTA_PAIRS_ON) {
+    return fail(MEGACU_INVALID_ARGUMENT, 1, "unknown cta_pairs");
   }
   bf16_plan pl;
   pl.m_tiles = static_cast<std::int32_t>((p.m + kBlockM - 1) / kBlockM);
@@ -212,6 +218,21 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
     pl.one_shot = (pl.m_tiles == 1 || n_pes == 2) ? 1 : 0;
   }
   pl.wire_bytes = p.deterministic ? 4 : 2;
+  // CTA pairs halve each SM's shared-memory operand traffic per MMA (256-row
+  // MMAs, B split across the pair); they need pair tiles the grid can hold.
+  {
+    tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes,
+                              p.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
+                                                                   : mode_allreduce,
+                              pl.group_m};
+    bool const can_pair = pl.tile_n >= 128 && pairs_fit(sched);
+    if (p.cta_pairs == MEGACU_CTA_PAIRS_ON && !can_pair) {
+      return fail(MEGACU_UNSUPPORTED, 27,
+                  "CTA pairs need tile_n >= 128 and an even number of tile rows (per PE block)");
+    }
+    pl.pairs = (can_pair && p.cta_pairs != MEGACU_CTA_PAIRS_OFF) ? 1 : 0;
+    pl.gemm_units = pl.pairs ? pl.tiles / 2 : pl.tiles;
+  }
   // Each PE keeps its own partial of every tile (two parity planes); the
   // tile's reducers read it over NVLink.
   pl.slots_per_src = n_pes == 1 ? 0 : pl.tiles;
@@ -223,21 +244,6 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
 }
 
 bool aligned16(void const *p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
-
-template <int BN, bool F32>
-cudaError_t launch_bf16_kernel(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
-                               CUtensorMap const &mb, gemm_ar_params const &prm) {
-  static bool configured[kMaxDevices] = {};
-  auto kernel = &gemm_ar_megakernel<BN, F32>;
-  if (device >= 0 && device < kMaxDevices && !configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         gemm_config<BN>::smem_bytes);
-    if (e != cudaSuccess) return e;
-    configured[device] = true;
-  }
-  kernel<<<grid, kThreads, gemm_config<BN>::smem_bytes, stream>>>(ma, mb, prm);
-  return cudaGetLastError();
-}
 
 megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, void *workspace,
                        void *out, void *events, megacu_gemm_ar_problem_v2 problem) {
@@ -328,20 +334,8 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   int grid = problem.num_ctas > 0 ? problem.num_ctas : sm_count(device);
   auto stream = static_cast<cudaStream_t>(driver.launch.stream);
   bool const f32 = pl.wire_bytes == 4;
-  switch (pl.tile_n) {
-    case 256:
-      e = f32 ? launch_bf16_kernel<256, true>(device, grid, stream, map_a, map_b, prm)
-              : launch_bf16_kernel<256, false>(device, grid, stream, map_a, map_b, prm);
-      break;
-    case 128:
-      e = f32 ? launch_bf16_kernel<128, true>(device, grid, stream, map_a, map_b, prm)
-              : launch_bf16_kernel<128, false>(device, grid, stream, map_a, map_b, prm);
-      break;
-    default:
-      e = f32 ? launch_bf16_kernel<64, true>(device, grid, stream, map_a, map_b, prm)
-              : launch_bf16_kernel<64, false>(device, grid, stream, map_a, map_b, prm);
-      break;
-  }
+  e = f32 ? launch_gemm_ar<true>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm)
+          : launch_gemm_ar<false>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm);
   if (e != cudaSuccess) return cuda_fail(e, 14);
   return ok_status();
 }
@@ -684,7 +678,7 @@ extern "C" megacu_status megacu_b200_events_bytes(megacu_gemm_ar_problem_v2 prob
 }
 
 extern "C" megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem, std::int32_t n_pes,
-                                               std::int32_t info[8]) {
+                                               std::int32_t info[10]) {
   if (info == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing output");
   bf16_plan pl;
   megacu_status st = make_plan(problem, n_pes, pl);
@@ -697,6 +691,26 @@ extern "C" megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem
   info[5] = pl.slots_per_src;
   info[6] = pl.group_m;
   info[7] = pl.wire_bytes;
+  info[8] = pl.pairs;
+  info[9] = pl.gemm_units;
+  return ok_status();
+}
+
+extern "C" megacu_status megacu_b200_plan_pair(megacu_gemm_ar_problem_v2 problem,
+                                               std::int32_t n_pes, std::int32_t q,
+                                               std::int32_t out[2]) {
+  if (out == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing output");
+  bf16_plan pl;
+  megacu_status st = make_plan(problem, n_pes, pl);
+  if (st.code != MEGACU_OK) return st;
+  if (!pl.pairs) return fail(MEGACU_UNSUPPORTED, 27, "this plan computes no CTA pairs");
+  if (q < 0 || q >= pl.gemm_units) return fail(MEGACU_INVALID_ARGUMENT, 1, "pair ticket out of range");
+  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes,
+                            problem.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
+                                                                       : mode_allreduce,
+                            pl.group_m};
+  out[0] = pair_raster(sched, q, 0);
+  out[1] = pair_raster(sched, q, 1);
   return ok_status();
 }
 

@@ -55,14 +55,20 @@ inline constexpr int kReduceWarps = 4;
 inline constexpr int kWorkerWarps = 8;
 inline constexpr std::uint64_t kLocalTimeoutNs = 4000000000ull;
 
-template <int BN>
+// kPair: the CTA of a 2-CTA cluster that computes one half of a 256-row pair
+// tile; it stages its own 128 rows of A and half (BN / 2 columns) of B.
+template <int BN, bool kPair = false>
 struct gemm_config {
   static_assert(BN == 64 || BN == 128 || BN == 256, "tile_n must be 64, 128 or 256");
+  static_assert(!kPair || BN >= 128, "CTA pairs need tile_n >= 128");
+  static constexpr int b_cols = kPair ? BN / 2 : BN;          // B columns staged per CTA
   static constexpr int a_bytes = kBlockM * kBlockK * 2;        // 16 KiB
   static constexpr int b_panel_bytes = kBlockK * 64 * 2;       // 8 KiB per 64 columns
-  static constexpr int b_bytes = kBlockK * BN * 2;
+  static constexpr int b_bytes = kBlockK * b_cols * 2;
   static constexpr int stage_bytes = a_bytes + b_bytes;
-  static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8
+  // Bytes one stage's full barrier waits for (the leader's counts both CTAs).
+  static constexpr int tx_bytes = kPair ? 2 * stage_bytes : stage_bytes;
+  static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8; pairs 8 / 6
   static constexpr int col_blocks = BN / 64;                   // sub-tasks per quarter
   static constexpr int reduce_bytes = kWorkerWarps * 32 * 128; // transpose tiles
   static constexpr int n_barriers = 2 * stages + 4 + 2 * kTaskRing + 1;
@@ -379,12 +385,34 @@ __device__ __forceinline__ void wait_all_pushes(gemm_ar_params const &p, std::ui
 
 }  // namespace detail
 
-template <int BN, bool kWireF32>
+// Bounded mbarrier wait; CTA-pair kernels wait with cluster-scope acquire
+// because the other CTA of the pair arrives on some of their barriers.
+template <bool kPair>
+__device__ __forceinline__ bool bar_wait(std::uint64_t *bar, std::uint32_t parity,
+                                         std::uint32_t const *abort_word) {
+  if constexpr (kPair) {
+    return ptx::mbar_wait_cluster(bar, parity, abort_word, kLocalTimeoutNs);
+  } else {
+    return ptx::mbar_wait(bar, parity, abort_word, kLocalTimeoutNs);
+  }
+}
+
+// kPair = false: one CTA per SM, each GEMM ticket is one 128 x BN tile.
+// kPair = true: launched as 2-CTA clusters; each GEMM ticket is a 256 x BN
+// pair tile computed by both CTAs with cta_group::2 MMAs issued by the
+// leader (cluster rank 0). Each CTA TMA-loads its own 128 rows of A and its
+// half of B into its own shared memory (completion counted on the leader's
+// full barrier), and holds its 128 accumulator rows in its own TMEM, so the
+// epilogue and everything after it are the same in both CTAs. The leader
+// relays the barrier events the follower needs (stage free, accumulator
+// ready, next task) with remote mbarrier arrives; the follower reports back
+// (task taken, accumulator drained) the same way.
+template <int BN, bool kWireF32, bool kPair = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ar_megakernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ gemm_ar_params p) {
-  using cfg = gemm_config<BN>;
+  using cfg = gemm_config<BN, kPair>;
   constexpr int kWireBytes = kWireF32 ? 4 : 2;
   constexpr int kVecCols = 16 / kWireBytes;                   // columns per 16 B wire vector
   constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * kWireBytes;
@@ -412,19 +440,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::uint32_t const *abort_word = &ctrl->error_code;
   tile_schedule const sched{p.m_tiles, p.n_tiles, p.n_pes, p.mode, p.group_m};
   std::int32_t const k_blocks = (p.k + kBlockK - 1) / kBlockK;
+  // GEMM tickets: tiles, or pair tiles.
+  std::int32_t const gemm_units = kPair ? p.tiles / 2 : p.tiles;
+  std::uint32_t const cta_rank = kPair ? ptx::cluster_ctarank() : 0u;
+  bool const leader = cta_rank == 0;
+  // Raster index of the tile this CTA computes for GEMM ticket q.
+  auto tile_of = [&](std::int32_t q) {
+    return kPair ? pair_raster(sched, q, static_cast<std::int32_t>(cta_rank)) : q;
+  };
 
   if (threadIdx.x == 0) {
+    // Arrivals per phase. Pairs: the leader's acc_empty also counts the
+    // follower's 4 epilogue warps, its task_empty the follower's 4 epilogue
+    // warps and producer; the follower's own empty / acc_full / task_full
+    // are arrived by the leader (one each).
     for (int s = 0; s < cfg::stages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&acc_full[b], 1);
-      ptx::mbar_init(&acc_empty[b], 4);
+      ptx::mbar_init(&acc_empty[b], kPair ? 8 : 4);
     }
     for (int i = 0; i < kTaskRing; ++i) {
       ptx::mbar_init(&task_full[i], 1);
-      ptx::mbar_init(&task_empty[i], 5);
+      ptx::mbar_init(&task_empty[i], kPair ? 10 : 5);
     }
     ptx::mbar_init(mma_done, 1);
     ptx::fence_barrier_init();
@@ -433,11 +473,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::prefetch_tensor_map(&map_b);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, cfg::tmem_columns);
-    ptx::tmem_relinquish();
+    if constexpr (kPair) {
+      ptx::tmem_alloc_pair(tmem_slot, cfg::tmem_columns);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(tmem_slot, cfg::tmem_columns);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before_sync();
   __syncthreads();
+  if constexpr (kPair) {
+    ptx::cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  }
   ptx::tc_fence_after_sync();
   std::uint32_t const tmem_base = *tmem_slot;
   std::uint32_t const epoch = *epoch_slot;
@@ -451,53 +499,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (std::uint32_t n = 0; ok; ++n) {
         std::uint32_t const slot = n % kTaskRing;
-        if (!ptx::mbar_wait(&task_empty[slot], ((n / kTaskRing) & 1u) ^ 1u, abort_word,
-                            kLocalTimeoutNs)) {
-          detail::record_error(p, err_local_timeout, 0, 0, 1);
+        std::int32_t q = -1;
+        if (leader) {
+          // Fetch the next GEMM ticket into this CTA's ring (and the
+          // follower's) once every consumer has taken the slot's last one.
+          if (!bar_wait<kPair>(&task_empty[slot], ((n / kTaskRing) & 1u) ^ 1u, abort_word)) {
+            detail::record_error(p, err_local_timeout, 0, 0, 1);
+            break;
+          }
+          std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
+          q = ticket < static_cast<std::uint32_t>(gemm_units) ? static_cast<std::int32_t>(ticket)
+                                                              : -1;
+          ring[slot] = q;
+          if constexpr (kPair) {
+            ptx::st_shared_remote(ptx::map_to_rank(const_cast<std::int32_t *>(&ring[slot]), 1), q);
+            ptx::mbar_arrive_remote(ptx::map_to_rank(&task_full[slot], 1));
+          }
+          ptx::mbar_arrive(&task_full[slot]);
+        } else {
+          // Follower: take the ticket the leader wrote into this CTA's ring.
+          if (!bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word)) {
+            detail::record_error(p, err_local_timeout, 0, 1, 1);
+            break;
+          }
+          q = ring[slot];
+          ptx::mbar_arrive_remote(ptx::map_to_rank(&task_empty[slot], 0));
+        }
+        if (q < 0) {
           break;
         }
-        std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
-        std::int32_t const r = ticket < static_cast<std::uint32_t>(p.tiles)
-                                   ? static_cast<std::int32_t>(ticket)
-                                   : -1;
-        ring[slot] = r;
-        ptx::mbar_arrive(&task_full[slot]);
-        if (r < 0) {
-          break;
-        }
+        std::int32_t const r = tile_of(q);
         tile_coord const c = locate(sched, r);
+        std::int32_t const b_col0 = c.tile_col * BN + static_cast<std::int32_t>(cta_rank) * cfg::b_cols;
         for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
           std::uint32_t const s = it % cfg::stages;
-          if (!ptx::mbar_wait(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word,
-                              kLocalTimeoutNs)) {
+          if (!bar_wait<kPair>(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word)) {
             detail::record_error(p, err_local_timeout, r, 0, 2);
             ok = false;
             break;
           }
           std::uint8_t *sa = stages + s * cfg::stage_bytes;
           std::uint8_t *sb = sa + cfg::a_bytes;
-          ptx::mbar_arrive_expect_tx(&full[s], cfg::stage_bytes);
-          ptx::tma_load_2d(&map_a, &full[s], sa, kb * kBlockK, c.tile_row * kBlockM);
+          if constexpr (kPair) {
+            // The pair MMAs that freed this stage read the follower's copy
+            // too: pass the event on (from the second use of the stage on).
+            // Relaxed: the event orders async-proxy work only (MMA reads
+            // complete, then the follower's TMA overwrites), and the arrive
+            // follows this thread's acquire of the MMA's commit.
+            if (leader && it >= static_cast<std::uint32_t>(cfg::stages)) {
+              ptx::mbar_arrive_remote_relaxed(ptx::map_to_rank(&empty[s], 1));
+            }
+            std::uint32_t const bar = ptx::map_to_rank(&full[s], 0);
+            if (leader) ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
+            ptx::tma_load_2d_pair(&map_a, bar, sa, kb * kBlockK, c.tile_row * kBlockM);
 #pragma unroll
-          for (int panel = 0; panel < BN / 64; ++panel) {
-            ptx::tma_load_2d(&map_b, &full[s], sb + panel * cfg::b_panel_bytes,
-                             c.tile_col * BN + panel * 64, kb * kBlockK);
+            for (int panel = 0; panel < cfg::b_cols / 64; ++panel) {
+              ptx::tma_load_2d_pair(&map_b, bar, sb + panel * cfg::b_panel_bytes,
+                                    b_col0 + panel * 64, kb * kBlockK);
+            }
+          } else {
+            ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
+            ptx::tma_load_2d(&map_a, &full[s], sa, kb * kBlockK, c.tile_row * kBlockM);
+#pragma unroll
+            for (int panel = 0; panel < BN / 64; ++panel) {
+              ptx::tma_load_2d(&map_b, &full[s], sb + panel * cfg::b_panel_bytes,
+                               b_col0 + panel * 64, kb * kBlockK);
+            }
           }
         }
       }
       // Drain: the most recent load of every stage must have landed before
-      // this CTA may exit (normally they were all consumed already).
-      for (std::uint32_t back = 1; back <= cfg::stages && back <= it; ++back) {
+      // this CTA may exit (normally they were all consumed already). A
+      // follower's loads complete on the leader's barriers; the leader's
+      // drain covers them, and the follower cannot exit before the leader
+      // reaches the closing cluster barrier.
+      for (std::uint32_t back = 1; leader && back <= cfg::stages && back <= it; ++back) {
         std::uint32_t const i = it - back;
-        ptx::mbar_wait(&full[i % cfg::stages], (i / cfg::stages) & 1u, nullptr,
-                       kLocalTimeoutNs);
+        bar_wait<kPair>(&full[i % cfg::stages], (i / cfg::stages) & 1u, nullptr);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- tcgen05.mma issuer ----------------
-    if (lane == 0) {
-      std::uint32_t const idesc = ptx::idesc_bf16_f32(kBlockM, BN, true);
+    // (Pairs: the leader issues for both CTAs; the follower's warp 1 only
+    // holds its half of the TMEM allocation.)
+    if (lane == 0 && leader) {
+      std::uint32_t const idesc = ptx::idesc_bf16_f32(kPair ? 2 * kBlockM : kBlockM, BN, true);
       std::uint32_t it = 0;
       for (std::uint32_t n = 0;; ++n) {
         std::uint32_t const slot = n % kTaskRing;
@@ -512,8 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         std::uint32_t const buf = n & 1u;
-        if (!ptx::mbar_wait(&acc_empty[buf], ((n >> 1) & 1u) ^ 1u, abort_word,
-                            kLocalTimeoutNs)) {
+        if (!bar_wait<kPair>(&acc_empty[buf], ((n >> 1) & 1u) ^ 1u, abort_word)) {
           detail::record_error(p, err_local_timeout, r, 0, 4);
           break;
         }
@@ -522,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
           std::uint32_t const s = it % cfg::stages;
-          if (!ptx::mbar_wait(&full[s], (it / cfg::stages) & 1u, abort_word, kLocalTimeoutNs)) {
+          if (!bar_wait<kPair>(&full[s], (it / cfg::stages) & 1u, abort_word)) {
             detail::record_error(p, err_local_timeout, r, 0, 5);
             ok = false;
             break;
@@ -537,20 +623,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             std::uint64_t const a_desc = ptx::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             // B: MN-major, 128 B swizzle; 64-column panels `b_panel_bytes`
             // apart (leading), 8-k-row groups 1024 B apart (stride); a K step
-            // of 16 rows is 2048 B.
+            // of 16 rows is 2048 B. (Pairs: both descriptors address the
+            // same offsets in both CTAs; each CTA holds its half of B.)
             std::uint64_t const b_desc =
                 ptx::smem_desc_sw128(b_addr + kk * 2048, cfg::b_panel_bytes, 1024);
-            ptx::umma_f16(d_tmem, a_desc, b_desc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            std::uint32_t const acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (kPair) {
+              ptx::umma_f16_pair(d_tmem, a_desc, b_desc, idesc, acc);
+            } else {
+              ptx::umma_f16(d_tmem, a_desc, b_desc, idesc, acc);
+            }
           }
-          ptx::umma_commit(&empty[s]);
+          if constexpr (kPair) {
+            ptx::umma_commit_pair(&empty[s]);
+          } else {
+            ptx::umma_commit(&empty[s]);
+          }
         }
         if (!ok) {
           break;
         }
-        ptx::umma_commit(&acc_full[buf]);
+        if constexpr (kPair) {
+          ptx::umma_commit_pair(&acc_full[buf]);
+        } else {
+          ptx::umma_commit(&acc_full[buf]);
+        }
       }
       // Every issued MMA must be complete before TMEM is released.
-      ptx::umma_commit(mma_done);
+      if constexpr (kPair) {
+        ptx::umma_commit_pair(mma_done);
+      } else {
+        ptx::umma_commit(mma_done);
+      }
       ptx::mbar_wait(mma_done, 0, nullptr, kLocalTimeoutNs);
     }
     __syncwarp();
@@ -561,21 +665,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (std::uint32_t n = 0;; ++n) {
       std::uint32_t const slot = n % kTaskRing;
       // Warp-uniform decision: every lane waits, the warp acts on the vote.
-      if (!__all_sync(0xffffffffu, ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u,
-                                                  abort_word, kLocalTimeoutNs))) {
-        if (lane == 0) detail::record_error(p, err_local_timeout, 0, 0, 6);
-        break;
-      }
-      std::int32_t const r = __shfl_sync(0xffffffffu, ring[slot], 0);
-      if (lane == 0) ptx::mbar_arrive(&task_empty[slot]);
-      if (r < 0) {
-        break;
-      }
-      std::uint32_t const buf = n & 1u;
       if (!__all_sync(0xffffffffu,
-                      ptx::mbar_wait(&acc_full[buf], (n >> 1) & 1u, abort_word, kLocalTimeoutNs))) {
-        if (lane == 0) detail::record_error(p, err_local_timeout, r, 0, 7);
+                      bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word))) {
+        if (lane == 0) detail::record_error(p, err_local_timeout, 0, cta_rank, 6);
         break;
+      }
+      std::int32_t const q = __shfl_sync(0xffffffffu, ring[slot], 0);
+      if (lane == 0) {
+        if (leader) {
+          ptx::mbar_arrive(&task_empty[slot]);
+        } else {
+          ptx::mbar_arrive_remote(ptx::map_to_rank(&task_empty[slot], 0));
+        }
+      }
+      if (q < 0) {
+        break;
+      }
+      std::int32_t const r = tile_of(q);
+      std::uint32_t const buf = n & 1u;
+      if (!__all_sync(0xffffffffu, bar_wait<kPair>(&acc_full[buf], (n >> 1) & 1u, abort_word))) {
+        if (lane == 0) detail::record_error(p, err_local_timeout, r, cta_rank, 7);
+        break;
+      }
+      if constexpr (kPair) {
+        // The pair MMAs also wrote the follower's accumulator rows.
+        if (leader && warp == kEpilogueWarp0 && lane == 0) {
+          ptx::mbar_arrive_remote(ptx::map_to_rank(&acc_full[buf], 1));
+        }
       }
       ptx::tc_fence_after_sync();
       std::uint64_t const t0 = ptx::now_ns();
@@ -636,7 +752,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // TMEM buffer is free for the next tile once every lane has read it.
       ptx::tc_fence_before_sync();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if (leader) {
+          ptx::mbar_arrive(&acc_empty[buf]);
+        } else {
+          ptx::mbar_arrive_remote(ptx::map_to_rank(&acc_empty[buf], 0));
+        }
+      }
 
       if (lane == 0 && quarter == 0) {
         detail::count(p, ctr_gemm_tasks, 1);
@@ -687,9 +809,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   ptx::tc_fence_before_sync();
   __syncthreads();
+  if constexpr (kPair) {
+    // No remote arrive, MMA or TMA write may still target the other CTA.
+    ptx::cluster_sync();
+  }
   ptx::tc_fence_after_sync();
   if (warp == 1) {
-    ptx::tmem_dealloc(tmem_base, cfg::tmem_columns);
+    if constexpr (kPair) {
+      ptx::tmem_dealloc_pair(tmem_base, cfg::tmem_columns);
+    } else {
+      ptx::tmem_dealloc(tmem_base, cfg::tmem_columns);
+    }
   }
   if (threadIdx.x == 0) {
     __threadfence();

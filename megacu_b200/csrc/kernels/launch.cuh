@@ -1,0 +1,76 @@
+// Host-side launch of the megakernel variants: one CTA per SM, or 2-CTA
+// clusters (CTA pairs) for the cta_group::2 GEMM.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "gemm_ar_kernel.cuh"
+
+namespace megacu_b200 {
+
+inline constexpr int kLaunchMaxDevices = 64;
+
+template <int BN, bool kWireF32, bool kPair>
+cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
+                           CUtensorMap const &mb, gemm_ar_params const &prm) {
+  static bool configured[kLaunchMaxDevices] = {};
+  static int max_pairs[kLaunchMaxDevices] = {};
+  constexpr int smem = gemm_config<BN, kPair>::smem_bytes;
+  auto kernel = &gemm_ar_megakernel<BN, kWireF32, kPair>;
+  bool const known = device >= 0 && device < kLaunchMaxDevices;
+  if (!known || !configured[device]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (known) configured[device] = true;
+  }
+  if constexpr (!kPair) {
+    kernel<<<grid, kThreads, smem, stream>>>(ma, mb, prm);
+    return cudaGetLastError();
+  } else {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Persistent: at most as many pairs as fit on the device at once.
+    int pairs = known ? max_pairs[device] : 0;
+    if (pairs == 0) {
+      cfg.gridDim = dim3(2, 1, 1);
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+      if (pairs < 1) return cudaErrorInvalidConfiguration;
+      if (known) max_pairs[device] = pairs;
+    }
+    int const g = std::max(2, std::min(grid / 2, pairs) * 2);
+    cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, prm);
+  }
+}
+
+// Launches the variant a plan picked: tile_n 64 / 128 / 256, CTA pairs
+// (tile_n >= 128 only) or not.
+template <bool kWireF32>
+cudaError_t launch_gemm_ar(int tile_n, bool pairs, int device, int grid, cudaStream_t stream,
+                           CUtensorMap const &ma, CUtensorMap const &mb,
+                           gemm_ar_params const &prm) {
+  switch (tile_n) {
+    case 256:
+      return pairs ? launch_variant<256, kWireF32, true>(device, grid, stream, ma, mb, prm)
+                   : launch_variant<256, kWireF32, false>(device, grid, stream, ma, mb, prm);
+    case 128:
+      return pairs ? launch_variant<128, kWireF32, true>(device, grid, stream, ma, mb, prm)
+                   : launch_variant<128, kWireF32, false>(device, grid, stream, ma, mb, prm);
+    default:
+      return launch_variant<64, kWireF32, false>(device, grid, stream, ma, mb, prm);
+  }
+}
+
+}  // namespace megacu_b200

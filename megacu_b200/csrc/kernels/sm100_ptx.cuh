@@ -154,6 +154,81 @@ __device__ __forceinline__ bool mbar_wait(std::uint64_t *bar, std::uint32_t pari
   }
 }
 
+// ---- clusters (CTA pairs) --------------------------------------------------------
+
+__device__ __forceinline__ std::uint32_t cluster_ctarank() {
+  std::uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ std::uint32_t map_to_rank(void const *local, std::uint32_t rank) {
+  std::uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(local)), "r"(rank));
+  return out;
+}
+
+// Arrive once on an mbarrier of another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(std::uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               :: "r"(cluster_addr) : "memory");
+}
+
+// Relaxed form, for pure events that publish no data of this thread. A
+// release at cluster scope costs the issuing thread about a microsecond when
+// it has TMA loads in flight (measured), so the per-k-block relay uses this.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(std::uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];"
+               :: "r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_remote(std::uint32_t cluster_addr, std::int32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test_cluster(std::uint32_t bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait for barriers that other CTAs of the cluster arrive on: the wait
+// acquires at cluster scope.
+__device__ __forceinline__ bool mbar_wait_cluster(std::uint64_t *bar, std::uint32_t parity,
+                                                  std::uint32_t const *abort_word,
+                                                  std::uint64_t timeout_ns) {
+  std::uint32_t const a = smem_addr(bar);
+  if (mbar_test_cluster(a, parity)) {
+    return true;
+  }
+  std::uint64_t const start = now_ns();
+  for (std::uint32_t spin = 1;; ++spin) {
+    if (mbar_test_cluster(a, parity)) {
+      return true;
+    }
+    if ((spin & 127u) == 0) {
+      if (abort_word != nullptr && ld_relaxed_gpu(abort_word) != 0) {
+        return false;
+      }
+      if (now_ns() - start > timeout_ns) {
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---- TMA -------------------------------------------------------------------------
 
 __device__ __forceinline__ void prefetch_tensor_map(CUtensorMap const *map) {
@@ -167,6 +242,17 @@ __device__ __forceinline__ void tma_load_2d(CUtensorMap const *map, std::uint64_
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];"
       :: "r"(smem_addr(dst)), "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's leader CTA (`bar_cluster` from map_to_rank).
+__device__ __forceinline__ void tma_load_2d_pair(CUtensorMap const *map, std::uint32_t bar_cluster,
+                                                 void *dst, std::int32_t x, std::int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];"
+      :: "r"(smem_addr(dst)), "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -205,6 +291,44 @@ __device__ __forceinline__ void umma_f16(std::uint32_t d_tmem, std::uint64_t a_d
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
       :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(no_mask)
       : "memory");
+}
+
+// ---- the CTA-pair (cta_group::2) forms: both CTAs of the pair allocate the
+// same TMEM columns; the leader issues MMAs whose A and B halves and
+// accumulator rows live in both CTAs.
+
+__device__ __forceinline__ void tmem_alloc_pair(std::uint32_t *dst, std::uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               :: "r"(smem_addr(dst)), "r"(columns) : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(std::uint32_t taddr, std::uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+               :: "r"(taddr), "r"(columns) : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(std::uint32_t d_tmem, std::uint64_t a_desc,
+                                              std::uint64_t b_desc, std::uint32_t idesc,
+                                              std::uint32_t accumulate) {
+  std::uint32_t const no_mask = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, "
+      "{%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+      :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(no_mask)
+      : "memory");
+}
+
+// Arrives once on the leader's `bar` when every previously issued pair MMA of
+// this thread has completed.
+__device__ __forceinline__ void umma_commit_pair(std::uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(smem_addr(bar)) : "memory");
 }
 
 // Arrives once on `bar` when every previously issued tcgen05.mma of this

@@ -76,6 +76,32 @@ MEGACU_B200_HD tile_coord locate(tile_schedule const &s, std::int32_t r) {
   return c;
 }
 
+// CTA-pair schedule. The two CTAs of a cluster compute the two vertically
+// adjacent 128-row tiles (2i, col) and (2i + 1, col) of one 256-row pair
+// tile; the GEMM queue then hands out pair tickets q, and CTA `rank` (0 or 1)
+// of the pair computes raster index pair_raster(q, rank). Allreduce: the
+// raster walks a band's rows column by column, so with an even band height
+// r = 2q and 2q + 1 are such neighbours. Reduce-scatter: PE o's tiles have
+// raster indices local * n_pes + o, and locals 2u, 2u + 1 are neighbours in
+// o's row block.
+MEGACU_B200_HD bool pairs_fit(tile_schedule const &s) {
+  if (s.group_m % 2 != 0) {
+    return false;
+  }
+  if (s.mode == mode_reduce_scatter) {
+    return (s.m_tiles / s.n_pes) % 2 == 0;
+  }
+  return s.m_tiles % 2 == 0;
+}
+
+MEGACU_B200_HD std::int32_t pair_raster(tile_schedule const &s, std::int32_t q,
+                                        std::int32_t rank) {
+  if (s.mode == mode_reduce_scatter) {
+    return (2 * (q / s.n_pes) + rank) * s.n_pes + q % s.n_pes;
+  }
+  return 2 * q + rank;
+}
+
 // Number of tiles PE q reduces under the two-shot / reduce-scatter split.
 MEGACU_B200_HD std::int32_t owned_tiles(tile_schedule const &s, std::int32_t q) {
   std::int32_t const t = s.tiles();

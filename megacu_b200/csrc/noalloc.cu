@@ -29,6 +29,7 @@
 #include <megacu_b200.h>
 
 #include "kernels/gemm_ar_kernel.cuh"
+#include "kernels/launch.cuh"
 
 namespace {
 
@@ -43,7 +44,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 std::mutex g_noalloc_mu;
 void *g_noalloc_addr[kNoAllocMaxDevices] = {};
-bool g_noalloc_configured[kNoAllocMaxDevices][3] = {};
 
 megacu_status na_ok() { return {MEGACU_OK, 0, nullptr}; }
 
@@ -96,20 +96,6 @@ bool na_encode(CUtensorMap *map, void const *base, std::int64_t rows, std::int64
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-cudaError_t na_launch(int device, int slot, int grid, cudaStream_t stream, CUtensorMap const &ma,
-                      CUtensorMap const &mb, gemm_ar_params const &prm) {
-  auto kernel = &gemm_ar_megakernel<BN, false>;
-  if (!g_noalloc_configured[device][slot]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         gemm_config<BN>::smem_bytes);
-    if (e != cudaSuccess) return e;
-    g_noalloc_configured[device][slot] = true;
-  }
-  kernel<<<grid, kThreads, gemm_config<BN>::smem_bytes, stream>>>(ma, mb, prm);
-  return cudaGetLastError();
-}
-
 }  // namespace
 
 extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver, void const *a,
@@ -120,7 +106,7 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
                    "the allocation-free entry runs on one PE only (team_n_pes must be 1)");
   }
   problem.mode = MEGACU_MODE_ALLREDUCE;
-  std::int32_t info[8];
+  std::int32_t info[10];
   megacu_status st = megacu_b200_plan_info(problem, 1, info);
   if (st.code != MEGACU_OK) return st;
   if (a == nullptr || b == nullptr || out == nullptr) {
@@ -181,17 +167,7 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return na_cuda(e, 10);
   int const grid = problem.num_ctas > 0 ? problem.num_ctas : sms;
-  switch (tile_n) {
-    case 256:
-      e = na_launch<256>(device, 2, grid, stream, map_a, map_b, prm);
-      break;
-    case 128:
-      e = na_launch<128>(device, 1, grid, stream, map_a, map_b, prm);
-      break;
-    default:
-      e = na_launch<64>(device, 0, grid, stream, map_a, map_b, prm);
-      break;
-  }
+  e = launch_gemm_ar<false>(tile_n, info[8] != 0, device, grid, stream, map_a, map_b, prm);
   if (e != cudaSuccess) return na_cuda(e, 14);
   return na_ok();
 }

@@ -169,6 +169,14 @@ void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode
   }
 }
 
+void oracle_pair_raster(int32_t n_pes, int32_t mode, int32_t q, int32_t out[2]) {
+  for (int32_t rank = 0; rank < 2; ++rank) {
+    /* allreduce: raster neighbours 2q, 2q + 1 (a band is walked column by
+     * column); reduce-scatter: owner q % n_pes's local tiles 2u, 2u + 1. */
+    out[rank] = mode == 1 ? (2 * (q / n_pes) + rank) * n_pes + q % n_pes : 2 * q + rank;
+  }
+}
+
 /* Event tensor words after the control block (restates layout.h):
  * arrive[p][src][t][q] (q < 4 quarters), then done[p][src]. */
 static int64_t arrive_idx(int32_t parity, int32_t src, int32_t tile, int32_t quarter,

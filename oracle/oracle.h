@@ -60,6 +60,11 @@ int oracle_phased_f32(int64_t m, int64_t n, int64_t k, int32_t tile_m, int32_t t
 void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode,
                    int32_t group_m, int32_t r, int32_t out[4]);
 
+/* CTA-pair schedule restatement (a B200 addition with no counterpart in
+ * megacu): GEMM pair ticket q -> out[0], out[1] = raster indices of the
+ * upper and lower 128-row tiles the two CTAs of a cluster compute. */
+void oracle_pair_raster(int32_t n_pes, int32_t mode, int32_t q, int32_t out[2]);
+
 typedef struct oracle_bf16_problem {
   int64_t m, n, k;       /* k = per-PE slice */
   int32_t tile_m;        /* 128 */

@@ -44,6 +44,7 @@ def load():
                                           ctypes.POINTER(_f32p),
                                           ctypes.POINTER(ctypes.POINTER(ctypes.c_int32))]
         lib.oracle_locate.argtypes = [ctypes.c_int32] * 6 + [ctypes.POINTER(ctypes.c_int32)]
+        lib.oracle_pair_raster.argtypes = [ctypes.c_int32] * 3 + [ctypes.POINTER(ctypes.c_int32)]
         lib.oracle_bf16_call.argtypes = [ctypes.POINTER(OracleBf16Problem),
                                          ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
                                          ctypes.POINTER(_f32p),
@@ -106,6 +107,12 @@ def phased_f32(a_list, b_list, m, n, k, tile_m, tile_n):
 def locate(m_tiles, n_tiles, n_pes, mode, group_m, r):
     out = (ctypes.c_int32 * 4)()
     load().oracle_locate(m_tiles, n_tiles, n_pes, mode, group_m, r, out)
+    return tuple(out)
+
+
+def pair_raster(n_pes, mode, q):
+    out = (ctypes.c_int32 * 2)()
+    load().oracle_pair_raster(n_pes, mode, q, out)
     return tuple(out)
 
 

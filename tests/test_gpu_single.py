@@ -30,10 +30,13 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "kat_gemm_allreduce.j
     (1024, 1024, 1024, 256),
     (16, 8192, 3584, 0),     # decode shape: one 16-row tile row, tile_n 64
     (130, 264, 8, 64),       # k shorter than one k-block
+    (200, 264, 72, 128),     # one CTA pair: ragged lower tile, ragged last column tile
+    (512, 768, 1000, 256),   # pairs with tile_n 256, k not a multiple of 64
 ])
-def test_bf16_tp1_matches_oracle(m, n, k, tile_n):
+@pytest.mark.parametrize("pairs", [mb.CTA_PAIRS_OFF, mb.CTA_PAIRS_AUTO])
+def test_bf16_tp1_matches_oracle(m, n, k, tile_n, pairs):
     a, b = inputs(1, 1, m, n, k)
-    prob = mb.Problem(m, n, k, tile_n=tile_n)
+    prob = mb.Problem(m, n, k, tile_n=tile_n, cta_pairs=pairs)
     ctx = SinglePE(prob)
     out = ctx.run(a[0].cuda(), b[0].cuda())
     torch.cuda.synchronize()
@@ -42,11 +45,13 @@ def test_bf16_tp1_matches_oracle(m, n, k, tile_n):
     assert rel_error(f32(out), want) < REL_TOL
 
 
-def test_bf16_tp1_events_counters_trace_and_determinism():
+@pytest.mark.parametrize("pairs", [mb.CTA_PAIRS_OFF, mb.CTA_PAIRS_ON])
+def test_bf16_tp1_events_counters_trace_and_determinism(pairs):
     m, n, k = 512, 768, 320
     a, b = inputs(2, 1, m, n, k)
-    prob = mb.Problem(m, n, k, tile_n=128)
+    prob = mb.Problem(m, n, k, tile_n=128, cta_pairs=pairs)
     ctx = SinglePE(prob)
+    assert ctx.plan.cta_pairs == (pairs == mb.CTA_PAIRS_ON)
     tiles = ctx.plan.tiles
     trace = torch.zeros(tiles * 4 * 4, dtype=torch.int64, device="cuda")
     ev0 = ctx.event_words()
@@ -71,6 +76,21 @@ def test_bf16_tp1_events_counters_trace_and_determinism():
                                 events=[ev1])
     assert np.array_equal(ev2, ref2["events"][0])
     assert mb.events_counters(ctx.events)[6] == 2
+
+
+def test_bf16_tp1_pairs_equal_single_ctas_bitwise():
+    """A 256-row pair MMA sums each output element over k in the same order as
+    two 128-row MMAs: both tilings give the same bits."""
+    m, n, k = 1024, 2048, 1536
+    a, b = inputs(4, 1, m, n, k)
+    ad, bd = a[0].cuda(), b[0].cuda()
+    outs = []
+    for pairs in (mb.CTA_PAIRS_OFF, mb.CTA_PAIRS_ON):
+        ctx = SinglePE(mb.Problem(m, n, k, tile_n=256, cta_pairs=pairs))
+        outs.append(ctx.run(ad, bd).clone())
+    torch.cuda.synchronize()
+    assert rel_error(f32(outs[1]), f32(outs[0])) < REL_TOL
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_bf16_tp1_direct_launcher_equals_orchestrated():

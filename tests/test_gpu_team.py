@@ -88,16 +88,19 @@ need2 = pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
 
 
 @need2
-@pytest.mark.parametrize("m,n,k,mode,algo,det", [
-    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False),
-    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False),
-    (300, 520, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True),
-    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False),
-    (2048, 4096, 1024, mb.MODE_ALLREDUCE, mb.ALGO_AUTO, False),
+@pytest.mark.parametrize("m,n,k,mode,algo,det,tile_n", [
+    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0),
+    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0),
+    (300, 520, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True, 0),
+    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 0),
+    (2048, 4096, 1024, mb.MODE_ALLREDUCE, mb.ALGO_AUTO, False, 0),        # CTA pairs
+    (1024, 640, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, True, 128),   # CTA pairs, ragged n
+    (768, 1024, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 256),   # CTA pairs, two-shot
 ])
-def test_two_gpu_matches_oracle(m, n, k, mode, algo, det):
+def test_two_gpu_matches_oracle(m, n, k, mode, algo, det, tile_n):
     teams = _same_process_team([0, 1])
-    prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det, timeout_ns=5_000_000_000)
+    prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det, tile_n=tile_n,
+                      timeout_ns=5_000_000_000)
     call = TeamCall(teams, prob)
     a, b = inputs(7, 2, m, n, k)
     ad = [a[pe].to(f"cuda:{pe}") for pe in range(2)]

@@ -171,3 +171,50 @@ def test_locate_matches_product_schedule():
             if mode == 1:  # reduce-scatter: the owner holds the tile's rows
                 assert got[0] // (pl.m_tiles // n_pes) == got[2]
         assert len(seen) == pl.tiles
+
+
+def test_pair_schedule_matches_oracle_and_pairs_neighbours():
+    """CTA pairs: every pair ticket maps (product and oracle alike) to two
+    vertically adjacent 128-row tiles of one column, the upper one first, with
+    the same owner in reduce-scatter; the tickets cover every tile once."""
+    import megacu_b200 as mb
+    cases = [(4096, 8192, 1, 0, 0), (4096, 8192, 8, 0, 0), (8192, 8192, 8, 1, 0),
+             (4096, 8192, 2, 1, 0), (1024, 2000, 3, 0, 128), (2048, 512, 4, 1, 256),
+             (200, 264, 1, 0, 128)]
+    for m, n, n_pes, mode, tile_n in cases:
+        prob = mb.Problem(m, n, 64, mode=mode, tile_n=tile_n)
+        pl = mb.plan(prob, n_pes)
+        assert pl.cta_pairs and pl.gemm_units == pl.tiles // 2, (m, n, n_pes, mode)
+        seen = set()
+        for q in range(pl.gemm_units):
+            pair = mb.plan_pair(prob, n_pes, q)
+            assert pair == oracle_lib.pair_raster(n_pes, mode, q)
+            up, low = (mb.plan_tile(prob, n_pes, r) for r in pair)
+            assert up[0] % 2 == 0 and low[0] == up[0] + 1 and low[1] == up[1]
+            if mode == 1:
+                assert up[2] == low[2]
+            seen.add(up[0] * pl.n_tiles + up[1])
+            seen.add(low[0] * pl.n_tiles + low[1])
+        assert len(seen) == pl.tiles
+
+
+def test_pair_plan_choices():
+    import megacu_b200 as mb
+    # odd tile rows, tile_n 64 (decode shapes), or an odd per-PE row block: no pairs
+    for prob, n_pes in [(mb.Problem(384, 8192, 64), 1), (mb.Problem(16, 8192, 3584), 8),
+                        (mb.Problem(256, 512, 64, tile_n=64), 1),
+                        (mb.Problem(3072, 8192, 64, mode=mb.MODE_REDUCE_SCATTER), 8)]:
+        pl = mb.plan(prob, n_pes)
+        assert not pl.cta_pairs and pl.gemm_units == pl.tiles
+        prob.cta_pairs = mb.CTA_PAIRS_ON
+        with pytest.raises(mb.MegacuError) as err:
+            mb.plan(prob, n_pes)
+        assert err.value.detail == 27
+    prob = mb.Problem(4096, 8192, 1024, cta_pairs=mb.CTA_PAIRS_OFF)
+    pl = mb.plan(prob, 8)
+    assert not pl.cta_pairs and pl.gemm_units == pl.tiles
+    with pytest.raises(mb.MegacuError):
+        mb.plan_pair(prob, 8, 0)
+    prob.cta_pairs = 3
+    with pytest.raises(mb.MegacuError):
+        mb.plan(prob, 8)
