@@ -240,35 +240,59 @@ def run_gpu(args, rank, world, local_rank):
         if tp > 1:
             dist.barrier()
 
-    def timed_steps(body, steps, warmup):
+    def timed_steps(bodies, steps, warmup):
+        """Times each body `steps` times, interleaved step by step (body 0,
+        body 1, ..., then the next step), so that every arm sees the same
+        clocks and temperature; returns the mean ms per step of each body,
+        the max over ranks."""
         for _ in range(warmup):
-            align()
-            body()
+            for body in bodies:
+                align()
+                body()
         sync_all()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(steps)]
-        for s, e in ev:
-            align()
-            s.record(stream)
-            body()
-            e.record(stream)
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)] for _ in bodies]
+        for i in range(steps):
+            for body, evs in zip(bodies, ev):
+                align()
+                evs[i][0].record(stream)
+                body()
+                evs[i][1].record(stream)
         torch.cuda.synchronize()
-        ms = [s.elapsed_time(e) for s, e in ev]
-        total = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+        total = torch.tensor([sum(s.elapsed_time(e) for s, e in evs) for evs in ev],
+                             dtype=torch.float64, device=dev)
         if tp > 1:
             dist.all_reduce(total, op=dist.ReduceOp.MAX)
         sync_all()
-        return float(total.item()) / steps, ms
+        return [float(x) / steps for x in total.tolist()]
 
-    # ---- fused megakernel, inputs resident ----
-    # The clock sampler runs from the warm-up through the timed steps; a fixed
-    # number of untimed calls first (the same on every rank: each call is a
-    # collective) gives nvidia-smi time to sample the GPU under this load.
+    # ---- fused megakernel (inputs resident) and the unfused baseline ----
+    # Unfused baseline: cuBLAS GEMM, then NCCL allreduce of its output.
+    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def fused():
+        call(a, b)
+
+    def unfused():
+        torch.matmul(a, b, out=c)
+        if tp > 1:
+            dist.all_reduce(c)
+
+    def gemm_only():
+        torch.matmul(a, b, out=c)
+
+    # The clock sampler runs from the heat-up through the timed steps. The
+    # heat-up (a fixed number of untimed calls of both arms, the same on every
+    # rank: each call is a collective) brings the GPU to its power-capped
+    # steady state and gives nvidia-smi time to sample it under load; the
+    # arms are then timed interleaved.
     with ClockSampler(local_rank) as clocks:
         for _ in range(args.heat_calls):
-            call(a, b)
+            fused()
+            unfused()
         torch.cuda.synchronize()
-        ms_fused, _ = timed_steps(lambda: call(a, b), args.steps, args.warmup)
+        ms_fused, ms_unfused, ms_gemm = timed_steps([fused, unfused, gemm_only], args.steps,
+                                                    args.warmup)
     mb.events_status(events, stream)
     flops_total = 2.0 * M * N * K_TOTAL
     flops_rank = flops_total / tp
@@ -281,25 +305,9 @@ def run_gpu(args, rank, world, local_rank):
         call(a, b)
         out_host.copy_(out, non_blocking=True)
 
-    ms_e2e, _ = timed_steps(e2e_body, max(3, args.steps // 2), max(1, args.warmup // 2))
+    (ms_e2e,) = timed_steps([e2e_body], max(3, args.steps // 2), max(1, args.warmup // 2))
     h2d = a_host.numel() * 2 + b_host.numel() * 2
     d2h = out_host.numel() * 2
-
-    # ---- unfused baseline: cuBLAS GEMM then NCCL allreduce ----
-    c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-
-    def unfused():
-        torch.matmul(a, b, out=c)
-        if tp > 1:
-            dist.all_reduce(c)
-
-    # Same heat-up as the fused arm, so both run at the same power-capped clocks.
-    with ClockSampler(local_rank) as clocks_unfused:
-        for _ in range(args.heat_calls):
-            unfused()
-        torch.cuda.synchronize()
-        ms_unfused, _ = timed_steps(unfused, args.steps, args.warmup)
-        ms_gemm, _ = timed_steps(lambda: torch.matmul(a, b, out=c), args.steps, args.warmup)
 
     # ---- CPU baseline (rank 0, N = 1 only) ----
     cpu = None
@@ -352,8 +360,8 @@ def run_gpu(args, rank, world, local_rank):
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
                                     "tflops": flops_total / (ms_unfused * 1e-3) / 1e12,
-                                    "heat_calls": args.heat_calls,
-                                    "clocks": clocks_unfused.summary()},
+                                    "timing": "interleaved step by step with the fused "
+                                              "arm, after the same heat-up"},
             "clocks": clocks.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -368,7 +376,7 @@ def main():
     ap.add_argument("--impl", default="megacu_b200", choices=["megacu_b200", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--heat-calls", type=int, default=1500,
+    ap.add_argument("--heat-calls", type=int, default=1000,
                     help="untimed calls before the warm-up, while clocks are sampled")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -25,11 +25,13 @@ import oracle_lib  # noqa: E402
 from gpu_util import REL_TOL, f32, inputs, rel_error, wire_scale  # noqa: E402
 
 CASES = [
-    # m, n, k, mode, algo, deterministic
-    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False),
-    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False),
-    (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True),
-    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False),
+    # m, n, k, mode, algo, deterministic, tile_n (0 = auto)
+    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0),
+    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0),
+    (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True, 0),
+    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 0),
+    (1024, 1024, 128, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 128),  # CTA pairs
+    (1024, 512, 128, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, True, 256),  # pairs up to 4 PEs
 ]
 
 
@@ -42,10 +44,10 @@ def main() -> int:
     team = mb.Team(rank, world, local, 1 << 30, mb.torch_exchange())
     stream = torch.cuda.Stream()
     failures = []
-    for idx, (m, n, k, mode, algo, det) in enumerate(CASES):
+    for idx, (m, n, k, mode, algo, det, tile_n) in enumerate(CASES):
         if mode == mb.MODE_REDUCE_SCATTER and m % (world * 128):
             continue
-        prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det,
+        prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det, tile_n=tile_n,
                           timeout_ns=10_000_000_000)
         pl = mb.plan(prob, world)
         rows = m // world if mode == mb.MODE_REDUCE_SCATTER else m
