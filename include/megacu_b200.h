@@ -44,6 +44,25 @@ typedef struct megacu_status {
   const char *message; /* static string, never freed */
 } megacu_status;
 
+/*
+ * Detail numbers. megacu's own: 1 invalid problem or argument value,
+ * 2 missing storage or output pointer, 10 cudaSetDevice / device ordinal,
+ * 11 memset, 12 team barrier launch, 13 remote PEs without a megacu_b200 team,
+ * 14 kernel launch. B200 additions:
+ *   20 dtype is not bf16            21 n, k or a buffer not 16-byte aligned
+ *   22 unsupported size or tile     23 team size / PE index out of range
+ *   24 team handle does not match   25 buffer outside the symmetric heap
+ *   26 reduce-scatter m not a multiple of tp * 128
+ *   27 CTA pairs requested but the tile grid cannot hold them
+ *   30 cuTensorMapEncodeTiled failed
+ *   31 exporting the team heap (CUDA IPC), 32 peer handle of another team,
+ *   33 peer mapping (CUDA IPC / peer access), 34 symmetric heap exhausted
+ *   40 a cross-GPU wait timed out, 41 a local pipeline wait timed out
+ *      (megacu_b200_events_status)
+ *   50 built-in scratch address lookup, 51 more than one PE,
+ *   52 tile grid larger than the built-in scratch (megacu_cuda_gemm_bf16_noalloc)
+ */
+
 typedef struct megacu_launch_view {
   void *stream; /* cudaStream_t; NULL = validate only */
   int32_t device_ordinal;
