@@ -103,9 +103,10 @@ enum megacu_gemm_ar_mode {
 
 enum megacu_gemm_ar_algo {
   MEGACU_ALGO_AUTO = 0,
-  MEGACU_ALGO_ONE_SHOT = 1, /* every PE pushes its partial to every PE */
-  MEGACU_ALGO_TWO_SHOT = 2  /* push to the tile owner, owner reduces and
-                               pushes the sum to every PE */
+  MEGACU_ALGO_ONE_SHOT = 1, /* every PE reads every PE's partial of every
+                               tile and reduces it into its own out */
+  MEGACU_ALGO_TWO_SHOT = 2  /* the tile's owner reads every PE's partial,
+                               reduces, and stores the sum into every PE's out */
 };
 
 /* How GEMM tiles map to CTAs. With pairs, the two CTAs of a 2-CTA cluster

@@ -13,20 +13,22 @@
 //      warps 2..5  epilogue: TMEM -> registers -> bf16/fp32 -> this PE's own
 //                  partial slot, then publish (task 0's "after" hook); once
 //                  the GEMM queue is drained they join the workers below
-//      warps 6..9  workers: one raster-ordered queue of task-2 sub-tasks —
-//                  reduces (acquire, PE-order fp32 sum of every PE's partial
-//                  read over NVLink, store into this PE's out) and gathers
-//                  (copy finished blocks of tiles other PEs own from the
-//                  owner's out)
+//      warps 6..9  workers: one raster-ordered queue of task-2 sub-tasks
+//                  (acquire, PE-order fp32 sum of every PE's partial read
+//                  over NVLink, store into this PE's out, or into every PE's
+//                  out in two-shot allreduce)
+//    optionally as 2-CTA clusters whose pair computes 256-row tiles with
+//    cta_group::2 MMAs (kPair below);
 //  * the static tile_grid dispatcher (tile = blockIdx + i * gridDim,
 //    tile_grid_device.cuh:13-23) is replaced by device task queues: an
 //    atomic ticket per queue, tickets mapped to tiles by tile_schedule.h;
-//  * the event tensor is per (PE, tile, 32-row quarter) for partials and per
-//    (tile, quarter, 64-column block) for results, tagged with the call's
-//    epoch, published with st.release.sys after a fence and acquired with
-//    ld.acquire.sys under a bounded wait;
-//  * every byte crosses NVLink as a load by the consumer: producers write only
-//    their own memory (so their fences are cheap) and push 4-byte flags.
+//  * the event tensor holds one arrive flag per (PE, tile, 32-row quarter)
+//    and, for two-shot allreduce, one done flag per PE, tagged with the
+//    call's epoch, stored after a fence and acquired with ld.acquire.sys
+//    under a bounded wait;
+//  * every partial crosses NVLink as a load by its consumer: producers write
+//    only their own memory (so a GPU-scope fence covers them) and send 4-byte
+//    flags.
 //
 // No loads here use cluster multicast.
 #pragma once
