@@ -219,10 +219,18 @@ def run_gpu(args, rank, world, local_rank):
     ev_bytes = mb.events_bytes(prob, tp)
     heap = ws_bytes + ev_bytes + M * N * 2 + (64 << 20)
     exchange = mb.torch_exchange() if tp > 1 else None
-    team = mb.Team(rank, tp, local_rank, heap, exchange)
-    ws = team.tensor((max(ws_bytes, 16),), torch.uint8)
+    # Two-shot allreduce: workspace and out in a multicast region select the
+    # in-switch reduction (NVLS); without one the exchange uses peer loads.
+    want_mc = tp > 1 and not plan.one_shot
+    team = mb.Team(rank, tp, local_rank, heap, exchange,
+                   multicast_bytes=(ws_bytes + M * N * 2 + (1 << 20)) if want_mc else 0)
+    use_mc = want_mc and team.multicast
+    ws = team.tensor((max(ws_bytes, 16),), torch.uint8, multicast=use_mc)
     events = team.tensor((ev_bytes // 4,), torch.int32)
-    out = team.tensor((M, N), torch.bfloat16)
+    out = team.tensor((M, N), torch.bfloat16, multicast=use_mc)
+    exchange_kind = ("none" if tp == 1 else
+                     "in-switch reduction (NVLS multimem) + peer flags" if use_mc else
+                     "peer loads / stores over NVLink")
     out_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
@@ -321,15 +329,19 @@ def run_gpu(args, rank, world, local_rank):
     peak, peak_src = peaks()
     achieved = flops_rank / (ms_fused * 1e-3) / 1e12
     # North-star roofline: the slower of the GEMM at the measured peak and the
-    # bytes each PE must send over NVLink (two-shot: 2 (tp-1)/tp of the bf16
-    # output) at the measured 770 GB/s per direction.
+    # allreduce's bytes per PE over NVLink (its bus bytes, 2 (tp-1)/tp of the
+    # bf16 output: what a two-shot exchange over peer memory moves each way,
+    # and NCCL's busbw definition) at the measured 770 GB/s per direction.
+    # The in-switch reduction moves fewer bytes per PE, (1 + 1/tp) of the
+    # output each way; that figure is reported beside it.
     out_bytes = M * N * 2
     link_bytes = 2.0 * (tp - 1) / tp * out_bytes
+    switch_bytes = (1.0 + 1.0 / tp) * out_bytes if use_mc else None
     t_gemm_us = flops_rank / (peak * 1e12) * 1e6
     t_link_us = link_bytes / (NVLINK_GBS * 1e9) * 1e6
     t_roof_us = max(t_gemm_us, t_link_us)
     traffic = traffic_for(f"gemm_ar_megakernel_tp{tp}")
-    launches_per_step = 1 + (1 if tp > 1 else 0)
+    launches_per_step = 1  # the megakernel; the team barrier runs before each step's events
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
@@ -338,7 +350,8 @@ def run_gpu(args, rank, world, local_rank):
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "m": M, "n": N, "k_total": K_TOTAL, "k_per_pe": k,
                        "tp": tp, "parallelism": f"tp{tp}", "tile": [plan.tile_m, plan.tile_n],
-                       "one_shot": plan.one_shot,
+                       "one_shot": plan.one_shot, "cta_pairs": plan.cta_pairs,
+                       "exchange": exchange_kind,
                        "l2": "flushed (256 MiB write) before every timed step"},
             "us_per_call": ms_fused * 1e3,
             "tflops_per_gpu": achieved,
@@ -354,8 +367,10 @@ def run_gpu(args, rank, world, local_rank):
                               "gemm_us_at_peak": t_gemm_us, "link_bytes_per_pe": link_bytes,
                               "link_us_at_770GBps": t_link_us, "roofline_us": t_roof_us,
                               "frac": t_roof_us / (ms_fused * 1e3),
-                              "note": "slower of GEMM at measured peak and NVLink bytes at the "
-                                      "measured 770 GB/s per direction (900 nominal)"},
+                              "in_switch_link_bytes_per_pe": switch_bytes,
+                              "note": "slower of GEMM at the measured peak and the allreduce "
+                                      "bus bytes 2(tp-1)/tp x output at the measured 770 GB/s "
+                                      "per direction (900 nominal)"},
             "cpu_baseline": cpu,
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,

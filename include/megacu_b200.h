@@ -54,9 +54,14 @@ typedef struct megacu_status {
  *   24 team handle does not match   25 buffer outside the symmetric heap
  *   26 reduce-scatter m not a multiple of tp * 128
  *   27 CTA pairs requested but the tile grid cannot hold them
+ *   28 workspace / out in the multicast region of a call that cannot reduce
+ *      in the switch (not a two-shot bf16-wire allreduce, or only one of them)
  *   30 cuTensorMapEncodeTiled failed
  *   31 exporting the team heap (CUDA IPC), 32 peer handle of another team,
  *   33 peer mapping (CUDA IPC / peer access), 34 symmetric heap exhausted
+ *   35 no multicast region possible (device, driver, one PE, shared process)
+ *   36 multicast region set-up out of order, 37 multicast driver call,
+ *   38 multicast object export / hand-over
  *   40 a cross-GPU wait timed out, 41 a local pipeline wait timed out
  *      (megacu_b200_events_status)
  *   50 built-in scratch address lookup, 51 more than one PE,
@@ -314,7 +319,30 @@ megacu_status megacu_b200_team_info(void *team, int32_t *my_pe,
  * (megacu_gemm_allreduce_phased.cu:186-193) without a host synchronisation.
  */
 megacu_status megacu_b200_team_barrier(void *team, void *stream);
+/* Collective when the team has a multicast region (see below). */
 megacu_status megacu_b200_team_destroy(void *team);
+
+/*
+ * Optional multicast (NVLS) region of a connected team, one process per PE:
+ * each PE's own device memory bound to one NVSwitch multicast object, so the
+ * two-shot allreduce can reduce partials in the switch (multimem.ld_reduce)
+ * and store each sum into every PE at once (multimem.st). Collective set-up:
+ *   megacu_b200_team_multicast_export(team, bytes, mine)   every PE
+ *   exchange the MEGACU_B200_TEAM_HANDLE_BYTES blobs, PE order
+ *   megacu_b200_team_multicast_connect(team, all)          every PE
+ * `bytes` is rounded up to the multicast granularity (512 MiB on B200).
+ * PE 0 hands the object to the others over an abstract unix socket named in
+ * its blob. MEGACU_UNSUPPORTED (detail 35) when the device, driver or team
+ * shape (one PE, or PEs sharing a process) cannot have one; callers then use
+ * the heap alone. megacu_b200_team_multicast_malloc is the region's
+ * symmetric allocator (same order on every PE). Workspace and out of a
+ * two-shot bf16 allreduce placed here select the in-switch reduction.
+ */
+megacu_status megacu_b200_team_multicast_export(void *team, int64_t bytes, void *handle);
+megacu_status megacu_b200_team_multicast_connect(void *team, const void *handles);
+megacu_status megacu_b200_team_multicast_malloc(void *team, int64_t bytes, void **ptr);
+/* base = NULL and bytes = 0 when the team has no multicast region. */
+megacu_status megacu_b200_team_multicast_info(void *team, void **base, int64_t *bytes);
 
 /* ---- component link anchors (megacu src/*: last line of each file) ------- */
 

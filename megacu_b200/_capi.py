@@ -98,6 +98,11 @@ _PROTOTYPES = {
                   ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64)]),
     "megacu_b200_team_barrier": (Status, [c_void_p, c_void_p]),
     "megacu_b200_team_destroy": (Status, [c_void_p]),
+    "megacu_b200_team_multicast_export": (Status, [c_void_p, c_int64, c_void_p]),
+    "megacu_b200_team_multicast_connect": (Status, [c_void_p, c_void_p]),
+    "megacu_b200_team_multicast_malloc": (Status, [c_void_p, c_int64, ctypes.POINTER(c_void_p)]),
+    "megacu_b200_team_multicast_info":
+        (Status, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64)]),
     "megacu_dispatcher_explicit_attrs_component": (ctypes.c_int, []),
     "megacu_scheduler_explicit_asap_component": (ctypes.c_int, []),
     "megacu_platform_cuda_component": (ctypes.c_int, []),

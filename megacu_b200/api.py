@@ -74,10 +74,17 @@ class Team:
     handle in PE order — e.g. :func:`torch_exchange` over torch.distributed.
     Every PE must create the team and allocate from it in the same order
     (as with ``nvshmem_init`` / ``nvshmem_malloc``).
+
+    ``multicast_bytes > 0`` also sets up a multicast (NVLS) region of at least
+    that size (one process per PE; rounded up to the multicast granularity).
+    Where the device, driver or team shape cannot have one, the team works
+    without it (``self.multicast`` is False); every PE reaches the same
+    decision, since all see every PE's set-up blob.
     """
 
     def __init__(self, my_pe: int, n_pes: int, device: int, heap_bytes: int,
-                 exchange: Optional[Callable[[bytes], Sequence[bytes]]] = None):
+                 exchange: Optional[Callable[[bytes], Sequence[bytes]]] = None,
+                 multicast_bytes: int = 0):
         self.my_pe, self.n_pes, self.device = my_pe, n_pes, device
         handle = ctypes.c_void_p()
         check(lib().megacu_b200_team_create(my_pe, n_pes, device, heap_bytes,
@@ -98,20 +105,55 @@ class Team:
         check(lib().megacu_b200_team_info(self.handle, None, None, ctypes.byref(base),
                                           ctypes.byref(size)))
         self.heap_base, self.heap_bytes = base.value, size.value
+        self.multicast = False
+        self.multicast_error = None
+        if multicast_bytes > 0 and n_pes > 1:
+            self._connect_multicast(multicast_bytes, exchange)
+
+    def _connect_multicast(self, nbytes: int, exchange) -> None:
+        mine = ctypes.create_string_buffer(_capi.TEAM_HANDLE_BYTES)
+        st = lib().megacu_b200_team_multicast_export(self.handle, nbytes, mine)
+        if st.code != _capi.OK:
+            self.multicast_error = MegacuError(st)
+        handles = list(exchange(mine.raw if st.code == _capi.OK else
+                                bytes(_capi.TEAM_HANDLE_BYTES)))
+        # A PE that could not export sends zeros: then nobody connects.
+        if any(not any(h[:4]) for h in handles):
+            if self.multicast_error is None:
+                self.multicast_error = RuntimeError("a peer cannot set up a multicast region")
+            return
+        blob = ctypes.create_string_buffer(b"".join(handles), self.n_pes * _capi.TEAM_HANDLE_BYTES)
+        st = lib().megacu_b200_team_multicast_connect(self.handle, blob)
+        if st.code != _capi.OK:
+            self.multicast_error = MegacuError(st)
+            return
+        base = ctypes.c_void_p()
+        size = ctypes.c_int64()
+        check(lib().megacu_b200_team_multicast_info(self.handle, ctypes.byref(base),
+                                                    ctypes.byref(size)))
+        self.multicast = size.value > 0
+        self.multicast_base, self.multicast_bytes = base.value, size.value
 
     def malloc(self, nbytes: int) -> int:
         ptr = ctypes.c_void_p()
         check(lib().megacu_b200_team_malloc(self.handle, nbytes, ctypes.byref(ptr)))
         return ptr.value
 
-    def tensor(self, shape, dtype):
-        """A torch tensor over a fresh symmetric allocation (zero-filled heap)."""
+    def multicast_malloc(self, nbytes: int) -> int:
+        ptr = ctypes.c_void_p()
+        check(lib().megacu_b200_team_multicast_malloc(self.handle, nbytes, ctypes.byref(ptr)))
+        return ptr.value
+
+    def tensor(self, shape, dtype, multicast: bool = False):
+        """A torch tensor over a fresh symmetric allocation (zero-filled), in
+        the heap or, with ``multicast=True``, in the multicast region."""
         import torch
         numel = 1
         for s in shape:
             numel *= s
         itemsize = torch.empty((), dtype=dtype).element_size()
-        ptr = self.malloc(max(numel * itemsize, 16))
+        nbytes = max(numel * itemsize, 16)
+        ptr = self.multicast_malloc(nbytes) if multicast else self.malloc(nbytes)
         return tensor_from_pointer(ptr, shape, dtype, self.device, owner=self)
 
     def barrier(self, stream=None) -> None:

@@ -264,6 +264,7 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
     return fail(MEGACU_INVALID_ARGUMENT, 23, "team_my_pe out of range");
   }
   team_impl *team = nullptr;
+  bool via_switch = false;
   if (n_pes > 1) {
     team = as_team(driver.team.team);
     if (team == nullptr) {
@@ -274,11 +275,24 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
     }
     bool const out_symmetric = problem.mode == MEGACU_MODE_ALLREDUCE && !pl.one_shot;
     std::int64_t const out_bytes = problem.m * problem.n * 2;
-    if (!team->contains(workspace, pl.workspace_bytes) ||
+    // Workspace and out in the multicast region select the in-switch
+    // reduction, which exists for the two-shot bf16-wire allreduce only.
+    bool const ws_mc = team->mc.contains(workspace, pl.workspace_bytes);
+    bool const out_mc = team->mc.contains(out, out_bytes);
+    if (ws_mc || out_mc) {
+      if (!ws_mc || !out_mc || !out_symmetric || pl.wire_bytes != 2) {
+        return fail(MEGACU_UNSUPPORTED, 28,
+                    "in-switch reduction needs workspace and out both in the multicast region "
+                    "and a two-shot allreduce with the bf16 wire");
+      }
+      via_switch = true;
+    }
+    if (!(ws_mc || team->contains(workspace, pl.workspace_bytes)) ||
         !team->contains(events, pl.events_bytes) ||
-        (out_symmetric && !team->contains(out, out_bytes))) {
+        (out_symmetric && !(out_mc || team->contains(out, out_bytes)))) {
       return fail(MEGACU_INVALID_ARGUMENT, 25,
-                  "workspace, events (and two-shot out) must lie in the team's symmetric heap");
+                  "workspace, events (and two-shot out) must lie in the team's symmetric heap "
+                  "(workspace and out may lie in its multicast region)");
     }
   }
   if (!megacu::cuda::has_stream(megacu::cuda::launch_view{driver.launch.stream,
@@ -322,6 +336,10 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   prm.out = static_cast<__nv_bfloat16 *>(out);
   prm.workspace = static_cast<char *>(workspace);
   prm.events = static_cast<std::uint32_t *>(events);
+  if (via_switch) {
+    prm.mc_workspace = team->mc.alias(workspace);
+    prm.mc_out = reinterpret_cast<__nv_bfloat16 *>(team->mc.alias(out));
+  }
   if (team != nullptr) {
     prm.peers = team->peers;
   } else {
@@ -921,6 +939,9 @@ extern "C" megacu_status megacu_b200_team_destroy(void *team) {
   if (t == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing team");
   cudaSetDevice(t->device);
   cudaDeviceSynchronize();
+  if (t->mc.have_memory || t->mc.have_object) {
+    release_multicast(t);  // collective when the region is ready
+  }
   for (int pe = 0; pe < t->n_pes; ++pe) {
     if (t->opened[pe]) cudaIpcCloseMemHandle(t->peers.base[pe]);
   }

@@ -93,6 +93,10 @@ struct gemm_ar_params {
   __nv_bfloat16 *out;         // this PE's output
   char *workspace;            // this PE's partial slots (symmetric)
   std::uint32_t *events;      // this PE's events buffer (symmetric)
+  // In-switch reduction (two-shot bf16 allreduce with workspace and out in
+  // the team's multicast region): their multicast addresses; else null.
+  char *mc_workspace;
+  __nv_bfloat16 *mc_out;
   megacu::nvshmem::peer_table peers;
   unsigned long long *trace;
   std::int64_t trace_capacity;
@@ -279,6 +283,18 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
           acc[h / 2][(h % 2) * 4 + 3] += __uint_as_float(w[h].w);
         }
       }
+    } else if (p.mc_workspace != nullptr) {
+      // One load per vector returns the sum over every PE's slot, reduced in
+      // the NVSwitch (fp32 accumulation, one bf16 rounding): the bf16 values
+      // are exact in fp32, so the packing below reproduces them.
+      char const *mc = p.mc_workspace + in_slot;
+      uint4 w[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        w[g] = ptx::multimem_ld_reduce_bf16x8(mc + (cb * 8 + g) * kVecStride);
+      }
+#pragma unroll
+      for (int g = 0; g < 8; ++g) add_bf16x8(acc[g], w[g]);
     } else {
 #pragma unroll 1
       for (std::int32_t src = 0; src < p.n_pes; src += 2) {
@@ -318,18 +334,25 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
         p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
     std::int32_t const g = lane % 8;
     std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
-    // Every PE's out in two-shot allreduce (starting with the next PE, so the
-    // PEs spread their stores over the links), this PE's out otherwise.
-    std::int32_t const n_out = push_all ? p.n_pes : 1;
+    // Every PE's out in two-shot allreduce (one multicast store each with
+    // the in-switch reduction; else starting with the next PE, so the PEs
+    // spread their stores over the links), this PE's out otherwise.
+    bool const via_switch = !kWireF32 && p.mc_out != nullptr;
+    std::int32_t const n_out = push_all && !via_switch ? p.n_pes : 1;
     for (std::int32_t d = 0; d < n_out; ++d) {
       std::int32_t const pe = push_all ? (p.my_pe + 1 + d) % p.n_pes : p.my_pe;
-      __nv_bfloat16 *dst = push_all ? p.peers.translate(p.out, pe) : p.out;
+      __nv_bfloat16 *dst = via_switch ? p.mc_out : push_all ? p.peers.translate(p.out, pe) : p.out;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
         uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
         if (row0 + rr < p.m && col < p.n) {
-          ptx::st_v4(dst + static_cast<std::int64_t>(out_row0 + rr) * p.n + col, q);
+          __nv_bfloat16 *at = dst + static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
+          if (via_switch) {
+            ptx::multimem_st_v4(at, q);
+          } else {
+            ptx::st_v4(at, q);
+          }
         }
       }
     }
@@ -344,13 +367,17 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
 }
 
 // Two-shot allreduce completion. Each worker warp, once the reduce queue is
-// empty, fences its stores at system scope (they went to every PE's out) and
+// empty, fences its stores at system scope (they went to every PE's out,
+// directly or through the multicast object) and
 // counts itself done; the last worker of this PE then sets done[p][my_pe] on
 // every PE. One system-scope fence per warp per call instead of one per block.
 __device__ __forceinline__ void finish_pushes(gemm_ar_params const &p, std::uint32_t parity,
                                               std::uint32_t epoch, std::uint32_t *my_events,
                                               std::uint32_t lane) {
   control_block *ctrl = control(p);
+  if (p.mc_out != nullptr) {
+    ptx::fence_proxy_alias();  // the stores went through the multicast mapping
+  }
   ptx::fence_acq_rel_sys();
   __syncwarp();
   std::uint32_t last = 0;

@@ -77,6 +77,33 @@ __device__ __forceinline__ void publish_local_data(std::uint32_t *flag, std::uin
   st_relaxed_sys(flag, v);
 }
 
+// ---- NVSwitch multicast (multimem) ----------------------------------------------
+// `mc` must be an address in a multicast mapping (a team's multicast region).
+
+// The sum over every PE's copy of 16 bytes (8 bf16) at `mc`, reduced in the
+// switch with fp32 accumulation and rounded to bf16 once.
+__device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(void const *mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
+// Stores 16 bytes into every PE's copy at `mc`.
+__device__ __forceinline__ void multimem_st_v4(void *mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};"
+               :: "l"(mc), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Orders this thread's accesses made through one virtual mapping of a
+// location (the multicast one) with those made through another (unicast).
+__device__ __forceinline__ void fence_proxy_alias() {
+  asm volatile("fence.proxy.alias;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_barrier_sync(std::uint32_t id, std::uint32_t threads) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
 }

@@ -9,6 +9,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <thread>
 
 #include <megacu/backends/nvshmem.h>
 
@@ -17,6 +18,35 @@ namespace megacu_b200 {
 inline constexpr std::uint32_t kTeamMagic = 0x6d636274u;
 // The first bytes of every heap are reserved for host-driven team barriers.
 inline constexpr std::int64_t kTeamReservedBytes = 4096;
+
+// Optional multicast (NVLS) region: this PE's own device memory bound to a
+// multicast object that every PE of the team bound its memory to. A store
+// through `multi` (multimem.st) reaches every PE's copy; a multimem.ld_reduce
+// through it returns the sum over all PEs' copies, reduced in the NVSwitch.
+// Allocations are symmetric (same offset on every PE), like the heap's.
+struct multicast_region {
+  bool ready = false;                // bound and mapped on every PE
+  std::int64_t bytes = 0;            // a multiple of the multicast granularity
+  std::int64_t granularity = 0;
+  std::int64_t used = 0;
+  unsigned long long object = 0;     // the multicast object (CUmemGenericAllocationHandle)
+  unsigned long long memory = 0;     // this PE's physical memory bound to it
+  char *local = nullptr;             // unicast mapping of this PE's memory
+  char *multi = nullptr;             // multicast mapping (multimem.* only)
+  bool have_object = false, have_memory = false, bound = false;
+  bool local_mapped = false, multi_mapped = false;
+  int export_fd = -1;                // PE 0: the object's shareable file descriptor
+  int listen_fd = -1;                // PE 0: socket that hands export_fd to the peers
+  std::thread server;                // PE 0: serves export_fd during set-up
+  char socket_name[64] = {};
+
+  bool contains(void const *p, std::int64_t n) const {
+    auto const *c = static_cast<char const *>(p);
+    return ready && c >= local && n >= 0 && c + n <= local + bytes;
+  }
+  // The multicast address of a pointer into this PE's region.
+  char *alias(void const *p) const { return multi + (static_cast<char const *>(p) - local); }
+};
 
 struct team_impl {
   std::uint32_t magic = kTeamMagic;
@@ -30,6 +60,7 @@ struct team_impl {
   bool opened[megacu::nvshmem::max_team_pes] = {};
   megacu::nvshmem::peer_table peers;
   std::uint32_t barrier_epoch = 0;  // team barriers issued so far
+  multicast_region mc;
   std::mutex mu;
 
   bool contains(void const *p, std::int64_t bytes) const {
@@ -37,6 +68,11 @@ struct team_impl {
     return c >= heap && bytes >= 0 && c + bytes <= heap + heap_bytes;
   }
 };
+
+// Releases the multicast region (multicast.cu). Collective when the region
+// is ready: it first meets every PE at a team barrier, so no PE unbinds its
+// memory while another may still reach it through the multicast object.
+void release_multicast(team_impl *t);
 
 inline team_impl *as_team(void *handle) {
   auto *t = static_cast<team_impl *>(handle);

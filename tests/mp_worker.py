@@ -25,14 +25,19 @@ import oracle_lib  # noqa: E402
 from gpu_util import REL_TOL, f32, inputs, rel_error, wire_scale  # noqa: E402
 
 CASES = [
-    # m, n, k, mode, algo, deterministic, tile_n (0 = auto)
-    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0),
-    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0),
-    (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True, 0),
-    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 0),
-    (1024, 1024, 128, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 128),  # CTA pairs
-    (1024, 512, 128, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, True, 256),  # pairs up to 4 PEs
+    # m, n, k, mode, algo, deterministic, tile_n (0 = auto), in the multicast region
+    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0, False),
+    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0, False),
+    (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, True, 0, False),
+    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 0, False),
+    (1024, 1024, 128, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 128, False),  # CTA pairs
+    (1024, 512, 128, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, True, 256, False),  # pairs to 4 PEs
+    # in-switch reduction (workspace and out in the multicast region)
+    (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0, True),
+    (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0, True),  # ragged m, n
+    (768, 1024, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 256, True),  # CTA pairs
 ]
+MULTICAST_BYTES = 1 << 29
 
 
 def main() -> int:
@@ -41,19 +46,24 @@ def main() -> int:
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
-    team = mb.Team(rank, world, local, 1 << 30, mb.torch_exchange())
+    team = mb.Team(rank, world, local, 1 << 30, mb.torch_exchange(),
+                   multicast_bytes=MULTICAST_BYTES)
     stream = torch.cuda.Stream()
     failures = []
-    for idx, (m, n, k, mode, algo, det, tile_n) in enumerate(CASES):
+    if not team.multicast:
+        failures.append(f"no multicast region: {team.multicast_error}")
+    for idx, (m, n, k, mode, algo, det, tile_n, mc) in enumerate(CASES):
         if mode == mb.MODE_REDUCE_SCATTER and m % (world * 128):
+            continue
+        if mc and not team.multicast:
             continue
         prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det, tile_n=tile_n,
                           timeout_ns=10_000_000_000)
         pl = mb.plan(prob, world)
         rows = m // world if mode == mb.MODE_REDUCE_SCATTER else m
-        ws = team.tensor((max(mb.workspace_bytes(prob, world), 16),), torch.uint8)
+        ws = team.tensor((max(mb.workspace_bytes(prob, world), 16),), torch.uint8, multicast=mc)
         ev = team.tensor((mb.events_bytes(prob, world) // 4,), torch.int32)
-        out = team.tensor((rows, n), torch.bfloat16)
+        out = team.tensor((rows, n), torch.bfloat16, multicast=mc)
         a, b = inputs(100 + idx, world, m, n, k)
         ad, bd = a[rank].cuda(), b[rank].cuda()
         ev0 = [np.zeros(oracle_lib.event_tensor_words(world, pl.tiles), np.uint32)
@@ -81,6 +91,22 @@ def main() -> int:
         if counters != (2 * ref["counters"][rank]).tolist():
             failures.append(f"case {idx}: counters {counters} != {2 * ref['counters'][rank]}")
         dist.barrier()
+    if team.multicast:
+        # Buffers in the multicast region of a call that cannot reduce in the
+        # switch (one-shot) are refused before any launch.
+        prob = mb.Problem(64, 2048, 64, algo=mb.ALGO_ONE_SHOT)
+        ws = team.tensor((mb.workspace_bytes(prob, world),), torch.uint8, multicast=True)
+        ev = team.tensor((mb.events_bytes(prob, world) // 4,), torch.int32)
+        out = team.tensor((64, 2048), torch.bfloat16, multicast=True)
+        a = torch.zeros(64, 64, dtype=torch.bfloat16, device="cuda")
+        b = torch.zeros(64, 2048, dtype=torch.bfloat16, device="cuda")
+        try:
+            mb.gemm_allreduce(a, b, out, workspace=ws, events=ev, problem=prob, stream=stream,
+                              device=local, team=team)
+            failures.append("one-shot call with multicast buffers was not refused")
+        except mb.MegacuError as err:
+            if err.detail != 28:
+                failures.append(f"one-shot call with multicast buffers: {err}")
     torch.cuda.synchronize()
     dist.barrier()
     team.close()
