@@ -149,8 +149,12 @@ typedef struct megacu_gemm_ar_problem_v2 {
   int32_t num_ctas;      /* 0 = one persistent CTA per SM */
   int32_t cta_pairs;     /* enum megacu_cta_pairs */
   uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 10 s */
-  uint64_t *trace;       /* optional device buffer of trace records
-                            (4 x uint64 each), NULL = off */
+  uint64_t *trace;       /* optional device buffer of trace records, NULL =
+                            off: 4 x uint64 {kind | sub << 8 | CTA << 16 |
+                            ticket << 32, tile, start ns, end ns}; kinds 0
+                            GEMM tile epilogue, 2 reduce sub-task, 3 worker
+                            completion fence, 4 done flags stored, 5 wait
+                            for every PE's done flag */
   int64_t trace_capacity; /* records that fit in `trace` */
 } megacu_gemm_ar_problem_v2;
 

@@ -129,6 +129,11 @@ __device__ __forceinline__ void count(gemm_ar_params const &p, int which,
   atomicAdd(&control(p)->counters[which], v);
 }
 
+// Optional trace record {kind | sub << 8 | CTA << 16 | ticket << 32, tile,
+// start ns, end ns} (%globaltimer). Kinds: 0 GEMM tile (epilogue span),
+// 2 reduce sub-task (after its acquire), 3 a worker's completion fence
+// (ticket = its place among the finished workers), 4 this PE's done flags
+// stored, 5 the wait for every PE's done flag.
 __device__ __forceinline__ void trace(gemm_ar_params const &p, std::uint32_t kind,
                                       std::uint32_t sub, std::uint32_t ticket,
                                       std::uint32_t tile, std::uint64_t t0) {
@@ -375,6 +380,7 @@ __device__ __forceinline__ void finish_pushes(gemm_ar_params const &p, std::uint
                                               std::uint32_t epoch, std::uint32_t *my_events,
                                               std::uint32_t lane) {
   control_block *ctrl = control(p);
+  std::uint64_t const t0 = ptx::now_ns();
   if (p.mc_out != nullptr) {
     ptx::fence_proxy_alias();  // the stores went through the multicast mapping
   }
@@ -383,16 +389,21 @@ __device__ __forceinline__ void finish_pushes(gemm_ar_params const &p, std::uint
   std::uint32_t last = 0;
   if (lane == 0) {
     std::uint32_t const total = gridDim.x * kWorkerWarps;
-    last = atomicAdd(&ctrl->workers_done, 1u) == total - 1 ? 1u : 0u;
+    std::uint32_t const done = atomicAdd(&ctrl->workers_done, 1u);
+    last = done == total - 1 ? 1u : 0u;
+    trace(p, 3, 0, done, 0, t0);
   }
   if (__shfl_sync(0xffffffffu, last, 0) == 0) {
     return;
   }
+  std::uint64_t const t1 = ptx::now_ns();
   ptx::fence_acq_rel_sys();
   if (static_cast<std::int32_t>(lane) < p.n_pes) {
     std::uint32_t *flags = p.peers.translate(my_events, lane);
     ptx::st_relaxed_sys(flags + done_index(parity, p.my_pe, p.n_pes, p.tiles), epoch);
   }
+  __syncwarp();
+  if (lane == 0) trace(p, 4, 0, 0, 0, t1);
 }
 
 // Two-shot allreduce: this PE's out is complete once every PE has announced
@@ -403,13 +414,17 @@ __device__ __forceinline__ void wait_all_pushes(gemm_ar_params const &p, std::ui
                                                 std::uint32_t const *abort_word,
                                                 std::uint32_t lane) {
   bool ok = true;
+  std::uint64_t const t0 = ptx::now_ns();
   if (static_cast<std::int32_t>(lane) < p.n_pes) {
     ok = wait_flag(my_events + done_index(parity, lane, p.n_pes, p.tiles), epoch, abort_word,
                    p.timeout_ns);
     if (!ok) record_error(p, err_remote_timeout, 0xffffffffu, lane, 9);
   }
   bool const all = __all_sync(0xffffffffu, ok);
-  if (lane == 0 && all) count(p, ctr_final_acquire, p.n_pes);
+  if (lane == 0 && all) {
+    count(p, ctr_final_acquire, p.n_pes);
+    trace(p, 5, 0, 0, 0, t0);
+  }
 }
 
 }  // namespace detail
