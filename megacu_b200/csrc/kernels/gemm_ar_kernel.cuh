@@ -87,7 +87,7 @@ struct gemm_ar_params {
   std::int32_t one_shot;      // 1: every PE reduces every tile
   std::int32_t group_m;
   std::int32_t n_comm;        // communication sub-tasks (tiles x quarters x blocks)
-  std::int32_t reserved;
+  std::int32_t comm_warps;    // warps per CTA running them: the last comm_warps of 2..9
   std::int32_t rows_per_pe;   // reduce-scatter: output rows per PE
   std::uint64_t timeout_ns;   // bound of cross-GPU waits
   __nv_bfloat16 *out;         // this PE's output
@@ -388,7 +388,7 @@ __device__ __forceinline__ void finish_pushes(gemm_ar_params const &p, std::uint
   __syncwarp();
   std::uint32_t last = 0;
   if (lane == 0) {
-    std::uint32_t const total = gridDim.x * kWorkerWarps;
+    std::uint32_t const total = gridDim.x * static_cast<std::uint32_t>(p.comm_warps);
     std::uint32_t const done = atomicAdd(&ctrl->workers_done, 1u);
     last = done == total - 1 ? 1u : 0u;
     trace(p, 3, 0, done, 0, t0);
@@ -835,15 +835,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- workers: reduce (task 2) ----------------
-  // Worker warps start at once; epilogue warps join once the GEMM queue is
-  // drained, so the last GEMM wave's reductions use both groups.
-  if (p.n_pes > 1 && warp >= kEpilogueWarp0) {
+  // Worker warps start at once; with comm_warps > 4 epilogue warps join once
+  // the GEMM queue is drained, so the last GEMM wave's reductions use both.
+  // `comm_warps` bounds how many requests a CTA keeps in flight over NVLink:
+  // more only deepen the fabric's queues once it is saturated.
+  int const first_comm_warp = kThreads / 32 - p.comm_warps;
+  if (p.n_pes > 1 && warp >= first_comm_warp) {
     int const worker = warp - kEpilogueWarp0;  // 0..7
     std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
     detail::comm_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
     if (p.mode == mode_allreduce && !p.one_shot) {
       detail::finish_pushes(p, parity, epoch, my_events, lane);
-      if (blockIdx.x == 0 && worker == 0) {
+      if (blockIdx.x == 0 && warp == first_comm_warp) {
         detail::wait_all_pushes(p, parity, epoch, my_events, abort_word, lane);
       }
     }

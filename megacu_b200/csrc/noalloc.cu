@@ -155,6 +155,7 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
   prm.my_pe = 0;
   prm.mode = mode_allreduce;
   prm.group_m = info[6];
+  prm.comm_warps = kWorkerWarps;  // unused with one PE
   prm.rows_per_pe = prm.m;
   prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
   prm.out = static_cast<__nv_bfloat16 *>(out);
