@@ -149,7 +149,7 @@ struct bf16_plan {
 };
 
 constexpr std::int32_t kPlanSms = 148;  // plans must not depend on the local device
-constexpr std::int32_t kSwitchCommWarps = 2;
+constexpr std::int32_t kSwitchCommWarps = 1;
 
 megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, bf16_plan &out) {
   if (p.m <= 0 || p.n <= 0 || p.k <= 0) {
@@ -333,11 +333,11 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
       n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
   prm.n_comm = reduced_tiles * kQuarters * (pl.tile_n / 64);
   // Warps per CTA running exchange sub-tasks. The in-switch reduction
-  // saturates the fabric with 2 per SM; more only lengthen its queues and
+  // saturates the fabric with one per SM; more only lengthen its queues and
   // with them every sub-task's latency and the drain at the end (tp = 8, C2:
-  // 194.6 us with 2, 201.7 with 3, 209.9 with 4, 223.7 with 8). Peer loads
-  // and stores need more in flight (240.6 us with 4 or 6, 244.7 with 8,
-  // 279.5 with 2).
+  // 184.3 us with 1, 195.0 with 2, 201.7 with 3, 209.9 with 4, 223.7 with
+  // 8). Peer loads and stores need more in flight (240.6 us with 4 or 6,
+  // 244.7 with 8, 279.5 with 2).
   prm.comm_warps = via_switch ? kSwitchCommWarps : kWorkerWarps;
   prm.rows_per_pe = static_cast<std::int32_t>(problem.m / n_pes);
   prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
