@@ -1,0 +1,19 @@
+"""The timeline tool's summary of trace records (no GPU: synthetic records)."""
+import numpy as np
+
+from megacu_b200 import timeline
+
+
+def test_summary_reads_every_kind_relative_to_first_event():
+    # kind, start ns, end ns
+    recs = [(0, 1000, 5000), (0, 3000, 9000), (2, 4000, 20000), (2, 6000, 30000),
+            (3, 21000, 40000), (3, 31000, 41000), (4, 41000, 42000), (5, 35000, 43000)]
+    tr = {"kind": np.array([r[0] for r in recs], np.int64),
+          "t0": np.array([r[1] for r in recs], np.uint64),
+          "t1": np.array([r[2] for r in recs], np.uint64)}
+    s = timeline._summary(tr, np)
+    assert s["gemm_tiles"] == 2 and s["gemm_end_us"] == 8.0 and s["gemm_end_p50_us"] == 6.0
+    assert s["reduce_tasks"] == 2 and s["reduce_first_start_us"] == 3.0
+    assert s["reduce_end_us"] == 29.0 and s["reduce_task_p50_us"] == 20.0
+    assert s["fence_start_us"] == [20.0, 30.0] and s["fence_end_us"] == [39.0, 40.0]
+    assert s["done_flags_end_us"] == [41.0, 41.0] and s["final_wait_start_us"] == [34.0, 34.0]
