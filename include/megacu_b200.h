@@ -198,6 +198,65 @@ megacu_status megacu_cuda_gemm_reduce_scatter_bf16(
     megacu_driver_view driver, const void *a, const void *b, void *workspace,
     void *out, void *events, megacu_gemm_ar_problem_v2 problem);
 
+/* ---- tensor-parallel MLP blocks (new, no counterpart in
+ *      megacu) -------------------------------------------------------------- */
+
+/*
+ * Column-parallel gate/up projection with the SwiGLU epilogue, one PE:
+ * act[m, n] = bf16(silu(x @ w_gate) * (x @ w_up)), the products accumulated in
+ * fp32 and the epilogue computed in fp32 (silu(g) = g / (1 + exp(-g))).
+ * x: row-major [m, k]; w_gate, w_up: row-major [k, n] (this PE's column
+ * slice); act: row-major [m, n], local. problem.m = tokens, n = this PE's
+ * intermediate columns, k = hidden; tile_n must be 0 (auto: 128 act columns,
+ * i.e. 128 gate + 128 up accumulator columns per tile). events: >=
+ * megacu_b200_swiglu_events_bytes(), local, zero-filled once.
+ */
+megacu_status megacu_cuda_gemm_swiglu_bf16(
+    megacu_driver_view driver, const void *x, const void *w_gate, const void *w_up,
+    void *act, void *events, megacu_gemm_ar_problem_v2 problem);
+megacu_status megacu_b200_swiglu_events_bytes(megacu_gemm_ar_problem_v2 problem,
+                                              int64_t *bytes);
+
+typedef struct megacu_mlp_chain_problem {
+  int64_t tokens;        /* rows of x and of every block's output */
+  int64_t hidden;        /* columns of x; multiple of 8 */
+  int64_t inter;         /* this PE's slice of the intermediate size; multiple of 8 */
+  int32_t layers;        /* MLP blocks, 1..64 */
+  int32_t algo;          /* allreduce algo of the down projection */
+  int32_t deterministic; /* as in megacu_gemm_ar_problem_v2 */
+  int32_t num_ctas;      /* 0 = one persistent CTA per SM */
+  int32_t cta_pairs;     /* enum megacu_cta_pairs, both launches of a block */
+  int32_t reserved;
+  uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 10 s */
+} megacu_mlp_chain_problem;
+
+/*
+ * Buffer sizes of megacu_cuda_mlp_chain_bf16 on `n_pes` PEs: sizes[0] act
+ * (local), [1] workspace (symmetric), [2] events_swiglu (local), [3]
+ * events_down (symmetric), [4] x_work (like out).
+ */
+megacu_status megacu_b200_mlp_chain_sizes(megacu_mlp_chain_problem problem, int32_t n_pes,
+                                          int64_t sizes[5]);
+
+/*
+ * `layers` tensor-parallel MLP blocks back to back, every PE collectively:
+ *   act = silu(x_l @ w_gate[l]) * (x_l @ w_up[l])           (local)
+ *   x_{l+1} = sum over PEs of act @ w_down[l]               (fused allreduce)
+ * x_0 = x: row-major [tokens, hidden], local. w_gate[l], w_up[l]: [hidden,
+ * inter]; w_down[l]: [inter, hidden] (host arrays of `layers` device
+ * pointers to this PE's slices). The blocks' outputs alternate between out
+ * and x_work so that the last one lands in out; both are placed like the
+ * out of megacu_cuda_gemm_allreduce_bf16 (symmetric for two-shot; in the
+ * team's multicast region, together with workspace, for the in-switch
+ * reduction). Two launches per block: megacu_cuda_gemm_swiglu_bf16, then
+ * megacu_cuda_gemm_allreduce_bf16.
+ */
+megacu_status megacu_cuda_mlp_chain_bf16(
+    megacu_driver_view driver, const void *x, const void *const *w_gate,
+    const void *const *w_up, const void *const *w_down, void *act, void *workspace,
+    void *x_work, void *out, void *events_swiglu, void *events_down,
+    megacu_mlp_chain_problem problem);
+
 /*
  * Orchestrated entry: builds megacu's three-task phase (GEMM tile producer
  * with tile_grid + publish, sync with join, reduce consumer with acquire),

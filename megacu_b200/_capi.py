@@ -64,8 +64,24 @@ class GemmArProblemV2(ctypes.Structure):
                 ("trace_capacity", c_int64)]
 
 
+class MlpChainProblem(ctypes.Structure):
+    _fields_ = [("tokens", c_int64), ("hidden", c_int64), ("inter", c_int64),
+                ("layers", c_int32), ("algo", c_int32), ("deterministic", c_int32),
+                ("num_ctas", c_int32), ("cta_pairs", c_int32), ("reserved", c_int32),
+                ("timeout_ns", c_uint64)]
+
+
 _PROTOTYPES = {
     # name: (restype, argtypes)
+    "megacu_cuda_gemm_swiglu_bf16":
+        (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
+    "megacu_b200_swiglu_events_bytes": (Status, [GemmArProblemV2, ctypes.POINTER(c_int64)]),
+    "megacu_b200_mlp_chain_sizes":
+        (Status, [MlpChainProblem, c_int32, ctypes.POINTER(c_int64)]),
+    "megacu_cuda_mlp_chain_bf16":
+        (Status, [DriverView, c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p),
+                  ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                  c_void_p, MlpChainProblem]),
     "megacu_cuda_gemm_allreduce_phased_f32":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblem]),
     "megacu_cuda_gemm_allreduce_f32_orchestrate":

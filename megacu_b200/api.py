@@ -321,6 +321,71 @@ def gemm_reduce_scatter(a, b, out, *, workspace, events, problem: Problem, **kw)
     gemm_allreduce(a, b, out, workspace=workspace, events=events, problem=problem, **kw)
 
 
+# ---- tensor-parallel MLP blocks ----------------------------------
+
+def swiglu_events_bytes(problem: Problem) -> int:
+    out = ctypes.c_int64()
+    check(lib().megacu_b200_swiglu_events_bytes(problem.to_c(), ctypes.byref(out)))
+    return out.value
+
+
+def gemm_swiglu(x, w_gate, w_up, act, *, events, problem: Problem, stream=None,
+                device: int = 0, trace=None) -> None:
+    """act = silu(x @ w_gate) * (x @ w_up) (one PE, async). ``problem``: m =
+    tokens, n = act columns, k = hidden."""
+    trace_ptr = _ptr(trace)
+    cap = trace.numel() // 4 if trace is not None else 0
+    check(lib().megacu_cuda_gemm_swiglu_bf16(driver_view(stream, device), _ptr(x), _ptr(w_gate),
+                                             _ptr(w_up), _ptr(act), _ptr(events),
+                                             problem.to_c(trace_ptr, cap)))
+
+
+@dataclass
+class MlpChainProblem:
+    """megacu_mlp_chain_problem: ``layers`` blocks x -> allreduce(swiglu(x) @ w_down)."""
+    tokens: int
+    hidden: int
+    inter: int          # this PE's slice of the intermediate size
+    layers: int = 1
+    algo: int = _capi.ALGO_AUTO
+    deterministic: bool = False
+    num_ctas: int = 0
+    cta_pairs: int = _capi.CTA_PAIRS_AUTO
+    timeout_ns: int = 0
+
+    def to_c(self) -> "_capi.MlpChainProblem":
+        return _capi.MlpChainProblem(tokens=self.tokens, hidden=self.hidden, inter=self.inter,
+                                     layers=self.layers, algo=self.algo,
+                                     deterministic=1 if self.deterministic else 0,
+                                     num_ctas=self.num_ctas, cta_pairs=self.cta_pairs,
+                                     reserved=0, timeout_ns=self.timeout_ns)
+
+
+def mlp_chain_sizes(problem: MlpChainProblem, n_pes: int) -> dict:
+    """Bytes of each buffer megacu_cuda_mlp_chain_bf16 needs on ``n_pes`` PEs."""
+    out = (ctypes.c_int64 * 5)()
+    check(lib().megacu_b200_mlp_chain_sizes(problem.to_c(), n_pes, out))
+    return {"act": out[0], "workspace": out[1], "events_swiglu": out[2],
+            "events_down": out[3], "x_work": out[4]}
+
+
+def mlp_chain(x, w_gate, w_up, w_down, out, *, act, workspace, x_work, events_swiglu,
+              events_down, problem: MlpChainProblem, stream=None, device: int = 0,
+              team: Optional[Team] = None) -> None:
+    """Runs ``problem.layers`` tensor-parallel MLP blocks (async); the last
+    block's output lands in ``out``. ``w_gate``, ``w_up``, ``w_down``: one
+    tensor per layer (this PE's slices)."""
+    n = problem.layers
+    if not (len(w_gate) == len(w_up) == len(w_down) == n):
+        raise ValueError("one gate, up and down weight per layer")
+    arr = lambda ws: (ctypes.c_void_p * n)(*[_ptr(w) for w in ws])
+    check(lib().megacu_cuda_mlp_chain_bf16(driver_view(stream, device, team), _ptr(x),
+                                           arr(w_gate), arr(w_up), arr(w_down), _ptr(act),
+                                           _ptr(workspace), _ptr(x_work), _ptr(out),
+                                           _ptr(events_swiglu), _ptr(events_down),
+                                           problem.to_c()))
+
+
 def events_status(events, stream=None) -> list[int]:
     """Synchronises ``stream`` and raises MegacuError if a device wait failed."""
     info = (ctypes.c_int64 * 4)()

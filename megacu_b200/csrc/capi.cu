@@ -32,6 +32,7 @@
 #include "kernels/gemm_ar_kernel.cuh"
 #include "kernels/launch.cuh"
 #include "team.h"
+#include "tma_map.h"
 
 // ---- the C structs are the C++ types, byte for byte --------------------------
 static_assert(sizeof(megacu_status) == sizeof(megacu::status), "status layout");
@@ -97,40 +98,6 @@ int sm_count(int device) {
     cached[device] = n;
   }
   return cached[device];
-}
-
-// ---- TMA descriptor encoding (driver entry point, no libcuda link) ---------
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-  });
-  return fn;
-}
-
-// Row-major bf16 matrix [rows, cols] tiled in boxes of box_rows x 64 columns
-// with the 128-byte swizzle the UMMA descriptors expect.
-bool encode_bf16_map(CUtensorMap *map, void const *base, std::int64_t rows, std::int64_t cols,
-                     std::uint32_t box_rows) {
-  auto encode = tensor_map_encoder();
-  if (encode == nullptr) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-  cuuint32_t box[2] = {64, box_rows};
-  cuuint32_t elem[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
-                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
 }
 
 // ---- plan of one bf16 call ---------------------------------------------------

@@ -451,11 +451,20 @@ __device__ __forceinline__ bool bar_wait(std::uint64_t *bar, std::uint32_t parit
 // relays the barrier events the follower needs (stage free, accumulator
 // ready, next task) with remote mbarrier arrives; the follower reports back
 // (task taken, accumulator drained) the same way.
-template <int BN, bool kWireF32, bool kPair = false>
+//
+// kSwiGLU = true (one PE, no exchange): the gate/up projection of an MLP
+// block. A tile's BN accumulator columns are BN/2 gate columns (B panels from
+// `map_b`) followed by the same BN/2 columns of up (`map_b2`; with pairs the
+// leader stages gate, the follower up); the epilogue stores
+// silu(gate) * up as bf16 into out[m, n] (n = the act columns, tiles of
+// BN/2). Otherwise `map_b2` is unused.
+template <int BN, bool kWireF32, bool kPair = false, bool kSwiGLU = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ar_megakernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_b2,
                        const __grid_constant__ gemm_ar_params p) {
+  static_assert(!kSwiGLU || (BN == 256 && !kWireF32), "SwiGLU tiles are 128 x (128 + 128)");
   using cfg = gemm_config<BN, kPair>;
   constexpr int kWireBytes = kWireF32 ? 4 : 2;
   constexpr int kVecCols = 16 / kWireBytes;                   // columns per 16 B wire vector
@@ -515,6 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *epoch_slot = ptx::ld_relaxed_gpu(&ctrl->launch_count) + 1u;
     ptx::prefetch_tensor_map(&map_a);
     ptx::prefetch_tensor_map(&map_b);
+    if constexpr (kSwiGLU) ptx::prefetch_tensor_map(&map_b2);
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -574,7 +584,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         std::int32_t const r = tile_of(q);
         tile_coord const c = locate(sched, r);
-        std::int32_t const b_col0 = c.tile_col * BN + static_cast<std::int32_t>(cta_rank) * cfg::b_cols;
+        // SwiGLU: gate and up columns [tile_col * BN/2, + BN/2) (the leader
+        // of a pair stages gate, the follower up); else B columns
+        // [tile_col * BN, + BN), split between the CTAs of a pair.
+        std::int32_t const b_col0 =
+            kSwiGLU ? c.tile_col * (BN / 2)
+                    : c.tile_col * BN + static_cast<std::int32_t>(cta_rank) * cfg::b_cols;
+        CUtensorMap const *pair_b = (kSwiGLU && cta_rank == 1) ? &map_b2 : &map_b;
         for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
           std::uint32_t const s = it % cfg::stages;
           if (!bar_wait<kPair>(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word)) {
@@ -598,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tma_load_2d_pair(&map_a, bar, sa, kb * kBlockK, c.tile_row * kBlockM);
 #pragma unroll
             for (int panel = 0; panel < cfg::b_cols / 64; ++panel) {
-              ptx::tma_load_2d_pair(&map_b, bar, sb + panel * cfg::b_panel_bytes,
+              ptx::tma_load_2d_pair(pair_b, bar, sb + panel * cfg::b_panel_bytes,
                                     b_col0 + panel * 64, kb * kBlockK);
             }
           } else {
@@ -606,8 +622,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tma_load_2d(&map_a, &full[s], sa, kb * kBlockK, c.tile_row * kBlockM);
 #pragma unroll
             for (int panel = 0; panel < BN / 64; ++panel) {
-              ptx::tma_load_2d(&map_b, &full[s], sb + panel * cfg::b_panel_bytes,
-                               b_col0 + panel * 64, kb * kBlockK);
+              constexpr int kHalf = BN / 128;  // panels per half (SwiGLU)
+              CUtensorMap const *map = (kSwiGLU && panel >= kHalf) ? &map_b2 : &map_b;
+              std::int32_t const col = kSwiGLU ? b_col0 + (panel % kHalf) * 64 : b_col0 + panel * 64;
+              ptx::tma_load_2d(map, &full[s], sb + panel * cfg::b_panel_bytes, col,
+                               kb * kBlockK);
             }
           }
         }
@@ -753,8 +772,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       // written nor published, and no reduce task exists for it.
       bool const active = c.tile_row * kBlockM + quarter * 32 < p.m;
 
+      if constexpr (kSwiGLU) {
+        // act[row, col] = silu(gate) * up, from accumulator columns col and
+        // BN/2 + col, in fp32, rounded once to bf16.
+        std::int32_t const acol0 = c.tile_col * (BN / 2);
 #pragma unroll 1
-      for (int ch = 0; active && ch < BN / 32; ++ch) {
+        for (int ch = 0; active && ch < BN / 64; ++ch) {
+          std::uint32_t g[32], u[32];
+          ptx::tmem_load_32x32b_x32(t_row + ch * 32, g);
+          ptx::tmem_load_32x32b_x32(t_row + BN / 2 + ch * 32, u);
+          ptx::tmem_wait_load();
+          if (grow < p.m) {
+            __nv_bfloat16 *dst = p.out + static_cast<std::int64_t>(grow) * p.n;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              std::int32_t const col = acol0 + ch * 32 + j * 8;
+              if (col < p.n) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  float const x = __uint_as_float(g[8 * j + e]);
+                  f[e] = x / (1.0f + __expf(-x)) * __uint_as_float(u[8 * j + e]);
+                }
+                uint4 q;
+                q.x = ptx::pack_bf16x2(f[0], f[1]);
+                q.y = ptx::pack_bf16x2(f[2], f[3]);
+                q.z = ptx::pack_bf16x2(f[4], f[5]);
+                q.w = ptx::pack_bf16x2(f[6], f[7]);
+                ptx::st_v4(dst + col, q);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll 1
+      for (int ch = 0; !kSwiGLU && active && ch < BN / 32; ++ch) {
         std::uint32_t v[32];
         ptx::tmem_load_32x32b_x32(t_row + ch * 32, v);
         ptx::tmem_wait_load();

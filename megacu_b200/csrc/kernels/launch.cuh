@@ -12,13 +12,14 @@ namespace megacu_b200 {
 
 inline constexpr int kLaunchMaxDevices = 64;
 
-template <int BN, bool kWireF32, bool kPair>
+template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false>
 cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
-                           CUtensorMap const &mb, gemm_ar_params const &prm) {
+                           CUtensorMap const &mb, CUtensorMap const &mb2,
+                           gemm_ar_params const &prm) {
   static bool configured[kLaunchMaxDevices] = {};
   static int max_pairs[kLaunchMaxDevices] = {};
   constexpr int smem = gemm_config<BN, kPair>::smem_bytes;
-  auto kernel = &gemm_ar_megakernel<BN, kWireF32, kPair>;
+  auto kernel = &gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU>;
   bool const known = device >= 0 && device < kLaunchMaxDevices;
   if (!known || !configured[device]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -26,7 +27,7 @@ cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMa
     if (known) configured[device] = true;
   }
   if constexpr (!kPair) {
-    kernel<<<grid, kThreads, smem, stream>>>(ma, mb, prm);
+    kernel<<<grid, kThreads, smem, stream>>>(ma, mb, mb2, prm);
     return cudaGetLastError();
   } else {
     cudaLaunchConfig_t cfg{};
@@ -51,7 +52,7 @@ cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMa
     }
     int const g = std::max(2, std::min(grid / 2, pairs) * 2);
     cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
-    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, prm);
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, mb2, prm);
   }
 }
 
@@ -63,14 +64,23 @@ cudaError_t launch_gemm_ar(int tile_n, bool pairs, int device, int grid, cudaStr
                            gemm_ar_params const &prm) {
   switch (tile_n) {
     case 256:
-      return pairs ? launch_variant<256, kWireF32, true>(device, grid, stream, ma, mb, prm)
-                   : launch_variant<256, kWireF32, false>(device, grid, stream, ma, mb, prm);
+      return pairs ? launch_variant<256, kWireF32, true>(device, grid, stream, ma, mb, mb, prm)
+                   : launch_variant<256, kWireF32, false>(device, grid, stream, ma, mb, mb, prm);
     case 128:
-      return pairs ? launch_variant<128, kWireF32, true>(device, grid, stream, ma, mb, prm)
-                   : launch_variant<128, kWireF32, false>(device, grid, stream, ma, mb, prm);
+      return pairs ? launch_variant<128, kWireF32, true>(device, grid, stream, ma, mb, mb, prm)
+                   : launch_variant<128, kWireF32, false>(device, grid, stream, ma, mb, mb, prm);
     default:
-      return launch_variant<64, kWireF32, false>(device, grid, stream, ma, mb, prm);
+      return launch_variant<64, kWireF32, false>(device, grid, stream, ma, mb, mb, prm);
   }
+}
+
+// The gate/up projection with the SiLU * up epilogue (one PE): `mg` and `mu`
+// are the gate and up weights [k, n] with 64 x 64 boxes.
+inline cudaError_t launch_swiglu(bool pairs, int device, int grid, cudaStream_t stream,
+                                 CUtensorMap const &ma, CUtensorMap const &mg,
+                                 CUtensorMap const &mu, gemm_ar_params const &prm) {
+  return pairs ? launch_variant<256, false, true, true>(device, grid, stream, ma, mg, mu, prm)
+               : launch_variant<256, false, false, true>(device, grid, stream, ma, mg, mu, prm);
 }
 
 }  // namespace megacu_b200

@@ -30,6 +30,7 @@
 
 #include "kernels/gemm_ar_kernel.cuh"
 #include "kernels/launch.cuh"
+#include "tma_map.h"
 
 namespace {
 
@@ -72,30 +73,6 @@ megacu_status scratch_address(int device, void **out) {
   return na_ok();
 }
 
-bool na_encode(CUtensorMap *map, void const *base, std::int64_t rows, std::int64_t cols,
-               std::uint32_t box_rows) {
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *fn = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess) {
-      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    }
-  });
-  if (encode == nullptr) return false;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-  cuuint32_t box[2] = {64, box_rows};
-  cuuint32_t elem[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
-                box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace
 
 extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver, void const *a,
@@ -134,8 +111,8 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
   if (st.code != MEGACU_OK) return st;
 
   CUtensorMap map_a, map_b;
-  if (!na_encode(&map_a, a, problem.m, problem.k, kBlockM) ||
-      !na_encode(&map_b, b, problem.k, problem.n, kBlockK)) {
+  if (!encode_bf16_map(&map_a, a, problem.m, problem.k, kBlockM) ||
+      !encode_bf16_map(&map_b, b, problem.k, problem.n, kBlockK)) {
     return na_fail(MEGACU_BACKEND_ERROR, 30, "cuTensorMapEncodeTiled failed");
   }
   auto stream = static_cast<cudaStream_t>(driver.launch.stream);

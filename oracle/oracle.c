@@ -382,3 +382,40 @@ void oracle_bf16_tiles(const oracle_bf16_problem *p, const float *const *a,
   free(jobs);
   free(tid);
 }
+
+/* ---- tensor-parallel MLP blocks -------------------------------------------- */
+
+void oracle_mlp_chain(int64_t t, int64_t h, int64_t i, int32_t layers, int32_t n_pes,
+                      int32_t wire_bytes, const float *x, const float *const *wg,
+                      const float *const *wu, const float *const *wd, float *out,
+                      int32_t threads) {
+  float *cur = (float *)malloc(sizeof(float) * (size_t)(t * h));
+  float *g = (float *)malloc(sizeof(float) * (size_t)(t * i));
+  float *u = (float *)malloc(sizeof(float) * (size_t)(t * i));
+  float *part = (float *)malloc(sizeof(float) * (size_t)(t * h));
+  float *sum = (float *)malloc(sizeof(float) * (size_t)(t * h));
+  memcpy(cur, x, sizeof(float) * (size_t)(t * h));
+  for (int32_t l = 0; l < layers; ++l) {
+    for (int64_t e = 0; e < t * h; ++e) sum[e] = 0.0f;
+    for (int32_t p = 0; p < n_pes; ++p) {
+      int64_t const w = (int64_t)l * n_pes + p;
+      oracle_gemm_f32(cur, wg[w], g, t, i, h, threads);
+      oracle_gemm_f32(cur, wu[w], u, t, i, h, threads);
+      for (int64_t e = 0; e < t * i; ++e) {
+        float const s = g[e] / (1.0f + expf(-g[e]));
+        g[e] = oracle_round_bf16(s * u[e]); /* act */
+      }
+      oracle_gemm_f32(g, wd[w], part, t, h, i, threads);
+      for (int64_t e = 0; e < t * h; ++e) {
+        sum[e] += wire_bytes == 2 ? oracle_round_bf16(part[e]) : part[e];
+      }
+    }
+    for (int64_t e = 0; e < t * h; ++e) cur[e] = oracle_round_bf16(sum[e]);
+  }
+  memcpy(out, cur, sizeof(float) * (size_t)(t * h));
+  free(cur);
+  free(g);
+  free(u);
+  free(part);
+  free(sum);
+}

@@ -60,6 +60,23 @@ int oracle_phased_f32(int64_t m, int64_t n, int64_t k, int32_t tile_m, int32_t t
 void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode,
                    int32_t group_m, int32_t r, int32_t out[4]);
 
+/*
+ * Tensor-parallel MLP blocks (a B200 addition with no
+ * counterpart in megacu, so its semantics are pinned by this restatement):
+ * for l = 0 .. layers-1, on every PE p,
+ *   act_p = bf16(silu(x_l @ wg[l][p]) * (x_l @ wu[l][p]))   (fp32 products and
+ *            epilogue, silu(g) = g / (1 + expf(-g)), one bf16 rounding)
+ *   x_{l+1} = bf16(sum over p = 0..n_pes-1 of wire(act_p @ wd[l][p]))
+ * with wire() rounding each partial to bf16 when wire_bytes == 2 (fp32 sum
+ * in PE order either way). x: [t, h]; wg, wu: [h, i] per layer and PE (index
+ * l * n_pes + p); wd: [i, h]; out: [t, h] = x_layers. Inputs are bf16 values
+ * held as fp32.
+ */
+void oracle_mlp_chain(int64_t t, int64_t h, int64_t i, int32_t layers, int32_t n_pes,
+                      int32_t wire_bytes, const float *x, const float *const *wg,
+                      const float *const *wu, const float *const *wd, float *out,
+                      int32_t threads);
+
 /* CTA-pair schedule restatement (a B200 addition with no counterpart in
  * megacu): GEMM pair ticket q -> out[0], out[1] = raster indices of the
  * upper and lower 128-row tiles the two CTAs of a cluster compute. */

@@ -55,6 +55,10 @@ def load():
         lib.oracle_bf16_tiles.argtypes = [ctypes.POINTER(OracleBf16Problem),
                                           ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
                                           ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, _f32p]
+        lib.oracle_mlp_chain.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p,
+                                         ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
+                                         ctypes.POINTER(_f32p), _f32p, ctypes.c_int32]
         _lib = lib
     return _lib
 
@@ -161,6 +165,21 @@ def bf16_tiles(a_list, b_list, tile_ids, *, m, n, k, tile_n, wire_bytes=2, threa
     load().oracle_bf16_tiles(ctypes.byref(p), _fp_array(list(a_list)), _fp_array(list(b_list)),
                              ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(ids),
                              _fp(out))
+    return out
+
+
+def mlp_chain(x, wg, wu, wd, *, wire_bytes=2, threads=0):
+    """The MLP chain's output. x: [t, h]; wg, wu: [layers][n_pes] of [h, i];
+    wd: [layers][n_pes] of [i, h] (bf16 values as float32)."""
+    layers, n_pes = len(wg), len(wg[0])
+    t, h = x.shape
+    i = wg[0][0].shape[1]
+    x = np.ascontiguousarray(x, np.float32)
+    flat = lambda ws: [np.ascontiguousarray(w, np.float32) for layer in ws for w in layer]
+    g, u, d = flat(wg), flat(wu), flat(wd)
+    out = np.empty((t, h), np.float32)
+    load().oracle_mlp_chain(t, h, i, layers, n_pes, wire_bytes, _fp(x), _fp_array(g), _fp_array(u),
+                            _fp_array(d), _fp(out), threads or os.cpu_count() or 1)
     return out
 
 

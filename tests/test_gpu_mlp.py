@@ -1,0 +1,134 @@
+"""Tensor-parallel MLP blocks through the C ABI against the
+CPU oracle: the SwiGLU gate/up projection alone, and chains of blocks on one
+PE and on a two-GPU team (one process, peer exchange)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import megacu_b200 as mb
+import oracle_lib
+from conftest import gpu_count
+from gpu_util import REL_TOL, f32, rel_error, seeded_bf16
+from test_gpu_team import _same_process_team
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(gpu_count() < 1, reason="needs a CUDA GPU")]
+
+
+def _weights(seed, layers, n_pes, h, i, std=0.05):
+    """Per layer and PE: gate, up [h, i] and down [i, h] slices (bf16, host)."""
+    mk = lambda l, p, j, shape: seeded_bf16(seed * 1000 + 100 * l + 10 * p + j, shape, std)
+    wg = [[mk(l, p, 0, (h, i)) for p in range(n_pes)] for l in range(layers)]
+    wu = [[mk(l, p, 1, (h, i)) for p in range(n_pes)] for l in range(layers)]
+    wd = [[mk(l, p, 2, (i, h)) for p in range(n_pes)] for l in range(layers)]
+    return wg, wu, wd
+
+
+def _f32s(ws):
+    return [[f32(w) for w in layer] for layer in ws]
+
+
+@pytest.mark.parametrize("t,h,i,pairs", [
+    (256, 320, 384, mb.CTA_PAIRS_AUTO),   # CTA pairs, k not a multiple of 64
+    (200, 256, 200, mb.CTA_PAIRS_OFF),    # ragged tokens and act columns
+    (256, 128, 136, mb.CTA_PAIRS_ON),     # pairs with a ragged last act tile
+])
+def test_swiglu_matches_oracle(t, h, i, pairs):
+    x = seeded_bf16(71, (t, h), 1.0)
+    (wg,), (wu,), _ = _weights(72, 1, 1, h, i)
+    prob = mb.Problem(t, i, h, cta_pairs=pairs)
+    act = torch.full((t, i), float("nan"), dtype=torch.bfloat16, device="cuda")
+    events = torch.zeros(mb.swiglu_events_bytes(prob) // 4, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream()
+    for _ in range(2):  # the second call reuses the events buffer (next epoch)
+        mb.gemm_swiglu(x.cuda(), wg[0].cuda(), wu[0].cuda(), act, events=events, problem=prob,
+                       stream=stream)
+        mb.events_status(events, stream)
+    g = oracle_lib.gemm_f32(f32(x), f32(wg[0]))
+    u = oracle_lib.gemm_f32(f32(x), f32(wu[0]))
+    want = oracle_lib.round_bf16((g / (1.0 + np.exp(-g)) * u).astype(np.float32))
+    assert rel_error(f32(act), want) < REL_TOL
+    assert mb.events_counters(events)[0] == 2 * (-(-t // 128)) * (-(-i // 128))
+
+
+def _chain_buffers(prob, n_pes, team=None, device=0):
+    sz = mb.mlp_chain_sizes(prob, n_pes)
+    dev = f"cuda:{device}"
+    sym = (lambda shape, dtype: team.tensor(shape, dtype)) if team is not None else \
+        (lambda shape, dtype: torch.zeros(shape, dtype=dtype, device=dev))
+    return dict(
+        act=torch.empty(sz["act"] // 2, dtype=torch.bfloat16, device=dev),
+        workspace=sym((max(sz["workspace"], 16),), torch.uint8),
+        x_work=sym((prob.tokens, prob.hidden), torch.bfloat16),
+        events_swiglu=torch.zeros(sz["events_swiglu"] // 4, dtype=torch.int32, device=dev),
+        events_down=sym((sz["events_down"] // 4,), torch.int32)), \
+        sym((prob.tokens, prob.hidden), torch.bfloat16)
+
+
+def _check_chain(x, wg, wu, wd, out, x_work):
+    """Every block is held to the single-block bar (REL_TOL) against the
+    oracle run from that block's actual input; from x, bf16 roundings of
+    independent blocks add up, so the end-to-end bar is REL_TOL per block.
+    With two or more blocks x_work holds the second-to-last block's output
+    (the outputs alternate so that the last lands in out)."""
+    layers = len(wg)
+    sub = lambda ws, l0, l1: [[f32(w) for w in layer] for layer in ws[l0:l1]]
+    got = f32(out)
+    if layers == 1:
+        first = oracle_lib.mlp_chain(f32(x), sub(wg, 0, 1), sub(wu, 0, 1), sub(wd, 0, 1))
+        assert rel_error(got, first) < REL_TOL
+        return
+    last_in = f32(x_work)
+    last = oracle_lib.mlp_chain(last_in, sub(wg, layers - 1, layers), sub(wu, layers - 1, layers),
+                                sub(wd, layers - 1, layers))
+    assert rel_error(got, last) < REL_TOL
+    if layers == 2:  # x_work is block 0's output
+        first = oracle_lib.mlp_chain(f32(x), sub(wg, 0, 1), sub(wu, 0, 1), sub(wd, 0, 1))
+        assert rel_error(last_in, first) < REL_TOL
+    whole = oracle_lib.mlp_chain(f32(x), _f32s(wg), _f32s(wu), _f32s(wd))
+    assert rel_error(got, whole) < REL_TOL * layers
+
+
+@pytest.mark.parametrize("layers", [1, 2, 3])
+def test_mlp_chain_one_pe_matches_oracle(layers):
+    t, h, i = 256, 256, 384
+    x = seeded_bf16(81, (t, h), 1.0)
+    wg, wu, wd = _weights(82, layers, 1, h, i)
+    prob = mb.MlpChainProblem(t, h, i, layers=layers)
+    bufs, out = _chain_buffers(prob, 1)
+    stream = torch.cuda.current_stream()
+    dev = lambda ws: [w[0].cuda() for w in ws]
+    mb.mlp_chain(x.cuda(), dev(wg), dev(wu), dev(wd), out, problem=prob, stream=stream, **bufs)
+    mb.events_status(bufs["events_swiglu"], stream)
+    mb.events_status(bufs["events_down"], stream)
+    _check_chain(x, wg, wu, wd, out, bufs["x_work"])
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
+def test_mlp_chain_two_gpus_matches_oracle():
+    t, h, i, layers = 256, 256, 192, 2
+    x = seeded_bf16(91, (t, h), 1.0)
+    wg, wu, wd = _weights(92, layers, 2, h, i)
+    prob = mb.MlpChainProblem(t, h, i, layers=layers, timeout_ns=5_000_000_000)
+    teams = _same_process_team([0, 1])
+    calls = []
+    for pe, team in enumerate(teams):
+        with torch.cuda.device(pe):
+            bufs, out = _chain_buffers(prob, 2, team, pe)
+            ws = lambda w: [layer[pe].to(f"cuda:{pe}") for layer in w]
+            calls.append((team, bufs, out, x.to(f"cuda:{pe}"), ws(wg), ws(wu), ws(wd),
+                          torch.cuda.Stream(device=pe)))
+    for pe, (team, bufs, out, xd, g, u, d, stream) in enumerate(calls):
+        with torch.cuda.device(pe):
+            mb.mlp_chain(xd, g, u, d, out, problem=prob, stream=stream, device=pe, team=team,
+                         **bufs)
+    for pe, (team, bufs, out, *_rest, stream) in enumerate(calls):
+        mb.events_status(bufs["events_swiglu"], stream)
+        mb.events_status(bufs["events_down"], stream)
+    for pe, (team, bufs, out, *_rest) in enumerate(calls):
+        _check_chain(x, wg, wu, wd, out, bufs["x_work"])
+    assert torch.equal(calls[0][2].cpu(), calls[1][2].cpu())  # every PE holds the same bits
+    for team, *_rest in calls:
+        team.close()

@@ -218,3 +218,33 @@ def test_pair_plan_choices():
     prob.cta_pairs = 3
     with pytest.raises(mb.MegacuError):
         mb.plan(prob, 8)
+
+
+def test_mlp_chain_matches_float64_restatement():
+    """oracle_mlp_chain against a numpy float64 restatement of the same
+    semantics (bf16 roundings at act, at the wire and at each block's output)."""
+    rng = np.random.default_rng(5)
+    t, h, i, layers, n_pes = 48, 64, 40, 2, 3
+    rb = oracle_lib.round_bf16
+    x = rb(rng.normal(0, 1, (t, h)).astype(np.float32))
+    wg = [[rb(rng.normal(0, 0.1, (h, i)).astype(np.float32)) for _ in range(n_pes)]
+          for _ in range(layers)]
+    wu = [[rb(rng.normal(0, 0.1, (h, i)).astype(np.float32)) for _ in range(n_pes)]
+          for _ in range(layers)]
+    wd = [[rb(rng.normal(0, 0.1, (i, h)).astype(np.float32)) for _ in range(n_pes)]
+          for _ in range(layers)]
+    for wire in (2, 4):
+        got = oracle_lib.mlp_chain(x, wg, wu, wd, wire_bytes=wire)
+        cur = x.astype(np.float64)
+        for l in range(layers):
+            total = np.zeros((t, h))
+            for p in range(n_pes):
+                g = cur @ wg[l][p]
+                u = cur @ wu[l][p]
+                act = rb((g / (1 + np.exp(-g)) * u).astype(np.float32)).astype(np.float64)
+                part = (act @ wd[l][p]).astype(np.float32)
+                total += rb(part) if wire == 2 else part
+            cur = rb(total.astype(np.float32)).astype(np.float64)
+        scale = np.abs(cur).max()
+        assert np.max(np.abs(got - cur)) < 1e-2 * scale, wire
+        assert np.all(np.isfinite(got))
