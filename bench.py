@@ -289,6 +289,22 @@ def run_gpu(args, rank, world, local_rank):
     def gemm_only():
         torch.matmul(a, b, out=c)
 
+    # The same kernel without its exchange: this PE's GEMM (its K slice) as a
+    # one-PE call into a local output. The fused call minus this is the
+    # exchange time the kernel did not hide behind its GEMM.
+    arms = [fused, unfused, gemm_only]
+    if tp > 1:
+        solo_prob = mb.Problem(M, N, k, timeout_ns=30_000_000_000)
+        solo_events = torch.zeros(mb.events_bytes(solo_prob, 1) // 4, dtype=torch.int32,
+                                  device=dev)
+        solo_out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+        def kernel_without_exchange():
+            mb.gemm_allreduce(a, b, solo_out, workspace=None, events=solo_events,
+                              problem=solo_prob, stream=stream, device=local_rank)
+
+        arms.append(kernel_without_exchange)
+
     # The clock sampler runs from the heat-up through the timed steps. The
     # heat-up (a fixed number of untimed calls of both arms, the same on every
     # rank: each call is a collective) brings the GPU to its power-capped
@@ -299,9 +315,12 @@ def run_gpu(args, rank, world, local_rank):
             fused()
             unfused()
         torch.cuda.synchronize()
-        ms_fused, ms_unfused, ms_gemm = timed_steps([fused, unfused, gemm_only], args.steps,
-                                                    args.warmup)
+        times = timed_steps(arms, args.steps, args.warmup)
+    ms_fused, ms_unfused, ms_gemm = times[:3]
+    ms_solo = times[3] if tp > 1 else None
     mb.events_status(events, stream)
+    if tp > 1:
+        mb.events_status(solo_events, stream)
     flops_total = 2.0 * M * N * K_TOTAL
     flops_rank = flops_total / tp
     value = flops_total / (ms_fused * 1e-3) / 1e12
@@ -371,6 +390,11 @@ def run_gpu(args, rank, world, local_rank):
                               "note": "slower of GEMM at the measured peak and the allreduce "
                                       "bus bytes 2(tp-1)/tp x output at the measured 770 GB/s "
                                       "per direction (900 nominal)"},
+            "exposed_comm": None if ms_solo is None else {
+                "us": (ms_fused - ms_solo) * 1e3,
+                "kernel_without_exchange_us": ms_solo * 1e3,
+                "note": "fused call minus the same kernel on one PE with this PE's K slice "
+                        "(no exchange), timed interleaved with the other arms"},
             "cpu_baseline": cpu,
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
