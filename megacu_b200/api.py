@@ -18,6 +18,7 @@ per-site detail number.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 from typing import Callable, Optional, Sequence
 
@@ -90,6 +91,10 @@ class Team:
         check(lib().megacu_b200_team_create(my_pe, n_pes, device, heap_bytes,
                                             ctypes.byref(handle)))
         self.handle = handle.value
+        # A team still open when the interpreter exits (an exception on the
+        # way) is destroyed then: a process must not end with its memory bound
+        # to a multicast object while the other PEs still use it.
+        self._finalizer = weakref.finalize(self, _destroy_team, self.handle)
         if n_pes > 1:
             if exchange is None:
                 raise ValueError("a team of more than one PE needs an exchange function")
@@ -160,7 +165,11 @@ class Team:
         check(lib().megacu_b200_team_barrier(self.handle, _stream_handle(stream)))
 
     def close(self) -> None:
+        """Destroys the team; collective when it has a multicast region."""
         if self.handle is not None:
+            finalizer = getattr(self, "_finalizer", None)
+            if finalizer is not None:
+                finalizer.detach()
             check(lib().megacu_b200_team_destroy(self.handle))
             self.handle = None
 
@@ -168,6 +177,10 @@ class Team:
         return _capi.TeamView(team=self.handle, team_my_pe=self.my_pe, team_n_pes=self.n_pes,
                               world_my_pe=self.my_pe, world_n_pes=self.n_pes,
                               cuda_device_ordinal=self.device)
+
+
+def _destroy_team(handle) -> None:
+    lib().megacu_b200_team_destroy(handle)
 
 
 def torch_exchange(group=None) -> Callable[[bytes], Sequence[bytes]]:
