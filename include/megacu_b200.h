@@ -56,6 +56,8 @@ typedef struct megacu_status {
  *   27 CTA pairs requested but the tile grid cannot hold them
  *   28 workspace / out in the multicast region of a call that cannot reduce
  *      in the switch (not a two-shot bf16-wire allreduce, or only one of them)
+ *   29 outside a single-launch MLP chain's limits (more than 6 blocks, or
+ *      the fp32 wire)
  *   30 cuTensorMapEncodeTiled failed
  *   31 exporting the team heap (CUDA IPC), 32 peer handle of another team,
  *   33 peer mapping (CUDA IPC / peer access), 34 symmetric heap exhausted
@@ -225,8 +227,11 @@ typedef struct megacu_mlp_chain_problem {
   int32_t algo;          /* allreduce algo of the down projection */
   int32_t deterministic; /* as in megacu_gemm_ar_problem_v2 */
   int32_t num_ctas;      /* 0 = one persistent CTA per SM */
-  int32_t cta_pairs;     /* enum megacu_cta_pairs, both launches of a block */
-  int32_t reserved;
+  int32_t cta_pairs;     /* enum megacu_cta_pairs, every launch */
+  int32_t single_launch; /* 0: two launches per block; 1: all blocks (at most
+                            6) in one persistent launch, blocks waiting for
+                            each other through counters in events_down
+                            (bf16 partials, two-shot peer exchange) */
   uint64_t timeout_ns;   /* bound of every cross-GPU wait; 0 = 10 s */
 } megacu_mlp_chain_problem;
 
@@ -248,8 +253,11 @@ megacu_status megacu_b200_mlp_chain_sizes(megacu_mlp_chain_problem problem, int3
  * and x_work so that the last one lands in out; both are placed like the
  * out of megacu_cuda_gemm_allreduce_bf16 (symmetric for two-shot; in the
  * team's multicast region, together with workspace, for the in-switch
- * reduction). Two launches per block: megacu_cuda_gemm_swiglu_bf16, then
- * megacu_cuda_gemm_allreduce_bf16.
+ * reduction). With single_launch = 0, two launches per block:
+ * megacu_cuda_gemm_swiglu_bf16, then megacu_cuda_gemm_allreduce_bf16. With
+ * single_launch = 1, one persistent launch runs every block; workspace, out,
+ * x_work and events_down then lie in the team's heap (not its multicast
+ * region). One events_down buffer serves either mode.
  */
 megacu_status megacu_cuda_mlp_chain_bf16(
     megacu_driver_view driver, const void *x, const void *const *w_gate,

@@ -67,7 +67,7 @@ class GemmArProblemV2(ctypes.Structure):
 class MlpChainProblem(ctypes.Structure):
     _fields_ = [("tokens", c_int64), ("hidden", c_int64), ("inter", c_int64),
                 ("layers", c_int32), ("algo", c_int32), ("deterministic", c_int32),
-                ("num_ctas", c_int32), ("cta_pairs", c_int32), ("reserved", c_int32),
+                ("num_ctas", c_int32), ("cta_pairs", c_int32), ("single_launch", c_int32),
                 ("timeout_ns", c_uint64)]
 
 

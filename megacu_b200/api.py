@@ -365,13 +365,15 @@ class MlpChainProblem:
     num_ctas: int = 0
     cta_pairs: int = _capi.CTA_PAIRS_AUTO
     timeout_ns: int = 0
+    single_launch: bool = False  # all blocks (at most 6) in one persistent launch
 
     def to_c(self) -> "_capi.MlpChainProblem":
         return _capi.MlpChainProblem(tokens=self.tokens, hidden=self.hidden, inter=self.inter,
                                      layers=self.layers, algo=self.algo,
                                      deterministic=1 if self.deterministic else 0,
                                      num_ctas=self.num_ctas, cta_pairs=self.cta_pairs,
-                                     reserved=0, timeout_ns=self.timeout_ns)
+                                     single_launch=1 if self.single_launch else 0,
+                                     timeout_ns=self.timeout_ns)
 
 
 def mlp_chain_sizes(problem: MlpChainProblem, n_pes: int) -> dict:

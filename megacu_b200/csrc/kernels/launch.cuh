@@ -12,22 +12,21 @@ namespace megacu_b200 {
 
 inline constexpr int kLaunchMaxDevices = 64;
 
-template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false>
-cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
-                           CUtensorMap const &mb, CUtensorMap const &mb2,
-                           gemm_ar_params const &prm) {
+// Persistent launch of `Kernel` (one CTA per SM, or 2-CTA clusters with
+// kPair): sets its dynamic shared memory once per device and, for clusters,
+// caps the grid at the pairs that fit on the device at once.
+template <auto Kernel, bool kPair, int kSmem, class... Args>
+cudaError_t launch_persistent(int device, int grid, cudaStream_t stream, Args const &...args) {
   static bool configured[kLaunchMaxDevices] = {};
   static int max_pairs[kLaunchMaxDevices] = {};
-  constexpr int smem = gemm_config<BN, kPair>::smem_bytes;
-  auto kernel = &gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU>;
   bool const known = device >= 0 && device < kLaunchMaxDevices;
   if (!known || !configured[device]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     if (known) configured[device] = true;
   }
   if constexpr (!kPair) {
-    kernel<<<grid, kThreads, smem, stream>>>(ma, mb, mb2, prm);
+    Kernel<<<grid, kThreads, kSmem, stream>>>(args...);
     return cudaGetLastError();
   } else {
     cudaLaunchConfig_t cfg{};
@@ -37,23 +36,31 @@ cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMa
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = kSmem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    // Persistent: at most as many pairs as fit on the device at once.
     int pairs = known ? max_pairs[device] : 0;
     if (pairs == 0) {
       cfg.gridDim = dim3(2, 1, 1);
-      cudaError_t e = cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg);
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&pairs, Kernel, &cfg);
       if (e != cudaSuccess) return e;
       if (pairs < 1) return cudaErrorInvalidConfiguration;
       if (known) max_pairs[device] = pairs;
     }
     int const g = std::max(2, std::min(grid / 2, pairs) * 2);
     cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
-    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, mb2, prm);
+    return cudaLaunchKernelEx(&cfg, Kernel, args...);
   }
+}
+
+template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false>
+cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
+                           CUtensorMap const &mb, CUtensorMap const &mb2,
+                           gemm_ar_params const &prm) {
+  return launch_persistent<&gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU>, kPair,
+                           gemm_config<BN, kPair>::smem_bytes>(device, grid, stream, ma, mb, mb2,
+                                                               prm);
 }
 
 // Launches the variant a plan picked: tile_n 64 / 128 / 256, CTA pairs

@@ -77,6 +77,20 @@ __device__ __forceinline__ void publish_local_data(std::uint32_t *flag, std::uin
   st_relaxed_sys(flag, v);
 }
 
+// Adds `v` to a counter (this GPU's or a peer's) with release semantics at
+// system scope: the issuing thread's earlier writes are visible to whoever
+// acquires the counter's new value.
+__device__ __forceinline__ void red_release_sys_add(std::uint32_t *p, std::uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses (and the acquires that
+// made other threads' writes visible to it) before its later async-proxy
+// ones, e.g. TMA loads of data that other SMs or GPUs wrote.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // ---- NVSwitch multicast (multimem) ----------------------------------------------
 // `mc` must be an address in a multicast mapping (a team's multicast region).
 

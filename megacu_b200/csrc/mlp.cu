@@ -3,9 +3,11 @@
 //   x_out = allreduce_pe(act @ w_down)          row-parallel, fused exchange
 // megacu_cuda_gemm_swiglu_bf16 is the first line as one persistent launch of
 // the megakernel's SwiGLU variant; megacu_cuda_mlp_chain_bf16 runs `layers`
-// such blocks back to back, each one SwiGLU launch and one fused GEMM +
-// allreduce launch (megacu_cuda_gemm_allreduce_bf16), the output of one block
-// feeding the next.
+// such blocks back to back: either each block as one SwiGLU launch and one
+// fused GEMM + allreduce launch (megacu_cuda_gemm_allreduce_bf16), the output
+// of one block feeding the next, or all blocks (up to six) in one persistent
+// launch of mlp_chain_megakernel, whose blocks wait for each other through
+// counters in the event tensor.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -13,8 +15,10 @@
 
 #include <megacu_b200.h>
 
+#include "kernels/chain_kernel.cuh"
 #include "kernels/gemm_ar_kernel.cuh"
 #include "kernels/launch.cuh"
+#include "team.h"
 #include "tma_map.h"
 
 namespace {
@@ -156,6 +160,173 @@ megacu_gemm_ar_problem_v2 down_problem(megacu_mlp_chain_problem const &p) {
   return q;
 }
 
+// ---- the whole chain in one persistent launch ---------------------------------
+
+static_assert(sizeof(chain_maps) + sizeof(chain_params) <= 4096, "kernel parameter space");
+
+struct chain_plan {
+  std::int32_t m_tiles = 0, gu_tiles_n = 0, dn_tiles_n = 0;
+  std::int32_t pairs = 0;
+  std::int64_t workspace_bytes = 0;  // one plane of partial slots
+  std::int64_t events_bytes = 0;
+};
+
+megacu_status make_chain_plan(megacu_mlp_chain_problem const &p, std::int32_t n_pes,
+                              chain_plan &out) {
+  if (p.layers > kChainMaxLayers) {
+    return fail(MEGACU_UNSUPPORTED, 29, "a single-launch chain holds at most 6 blocks");
+  }
+  if (p.deterministic) {
+    return fail(MEGACU_UNSUPPORTED, 29, "a single-launch chain exchanges bf16 partials");
+  }
+  if (p.hidden % 8 != 0 || p.inter % 8 != 0) {
+    return fail(MEGACU_INVALID_ARGUMENT, 21, "hidden and inter must be multiples of 8");
+  }
+  if (p.tokens > (1ll << 30) || p.hidden > (1ll << 30) || p.inter > (1ll << 30)) {
+    return fail(MEGACU_UNSUPPORTED, 22, "dimension too large");
+  }
+  if (n_pes < 1 || n_pes > megacu::nvshmem::max_team_pes) {
+    return fail(MEGACU_INVALID_ARGUMENT, 23, "team size must be 1..8");
+  }
+  if (p.cta_pairs < MEGACU_CTA_PAIRS_AUTO || p.cta_pairs > MEGACU_CTA_PAIRS_ON) {
+    return fail(MEGACU_INVALID_ARGUMENT, 1, "unknown cta_pairs");
+  }
+  chain_plan pl;
+  pl.m_tiles = static_cast<std::int32_t>((p.tokens + kBlockM - 1) / kBlockM);
+  pl.gu_tiles_n = static_cast<std::int32_t>((p.inter + kChainActTile - 1) / kChainActTile);
+  pl.dn_tiles_n = static_cast<std::int32_t>((p.hidden + kChainBN - 1) / kChainBN);
+  if (static_cast<std::int64_t>(pl.m_tiles) * (pl.gu_tiles_n + pl.dn_tiles_n) > (1 << 24)) {
+    return fail(MEGACU_UNSUPPORTED, 22, "too many tiles");
+  }
+  bool const can_pair = pl.m_tiles % 2 == 0;  // raster bands of 16 rows: even
+  if (p.cta_pairs == MEGACU_CTA_PAIRS_ON && !can_pair) {
+    return fail(MEGACU_UNSUPPORTED, 27, "CTA pairs need an even number of token blocks");
+  }
+  pl.pairs = (can_pair && p.cta_pairs != MEGACU_CTA_PAIRS_OFF) ? 1 : 0;
+  pl.workspace_bytes = n_pes == 1 ? 0
+                                  : static_cast<std::int64_t>(pl.m_tiles) * pl.dn_tiles_n *
+                                        kBlockM * kChainBN * 2;
+  pl.events_bytes = chain_events_bytes(p.layers, n_pes, pl.dn_tiles_n, pl.m_tiles);
+  out = pl;
+  return ok_status();
+}
+
+megacu_status run_chain_single_launch(megacu_driver_view driver, void const *x,
+                                      void const *const *w_gate, void const *const *w_up,
+                                      void const *const *w_down, void *act, void *workspace,
+                                      void *x_work, void *out, void *events,
+                                      megacu_mlp_chain_problem const &problem) {
+  std::int32_t const n_pes = driver.team.team_n_pes;
+  std::int32_t const my_pe = driver.team.team_my_pe;
+  chain_plan pl;
+  megacu_status st = make_chain_plan(problem, n_pes, pl);
+  if (st.code != MEGACU_OK) return st;
+  if (my_pe < 0 || my_pe >= n_pes) {
+    return fail(MEGACU_INVALID_ARGUMENT, 23, "team_my_pe out of range");
+  }
+  if (x == nullptr || act == nullptr || events == nullptr || (n_pes > 1 && workspace == nullptr)) {
+    return fail(MEGACU_INVALID_ARGUMENT, 2, "missing storage");
+  }
+  void const *all[] = {x, act, x_work, out, events};
+  for (void const *ptr : all) {
+    if (!aligned16(ptr)) return fail(MEGACU_INVALID_ARGUMENT, 21, "buffers must be 16-byte aligned");
+  }
+  for (std::int32_t l = 0; l < problem.layers; ++l) {
+    if (w_gate[l] == nullptr || w_up[l] == nullptr || w_down[l] == nullptr) {
+      return fail(MEGACU_INVALID_ARGUMENT, 2, "missing weights");
+    }
+    if (!aligned16(w_gate[l]) || !aligned16(w_up[l]) || !aligned16(w_down[l])) {
+      return fail(MEGACU_INVALID_ARGUMENT, 21, "buffers must be 16-byte aligned");
+    }
+  }
+  team_impl *team = nullptr;
+  std::int64_t const x_bytes = problem.tokens * problem.hidden * 2;
+  if (n_pes > 1) {
+    team = as_team(driver.team.team);
+    if (team == nullptr) {
+      return fail(MEGACU_UNSUPPORTED, 13, "remote PEs need a megacu_b200 team in team_view.team");
+    }
+    if (!team->connected || team->n_pes != n_pes || team->my_pe != my_pe) {
+      return fail(MEGACU_INVALID_ARGUMENT, 24, "team handle does not match team_view");
+    }
+    if (!team->contains(workspace, pl.workspace_bytes) ||
+        !team->contains(events, pl.events_bytes) || !team->contains(out, x_bytes) ||
+        !team->contains(x_work, x_bytes)) {
+      return fail(MEGACU_INVALID_ARGUMENT, 25,
+                  "workspace, events, out and x_work must lie in the team's symmetric heap");
+    }
+  }
+  if (driver.launch.stream == nullptr) return ok_status();
+  int const device = driver.launch.device_ordinal;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, 10);
+  if (team != nullptr && team->device != device) {
+    return fail(MEGACU_INVALID_ARGUMENT, 24, "team was created on another device");
+  }
+
+  chain_maps maps{};
+  bool ok = encode_bf16_map(&maps.map[kChainMapX], x, problem.tokens, problem.hidden, kBlockM) &&
+            encode_bf16_map(&maps.map[kChainMapOut], out, problem.tokens, problem.hidden, kBlockM) &&
+            encode_bf16_map(&maps.map[kChainMapWork], x_work, problem.tokens, problem.hidden,
+                            kBlockM) &&
+            encode_bf16_map(&maps.map[kChainMapAct], act, problem.tokens, problem.inter, kBlockM);
+  for (std::int32_t l = 0; ok && l < problem.layers; ++l) {
+    CUtensorMap *m = &maps.map[kChainMapLayer0 + 3 * l];
+    ok = encode_bf16_map(m + 0, w_gate[l], problem.hidden, problem.inter, kBlockK) &&
+         encode_bf16_map(m + 1, w_up[l], problem.hidden, problem.inter, kBlockK) &&
+         encode_bf16_map(m + 2, w_down[l], problem.inter, problem.hidden, kBlockK);
+  }
+  if (!ok) return fail(MEGACU_BACKEND_ERROR, 30, "cuTensorMapEncodeTiled failed");
+
+  chain_params prm{};
+  prm.tokens = static_cast<std::int32_t>(problem.tokens);
+  prm.hidden = static_cast<std::int32_t>(problem.hidden);
+  prm.inter = static_cast<std::int32_t>(problem.inter);
+  prm.layers = problem.layers;
+  prm.m_tiles = pl.m_tiles;
+  prm.gu_tiles_n = pl.gu_tiles_n;
+  prm.dn_tiles_n = pl.dn_tiles_n;
+  prm.gu_units = pl.m_tiles * pl.gu_tiles_n / (pl.pairs ? 2 : 1);
+  prm.dn_units = pl.m_tiles * pl.dn_tiles_n / (pl.pairs ? 2 : 1);
+  prm.n_pes = n_pes;
+  prm.my_pe = my_pe;
+  prm.group_m = 16;
+  tile_schedule const sched_dn{pl.m_tiles, pl.dn_tiles_n, n_pes, mode_allreduce, 16};
+  prm.n_comm = n_pes == 1 ? 0 : owned_tiles(sched_dn, my_pe) * kQuarters;
+  prm.comm_warps = kWorkerWarps;
+  prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
+  prm.act = static_cast<__nv_bfloat16 *>(act);
+  prm.out = static_cast<__nv_bfloat16 *>(out);
+  prm.x_work = static_cast<__nv_bfloat16 *>(x_work);
+  prm.workspace = static_cast<char *>(workspace);
+  prm.events = static_cast<std::uint32_t *>(events);
+  if (team != nullptr) {
+    prm.peers = team->peers;
+  } else {
+    prm.peers.n_pes = 1;
+    prm.peers.my_pe = 0;
+  }
+  auto stream = static_cast<cudaStream_t>(driver.launch.stream);
+  // The dependency counters start at zero in every launch; no peer reaches
+  // this PE's counters before this launch has published its own partials.
+  std::int64_t const counters = chain_counters_base(problem.layers, n_pes, pl.dn_tiles_n);
+  e = cudaMemsetAsync(static_cast<char *>(events) + kControlBytes + 4 * counters, 0,
+                      4 * 2 * static_cast<std::int64_t>(problem.layers) * pl.m_tiles, stream);
+  if (e != cudaSuccess) return cuda_fail(e, 11);
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return cuda_fail(e, 10);
+  int const grid = problem.num_ctas > 0 ? problem.num_ctas : sms;
+  e = pl.pairs ? launch_persistent<&mlp_chain_megakernel<true>, true,
+                                   gemm_config<kChainBN, true>::smem_bytes>(device, grid, stream,
+                                                                            maps, prm)
+               : launch_persistent<&mlp_chain_megakernel<false>, false,
+                                   gemm_config<kChainBN, false>::smem_bytes>(device, grid, stream,
+                                                                             maps, prm);
+  if (e != cudaSuccess) return cuda_fail(e, 14);
+  return ok_status();
+}
+
 megacu_status check_chain(megacu_mlp_chain_problem const &p) {
   if (p.layers < 1 || p.layers > kMaxLayers) {
     return fail(MEGACU_INVALID_ARGUMENT, 1, "layers must be 1..64");
@@ -195,6 +366,14 @@ extern "C" megacu_status megacu_b200_mlp_chain_sizes(megacu_mlp_chain_problem pr
   if (st.code == MEGACU_OK) st = megacu_b200_events_bytes(down, n_pes, &ev);
   if (st.code == MEGACU_OK) st = megacu_b200_swiglu_events_bytes(swiglu_problem(problem), &sev);
   if (st.code != MEGACU_OK) return st;
+  // A single-launch chain uses workspace and events_down with its own layout.
+  if (problem.single_launch) {
+    chain_plan cp;
+    st = make_chain_plan(problem, n_pes, cp);
+    if (st.code != MEGACU_OK) return st;
+    ws = ws > cp.workspace_bytes ? ws : cp.workspace_bytes;
+    ev = ev > cp.events_bytes ? ev : cp.events_bytes;
+  }
   sizes[0] = problem.tokens * problem.inter * 2;   // act, local
   sizes[1] = ws;                                   // down-projection workspace, symmetric
   sizes[2] = sev;                                  // SwiGLU events, local
@@ -213,6 +392,10 @@ extern "C" megacu_status megacu_cuda_mlp_chain_bf16(
   if (w_gate == nullptr || w_up == nullptr || w_down == nullptr || x_work == nullptr ||
       out == nullptr) {
     return fail(MEGACU_INVALID_ARGUMENT, 2, "missing storage");
+  }
+  if (problem.single_launch) {
+    return run_chain_single_launch(driver, x, w_gate, w_up, w_down, act, workspace, x_work, out,
+                                   events_down, problem);
   }
   megacu_gemm_ar_problem_v2 const gu = swiglu_problem(problem);
   megacu_gemm_ar_problem_v2 const down = down_problem(problem);

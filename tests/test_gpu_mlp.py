@@ -91,12 +91,16 @@ def _check_chain(x, wg, wu, wd, out, x_work):
     assert rel_error(got, whole) < REL_TOL * layers
 
 
-@pytest.mark.parametrize("layers", [1, 2, 3])
-def test_mlp_chain_one_pe_matches_oracle(layers):
+@pytest.mark.parametrize("layers,single,pairs", [
+    (1, False, mb.CTA_PAIRS_AUTO), (2, False, mb.CTA_PAIRS_AUTO), (3, False, mb.CTA_PAIRS_AUTO),
+    (1, True, mb.CTA_PAIRS_AUTO), (3, True, mb.CTA_PAIRS_AUTO),   # one persistent launch
+    (2, True, mb.CTA_PAIRS_OFF),
+])
+def test_mlp_chain_one_pe_matches_oracle(layers, single, pairs):
     t, h, i = 256, 256, 384
     x = seeded_bf16(81, (t, h), 1.0)
     wg, wu, wd = _weights(82, layers, 1, h, i)
-    prob = mb.MlpChainProblem(t, h, i, layers=layers)
+    prob = mb.MlpChainProblem(t, h, i, layers=layers, single_launch=single, cta_pairs=pairs)
     bufs, out = _chain_buffers(prob, 1)
     stream = torch.cuda.current_stream()
     dev = lambda ws: [w[0].cuda() for w in ws]

@@ -58,3 +58,30 @@ def test_chain_validation():
     st = lib.megacu_cuda_mlp_chain_bf16(d, FAKE, ptrs, ptrs, ptrs, FAKE, FAKE, None, FAKE, FAKE,
                                         FAKE, prob.to_c())
     assert (st.code, st.detail) == (_capi.INVALID_ARGUMENT, 2)
+
+
+def test_single_launch_chain_limits_and_sizes():
+    lib = _capi.load()
+    d = mb.driver_view(None, 0)
+    ptrs = (ctypes.c_void_p * 7)(*([FAKE] * 7))
+    prob = mb.MlpChainProblem(256, 256, 384, layers=2, single_launch=True)
+    st = lib.megacu_cuda_mlp_chain_bf16(d, FAKE, ptrs, ptrs, ptrs, FAKE, FAKE, FAKE, FAKE, FAKE,
+                                        FAKE, prob.to_c())
+    assert (st.code, st.detail) == (0, 0)
+    for bad in (dict(layers=7), dict(layers=2, deterministic=True)):
+        p = mb.MlpChainProblem(256, 256, 384, single_launch=True, **bad)
+        st = lib.megacu_cuda_mlp_chain_bf16(d, FAKE, ptrs, ptrs, ptrs, FAKE, FAKE, FAKE, FAKE,
+                                            FAKE, FAKE, p.to_c())
+        assert (st.code, st.detail) == (_capi.UNSUPPORTED, 29), bad
+    # the sizes cover the single launch's layout: one plane of 128 x 256 partial
+    # slots per (token block, hidden tile), and its event words
+    t, h, i, layers = 2048, 4096, 1792, 4
+    for n_pes in (1, 8):
+        one = mb.mlp_chain_sizes(mb.MlpChainProblem(t, h, i, layers=layers, single_launch=True),
+                                 n_pes)
+        two = mb.mlp_chain_sizes(mb.MlpChainProblem(t, h, i, layers=layers), n_pes)
+        m_tiles, dn = t // 128, h // 256
+        ws = 0 if n_pes == 1 else m_tiles * dn * 128 * 256 * 2
+        ev = 256 + 4 * (layers * n_pes * dn * 4 + 2 * layers * m_tiles)
+        assert one["workspace"] == max(two["workspace"], ws)
+        assert one["events_down"] == max(two["events_down"], ev)
