@@ -131,6 +131,46 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+class NvlinkCounters:
+    """NVML's NVLink data-throughput counters of one GPU (payload bytes sent
+    and received, summed over its links); `read` gives None where NVML or the
+    fields are unavailable. Reading counters changes no GPU setting."""
+
+    def __init__(self, index):
+        self.nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def read(self):
+        if self.nvml is None:
+            return None
+        p = self.nvml
+        try:
+            ids = []
+            for link in range(p.NVML_NVLINK_MAX_LINKS):
+                ids.append((p.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, link))
+                ids.append((p.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, link))
+            vals = p.nvmlDeviceGetFieldValues(self.handle, ids)
+            tx = rx = 0
+            seen = False
+            for i, v in enumerate(vals):
+                if v.nvmlReturn != p.NVML_SUCCESS:
+                    continue
+                seen = True
+                if i % 2 == 0:
+                    tx += int(v.value.ullVal)
+                else:
+                    rx += int(v.value.ullVal)
+            return (tx * 1024, rx * 1024) if seen else None  # the counters count KiB
+        except Exception:
+            return None
+
+
 # ---------------------------------------------------------------------------
 # CPU leg (oracle on the host cores): the reference arm and cpu_baseline
 # ---------------------------------------------------------------------------
@@ -325,6 +365,37 @@ def run_gpu(args, rank, world, local_rank):
     flops_rank = flops_total / tp
     value = flops_total / (ms_fused * 1e-3) / 1e12
 
+    # ---- NVLink bytes of the fused call (NVML counters, best effort) ----
+    # 20 back-to-back calls between two counter reads; per call and per GB/s
+    # over their CUDA-event time, averaged over the ranks.
+    nvlink = None
+    if tp > 1:
+        counters = NvlinkCounters(local_rank)
+        calls = 20
+        torch.cuda.synchronize()
+        team.barrier(stream)
+        before = counters.read()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(calls):
+            fused()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        after = counters.read()
+        ok = before is not None and after is not None
+        per_call_s = c0.elapsed_time(c1) * 1e-3 / calls
+        tx = (after[0] - before[0]) / calls if ok else 0.0
+        rx = (after[1] - before[1]) / calls if ok else 0.0
+        agg = torch.tensor([tx, rx, 1.0 if ok else 0.0, per_call_s], dtype=torch.float64, device=dev)
+        dist.all_reduce(agg)
+        if agg[2].item() == tp:
+            tx_m, rx_m, _, sec = (agg / tp).tolist()
+            nvlink = {"tx_bytes_per_call": tx_m, "rx_bytes_per_call": rx_m,
+                      "tx_gbs": tx_m / sec / 1e9, "rx_gbs": rx_m / sec / 1e9,
+                      "us_per_call": sec * 1e6,
+                      "source": "NVML NVLINK_THROUGHPUT_DATA_TX/RX summed over links, "
+                                "mean over ranks, 20 back-to-back calls"}
+
     # ---- end to end: pinned host inputs in, output back out ----
     def e2e_body():
         a.copy_(a_host, non_blocking=True)
@@ -395,6 +466,7 @@ def run_gpu(args, rank, world, local_rank):
                 "kernel_without_exchange_us": ms_solo * 1e3,
                 "note": "fused call minus the same kernel on one PE with this PE's K slice "
                         "(no exchange), timed interleaved with the other arms"},
+            "nvlink_measured": nvlink,
             "cpu_baseline": cpu,
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
