@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "gemm_ar_kernel.cuh"
 
@@ -17,13 +18,15 @@ inline constexpr int kLaunchMaxDevices = 64;
 // caps the grid at the pairs that fit on the device at once.
 template <auto Kernel, bool kPair, int kSmem, class... Args>
 cudaError_t launch_persistent(int device, int grid, cudaStream_t stream, Args const &...args) {
-  static bool configured[kLaunchMaxDevices] = {};
-  static int max_pairs[kLaunchMaxDevices] = {};
+  // Per device, set once; host threads may race here harmlessly (the
+  // attribute and the cluster count are the same whoever sets them).
+  static std::atomic<bool> configured[kLaunchMaxDevices] = {};
+  static std::atomic<int> max_pairs[kLaunchMaxDevices] = {};
   bool const known = device >= 0 && device < kLaunchMaxDevices;
-  if (!known || !configured[device]) {
+  if (!known || !configured[device].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
-    if (known) configured[device] = true;
+    if (known) configured[device].store(true, std::memory_order_release);
   }
   if constexpr (!kPair) {
     Kernel<<<grid, kThreads, kSmem, stream>>>(args...);
@@ -40,13 +43,13 @@ cudaError_t launch_persistent(int device, int grid, cudaStream_t stream, Args co
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int pairs = known ? max_pairs[device] : 0;
+    int pairs = known ? max_pairs[device].load(std::memory_order_acquire) : 0;
     if (pairs == 0) {
       cfg.gridDim = dim3(2, 1, 1);
       cudaError_t e = cudaOccupancyMaxActiveClusters(&pairs, Kernel, &cfg);
       if (e != cudaSuccess) return e;
       if (pairs < 1) return cudaErrorInvalidConfiguration;
-      if (known) max_pairs[device] = pairs;
+      if (known) max_pairs[device].store(pairs, std::memory_order_release);
     }
     int const g = std::max(2, std::min(grid / 2, pairs) * 2);
     cfg.gridDim = dim3(static_cast<unsigned>(g), 1, 1);
