@@ -271,7 +271,11 @@ def run_gpu(args, rank, world, local_rank):
     exchange_kind = ("none" if tp == 1 else
                      "in-switch reduction (NVLS multimem) + peer flags" if use_mc else
                      "peer loads / stores over NVLink")
-    out_host = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    # End to end, each rank reads back its own 1/tp of the output rows: every
+    # rank holds the same allreduced result, so the job's result reaches the
+    # host exactly once.
+    rows_back = M // tp
+    out_host = torch.empty((rows_back, N), dtype=torch.bfloat16).pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def call(aa, bb):
@@ -401,7 +405,7 @@ def run_gpu(args, rank, world, local_rank):
         a.copy_(a_host, non_blocking=True)
         b.copy_(b_host, non_blocking=True)
         call(a, b)
-        out_host.copy_(out, non_blocking=True)
+        out_host.copy_(out[rank * rows_back:(rank + 1) * rows_back], non_blocking=True)
 
     (ms_e2e,) = timed_steps([e2e_body], max(3, args.steps // 2), max(1, args.warmup // 2))
     h2d = a_host.numel() * 2 + b_host.numel() * 2
@@ -447,6 +451,7 @@ def run_gpu(args, rank, world, local_rank):
             "tflops_per_gpu": achieved,
             "e2e": {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "readback": "each rank its 1/tp of the output rows (the result once per job)",
                     "ms_per_step": ms_e2e},
             "gpu_launches": args.steps * launches_per_step,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
