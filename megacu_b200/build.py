@@ -15,6 +15,7 @@ the built ``.so`` files sit inside the repository and travel with it:
 from __future__ import annotations
 
 import glob
+import json
 import os
 import shutil
 import subprocess
@@ -93,9 +94,23 @@ def build_harness(verbose: bool = False, force: bool = False) -> str:
     return HARNESS_PATH
 
 
+def reference_root() -> str:
+    """The reference tree named by BASELINE.json (reference_path), if present."""
+    try:
+        with open(os.path.join(ROOT, "BASELINE.json")) as f:
+            path = json.load(f).get("reference_path") or ""
+    except (OSError, ValueError):
+        return ""
+    return path if path and os.path.isdir(path) else ""
+
+
 def build_oracle(verbose: bool = False) -> None:
     """Builds the CPU checker (and the reference builds when the tree exists)."""
-    _run(["make", "-s", "-C", os.path.join(ROOT, "oracle")], verbose)
+    cmd = ["make", "-s", "-C", os.path.join(ROOT, "oracle")]
+    ref = reference_root()
+    if ref:
+        cmd.append(f"REF={ref}")
+    _run(cmd, verbose)
 
 
 def build_all(verbose: bool = False, force: bool = False) -> None:

@@ -6,7 +6,7 @@
 // codes per site (1 invalid problem, 2 missing storage, 10 cudaSetDevice,
 // 11 memset, 12 team barrier, 13 remote PEs without a team backend,
 // 14 launch), a null stream validates only. Detail codes 20+ are B200
-// additions and are listed in megacu_b200.h's users' docs.
+// additions and are listed in megacu_b200.h.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>

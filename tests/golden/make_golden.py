@@ -69,7 +69,11 @@ def kat(ref: str) -> dict:
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    sys.path.insert(0, ROOT)
+    from megacu_b200.build import reference_root
+    ref = sys.argv[1] if len(sys.argv) > 1 else reference_root()
+    if not ref:
+        raise SystemExit("the reference tree (BASELINE.json reference_path) is not present")
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={ref}"],
                    check=True)
     lib = ctypes.CDLL(os.path.join(ROOT, "oracle", "_ref", "libref_host_harness.so"))
