@@ -24,10 +24,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import statistics
-import subprocess
 import sys
-import threading
 import time
 
 import numpy as np
@@ -35,13 +32,12 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from megacu_b200.measure import NVLINK_GBS, ClockSampler, NvlinkCounters, peaks, seeded  # noqa: E402
+
 M, N, K_TOTAL = 4096, 8192, 8192
 WORKLOAD = "C2 row-parallel GEMM+allreduce M4096 N8192 K8192/tp bf16"
 METRIC = "GEMM+allreduce TFLOP/s (whole job), C2 M4096 N8192 K8192 split over tp"
-PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
-FALLBACK_TFLOPS = 1590.0
-NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
 
 
 def env_int(name, default):
@@ -49,126 +45,6 @@ def env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
-
-
-def seeded(seed, shape, std):
-    import torch
-    g = torch.Generator().manual_seed(seed)
-    return (torch.randn(*shape, generator=g, dtype=torch.float32) * std).to(torch.bfloat16)
-
-
-def peaks():
-    """The dense bf16 peak for a kernel timed inside a long run of calls: the
-    measured sustained cuBLAS figure (power-capped clocks), else the burst
-    one, else the fallback."""
-    try:
-        with open(PEAKS_PATH) as f:
-            p = json.load(f)
-        if "bf16_tflops_sustained" in p:
-            return (float(p["bf16_tflops_sustained"]),
-                    "measured (MEASURED_PEAKS.json bf16_tflops_sustained: cuBLAS back to back "
-                    "under the power cap; the timed calls follow a heat-up run)")
-        return float(p["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
-    except Exception:
-        return FALLBACK_TFLOPS, "fallback (1.59 PFLOP/s, no MEASURED_PEAKS.json)"
-
-
-def traffic_for(key):
-    try:
-        with open(TRAFFIC_PATH) as f:
-            return json.load(f).get(key)
-    except Exception:
-        return None
-
-
-class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index):
-        self.index = index
-        self.rows = []
-        self.proc = None
-
-    def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
-                stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except Exception:
-            self.proc = None
-        return self
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([x.strip() for x in line.split(",")])
-
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.thread.join(timeout=2)
-
-    def summary(self):
-        rows = [r for r in self.rows if len(r) >= 9]
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
-
-
-class NvlinkCounters:
-    """NVML's NVLink data-throughput counters of one GPU (payload bytes sent
-    and received, summed over its links); `read` gives None where NVML or the
-    fields are unavailable. Reading counters changes no GPU setting."""
-
-    def __init__(self, index):
-        self.nvml = None
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.nvml = pynvml
-        except Exception:
-            self.nvml = None
-
-    def read(self):
-        if self.nvml is None:
-            return None
-        p = self.nvml
-        try:
-            ids = []
-            for link in range(p.NVML_NVLINK_MAX_LINKS):
-                ids.append((p.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX, link))
-                ids.append((p.NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX, link))
-            vals = p.nvmlDeviceGetFieldValues(self.handle, ids)
-            tx = rx = 0
-            seen = False
-            for i, v in enumerate(vals):
-                if v.nvmlReturn != p.NVML_SUCCESS:
-                    continue
-                seen = True
-                if i % 2 == 0:
-                    tx += int(v.value.ullVal)
-                else:
-                    rx += int(v.value.ullVal)
-            return (tx * 1024, rx * 1024) if seen else None  # the counters count KiB
-        except Exception:
-            return None
 
 
 # ---------------------------------------------------------------------------

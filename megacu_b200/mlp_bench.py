@@ -10,7 +10,8 @@ random weights N(0, 0.02^2), activations N(0, 1); synthetic data.
 
 Three arms, timed interleaved step by step after a common heat-up (L2 flushed
 and the PEs aligned by a team barrier before every step, outside the CUDA
-events; the max over ranks of the mean per step is reported):
+events; each step's time is the max over ranks, and the mean over steps is
+reported):
   two_launches   megacu_cuda_mlp_chain_bf16, two launches per block
   single_launch  the same, all blocks in one persistent launch
   unfused        torch: x @ gate, x @ up (cuBLAS), silu(g) * u, act @ down,
@@ -22,6 +23,8 @@ from __future__ import annotations
 import argparse
 import json
 import os
+
+from .measure import ClockSampler, interleaved, mean
 
 
 def main() -> int:
@@ -102,29 +105,13 @@ def main() -> int:
         flush.fill_(1)
         team.barrier(stream)
 
-    for _ in range(args.heat_calls):
-        for arm in arms:
-            arm()
-    torch.cuda.synchronize()
-    for _ in range(args.warmup):
-        for arm in arms:
-            align()
-            arm()
-    torch.cuda.synchronize()
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)] for _ in arms]
-    for step in range(args.steps):
-        for arm, evs in zip(arms, ev):
-            align()
-            evs[step][0].record(stream)
-            arm()
-            evs[step][1].record(stream)
-    torch.cuda.synchronize()
-    total = torch.tensor([sum(s.elapsed_time(e) for s, e in evs) for evs in ev],
-                         dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(total, op=dist.ReduceOp.MAX)
-    us = [float(v) * 1e3 / args.steps for v in total.tolist()]
+    with ClockSampler(local) as clocks:
+        for _ in range(args.heat_calls):
+            for arm in arms:
+                arm()
+        torch.cuda.synchronize()
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+    us = [mean(v) * 1e3 for v in ms]
     for s in arms_modes:
         mb.events_status(bufs[s]["events_down"], stream)
         mb.events_status(bufs[s]["events_swiglu"], stream)
@@ -138,7 +125,9 @@ def main() -> int:
                 "tp": world, "steps": args.steps, "data": "synthetic",
                 "us_per_call": dict(zip(names, us)),
                 "tflops_per_gpu": {n: flops / (u * 1e-6) / 1e12 for n, u in zip(names, us)},
-                "flops_per_pe": flops, "allreduce_bus_bytes_per_pe": link}
+                "flops_per_pe": flops, "allreduce_bus_bytes_per_pe": link,
+                "l2": "flushed (256 MiB write) before every timed step",
+                "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     team.close()
     if world > 1:

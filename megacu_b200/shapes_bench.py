@@ -1,0 +1,212 @@
+"""Timing of the fused megakernel at BASELINE configs 3 and 4 (bench.py times
+config 2, mlp_bench config 5).
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \\
+        --master-addr 127.0.0.1 --master-port 29700 -m megacu_b200.shapes_bench --config 3
+    ... -m megacu_b200.shapes_bench --config 4 [--m 16,32,64,128]
+
+Config 3: GEMM + reduce-scatter along M (sequence-parallel down-projection),
+M = 8192, N = 8192, K = 28672 split over tp; PE p keeps rows [p M/tp, (p+1)
+M/tp). Config 4: decode-shape GEMM + allreduce, M in {16, 32, 64, 128}, N =
+8192, K = 28672 split over tp (one-shot exchange: one tile row). Inputs bf16
+N(0, 0.02^2), seeded per PE and tensor; synthetic data.
+
+Arms, timed interleaved step by step after a common heat-up, with L2 flushed
+(a 256 MiB write) and the PEs aligned by a team barrier before every step,
+outside the CUDA events; every step's time is the max over ranks:
+  fused                    the megakernel (reduce-scatter or allreduce)
+  unfused                  torch.matmul (cuBLAS), then NCCL reduce_scatter /
+                           all_reduce of its output
+  gemm_only                torch.matmul alone
+  kernel_without_exchange  the megakernel on one PE with this PE's K slice
+                           (tp > 1): the fused time minus this is the
+                           exchange time the kernel did not hide
+Config 3 reports the mean per call, config 4 the p50. Prints one JSON line
+per shape on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+from .measure import (NVLINK_GBS, ClockSampler, hbm_peak, interleaved, mean, p50, peaks,
+                      seeded)
+
+C3 = dict(m=8192, n=8192, k_total=28672)
+C4 = dict(m=(16, 32, 64, 128), n=8192, k_total=28672)
+
+
+def roofline(config, m, n, k, tp, us):
+    """Slower of the GEMM at the measured bf16 peak, the weight stream at the
+    measured HBM bandwidth (it bounds the decode shapes) and the exchange's
+    bytes per PE over NVLink at the measured 770 GB/s per direction."""
+    peak, peak_src = peaks()
+    hbm, hbm_src = hbm_peak()
+    flops = 2.0 * m * n * k
+    out_bytes = m * n * 2
+    if config == 3:
+        link = (tp - 1) / tp * out_bytes          # reduce-scatter bus bytes
+        link_kind = "reduce-scatter (tp-1)/tp x output"
+    else:
+        link = (tp - 1) * out_bytes               # one-shot: every partial to every peer
+        link_kind = "one-shot (tp-1) x output"
+    # Bytes the GEMM must move through HBM at least once: A, B and the
+    # partial / output tile writes.
+    hbm_bytes = 2.0 * (m * k + k * n) + out_bytes
+    terms = {"tensor": flops / (peak * 1e12) * 1e6,
+             "hbm": hbm_bytes / (hbm * 1e9) * 1e6,
+             "nvlink": link / (NVLINK_GBS * 1e9) * 1e6}
+    bound = max(terms, key=terms.get)
+    return {"bound": bound, "terms_us": terms, "roofline_us": terms[bound],
+            "frac": terms[bound] / us, "flops_per_pe": flops, "hbm_bytes_per_pe": hbm_bytes,
+            "link_bytes_per_pe": link, "link": link_kind, "peak_tflops": peak,
+            "peak_source": peak_src, "hbm_gbs": hbm, "hbm_source": hbm_src}
+
+
+def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
+    import torch
+    import torch.distributed as dist
+
+    import megacu_b200 as mb
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    tp = world
+    k = k_total // tp
+    mode = mb.MODE_REDUCE_SCATTER if config == 3 else mb.MODE_ALLREDUCE
+    a = seeded(1000 * config + 10 * rank + 0, (m, k), 0.02).to(dev)
+    b = seeded(1000 * config + 10 * rank + 1, (k, n), 0.02).to(dev)
+    prob = mb.Problem(m, n, k, mode=mode, timeout_ns=30_000_000_000)
+    pl = mb.plan(prob, tp)
+    ws_bytes = max(mb.workspace_bytes(prob, tp), 16)
+    ev_bytes = mb.events_bytes(prob, tp)
+    rows = m // tp if config == 3 else m
+    team = team_cache(ws_bytes + ev_bytes + rows * n * 2 + (64 << 20))
+    ws = team.tensor((ws_bytes,), torch.uint8)
+    events = team.tensor((ev_bytes // 4,), torch.int32)
+    out = team.tensor((rows, n), torch.bfloat16)
+    c = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    c_rs = torch.empty((rows, n), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def fused():
+        mb.gemm_allreduce(a, b, out, workspace=ws, events=events, problem=prob, stream=stream,
+                          device=local, team=team if tp > 1 else None)
+
+    def unfused():
+        torch.matmul(a, b, out=c)
+        if tp > 1:
+            if config == 3:
+                dist.reduce_scatter_tensor(c_rs, c)
+            else:
+                dist.all_reduce(c)
+
+    def gemm_only():
+        torch.matmul(a, b, out=c)
+
+    arms, names = [fused, unfused, gemm_only], ["fused", "unfused", "gemm_only"]
+    solo_events = None
+    if tp > 1:
+        solo_prob = mb.Problem(m, n, k, timeout_ns=30_000_000_000)
+        solo_events = torch.zeros(mb.events_bytes(solo_prob, 1) // 4, dtype=torch.int32,
+                                  device=dev)
+        solo_out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+        def kernel_without_exchange():
+            mb.gemm_allreduce(a, b, solo_out, workspace=None, events=solo_events,
+                              problem=solo_prob, stream=stream, device=local)
+
+        arms.append(kernel_without_exchange)
+        names.append("kernel_without_exchange")
+
+    def align():
+        flush.fill_(1)
+        if tp > 1:
+            team.barrier(stream)
+
+    heat = args.heat_calls if args.heat_calls >= 0 else (200 if config == 3 else 2000)
+    with ClockSampler(local) as clocks:
+        for _ in range(heat):
+            fused()
+            unfused()
+        torch.cuda.synchronize()
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+    mb.events_status(events, stream)
+    if solo_events is not None:
+        mb.events_status(solo_events, stream)
+    stat = mean if config == 3 else p50
+    us = {name: stat(v) * 1e3 for name, v in zip(names, ms)}
+    flops_job = 2.0 * m * n * k_total
+    line = {
+        "workload": (f"C3 GEMM+reduce-scatter M{m} N{n} K{k_total}/tp bf16" if config == 3 else
+                     f"C4 decode GEMM+allreduce M{m} N{n} K{k_total}/tp bf16"),
+        "tp": tp, "m": m, "n": n, "k_per_pe": k, "steps": args.steps, "warmup": args.warmup,
+        "statistic": "mean" if config == 3 else "p50", "data": "synthetic",
+        "us_per_call": us,
+        "tflops_per_gpu": {name: flops_job / tp / (u * 1e-6) / 1e12 for name, u in us.items()},
+        "plan": {"tile": [pl.tile_m, pl.tile_n], "tiles": pl.tiles, "one_shot": pl.one_shot,
+                 "cta_pairs": pl.cta_pairs, "gemm_units": pl.gemm_units},
+        "roofline_call": roofline(config, m, n, k, tp, us["fused"]),
+        "exposed_comm_us": (us["fused"] - us["kernel_without_exchange"]) if tp > 1 else None,
+        "l2": "flushed (256 MiB write) before every timed step",
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    import torch
+    import torch.distributed as dist
+
+    import megacu_b200 as mb
+
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--config", type=int, choices=(3, 4), required=True)
+    ap.add_argument("--m", default="", help="config 4: comma-separated token counts")
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--heat-calls", type=int, default=-1,
+                    help="untimed calls of the fused and unfused arms before timing "
+                         "(default: about two seconds of work)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    teams = []
+
+    def team_cache(heap_bytes):
+        # One team per shape (a team's heap is sized once); the previous one
+        # is closed first, collectively.
+        for t in teams:
+            t.close()
+        teams.clear()
+        teams.append(mb.Team(rank, world, local, heap_bytes,
+                             mb.torch_exchange() if world > 1 else None))
+        return teams[0]
+
+    try:
+        if args.config == 3:
+            run_shape(args, 3, C3["m"], C3["n"], C3["k_total"], rank, world, local, team_cache)
+        else:
+            ms = [int(x) for x in args.m.split(",") if x] or list(C4["m"])
+            for m in ms:
+                run_shape(args, 4, m, C4["n"], C4["k_total"], rank, world, local, team_cache)
+        for t in teams:
+            t.close()
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,40 @@
+"""Host-side arithmetic of the timing tools (no GPU)."""
+import pytest
+
+from megacu_b200 import measure, shapes_bench
+
+
+def test_decode_roofline_is_the_weight_stream(monkeypatch):
+    monkeypatch.setattr(measure, "PEAKS_PATH", "/nonexistent")
+    monkeypatch.setattr(shapes_bench, "peaks", measure.peaks)
+    monkeypatch.setattr(shapes_bench, "hbm_peak", measure.hbm_peak)
+    m, n, k, tp = 16, 8192, 28672 // 8, 8
+    r = shapes_bench.roofline(4, m, n, k, tp, us=10.0)
+    hbm_bytes = 2.0 * (m * k + k * n) + m * n * 2
+    assert r["bound"] == "hbm"
+    assert r["hbm_bytes_per_pe"] == hbm_bytes
+    assert r["terms_us"]["hbm"] == pytest.approx(hbm_bytes / 6650e9 * 1e6)
+    assert r["link_bytes_per_pe"] == 7 * m * n * 2          # one-shot: to every peer
+    assert r["terms_us"]["tensor"] == pytest.approx(2.0 * m * n * k / 1590e12 * 1e6)
+    assert r["frac"] == pytest.approx(r["roofline_us"] / 10.0)
+    assert "fallback" in r["peak_source"] and "fallback" in r["hbm_source"]
+
+
+def test_reduce_scatter_roofline_is_the_gemm():
+    m, n, k, tp = 8192, 8192, 28672 // 8, 8
+    r = shapes_bench.roofline(3, m, n, k, tp, us=300.0)
+    assert r["link_bytes_per_pe"] == pytest.approx(7 / 8 * m * n * 2)
+    assert r["bound"] == "tensor"
+    assert r["flops_per_pe"] == 2.0 * m * n * k
+
+
+def test_clock_summary_reads_reasons():
+    s = measure.ClockSampler(0)
+    assert s.summary()["reasons"] == ["unsampled"]
+    s.rows = [["0", "1500", "1965", "900", "0x4", "Not Active", "Not Active", "Not Active",
+               "Active"],
+              ["0", "1300", "1965", "990", "0x4", "Not Active", "Not Active", "Not Active",
+               "Active"]]
+    out = s.summary()
+    assert out["sm_mhz"] == 1400 and out["sm_max_mhz"] == 1965
+    assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
