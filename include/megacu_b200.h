@@ -52,7 +52,7 @@ typedef struct megacu_status {
  *   20 dtype is not bf16            21 n, k or a buffer not 16-byte aligned
  *   22 unsupported size or tile     23 team size / PE index out of range
  *   24 team handle does not match   25 buffer outside the symmetric heap
- *   26 reduce-scatter m not a multiple of tp * 128
+ *   26 reduce-scatter or all-gather m not a multiple of tp * 128
  *   27 CTA pairs requested but the tile grid cannot hold them
  *   28 workspace / out in the multicast region of a call that cannot reduce
  *      in the switch (not a two-shot bf16-wire allreduce, or only one of them)
@@ -104,8 +104,10 @@ typedef struct megacu_gemm_ar_problem {
 /* ---- bf16 problem descriptor (new; no counterpart in megacu) ------------- */
 
 enum megacu_gemm_ar_mode {
-  MEGACU_MODE_ALLREDUCE = 0,     /* out[m, n] on every PE */
-  MEGACU_MODE_REDUCE_SCATTER = 1 /* PE p holds rows [p*m/tp, (p+1)*m/tp) */
+  MEGACU_MODE_ALLREDUCE = 0,      /* out[m, n] on every PE */
+  MEGACU_MODE_REDUCE_SCATTER = 1, /* PE p holds rows [p*m/tp, (p+1)*m/tp) */
+  MEGACU_MODE_ALLGATHER = 2       /* A gathered along M before the GEMM
+                                     (megacu_cuda_allgather_gemm_bf16) */
 };
 
 enum megacu_gemm_ar_algo {
@@ -156,7 +158,9 @@ typedef struct megacu_gemm_ar_problem_v2 {
                             ticket << 32, tile, start ns, end ns}; kinds 0
                             GEMM tile epilogue, 2 reduce sub-task, 3 worker
                             completion fence, 4 done flags stored, 5 wait
-                            for every PE's done flag */
+                            for every PE's done flag, 6 all-gather copy
+                            chunk (sub = hops to its shard's PE, tile =
+                            shard * (m / tp / 128) + tile row) */
   int64_t trace_capacity; /* records that fit in `trace` */
 } megacu_gemm_ar_problem_v2;
 
@@ -198,6 +202,32 @@ megacu_status megacu_cuda_gemm_allreduce_bf16(
  */
 megacu_status megacu_cuda_gemm_reduce_scatter_bf16(
     megacu_driver_view driver, const void *a, const void *b, void *workspace,
+    void *out, void *events, megacu_gemm_ar_problem_v2 problem);
+
+/*
+ * All-gather of A along M fused with the GEMM that consumes it (the
+ * sequence-parallel input of a column-parallel projection; new, no
+ * counterpart in megacu):
+ *   gathered[m, k] = every PE's a_shard stacked in PE order
+ *   out[m, n]      = gathered @ b (fp32 accumulate, one bf16 rounding)
+ * problem: m = total rows (a multiple of tp * 128), n = this PE's columns
+ * (multiple of 8), k = the full K (multiple of 8); mode is set to
+ * MEGACU_MODE_ALLGATHER; `deterministic` has no effect (nothing is summed
+ * across PEs). a_shard: row-major [m/tp, k] bf16 in the team's symmetric
+ * heap when team_n_pes > 1 (the peers copy it over NVLink); b: [k, n];
+ * gathered: [m, k]; out: [m, n]; all three local. events:
+ * megacu_b200_events_bytes() with mode MEGACU_MODE_ALLGATHER, symmetric,
+ * zero-filled once. No workspace. Inside the launch, worker warps copy the
+ * peers' shards (peer loads, the nearest PEs first) into `gathered` while
+ * the GEMM computes the tiles of rows already present, each tile row
+ * released by a counter of its copied chunks; the call ends once every
+ * peer has copied this PE's shard, so a_shard may be rewritten by the next
+ * stream-ordered work. Event tensor: arrive[p][0][t][q] = epoch per stored
+ * tile quarter; counters[1] counts copy chunks, [3] tiles that waited for
+ * gathered rows, [4] / [5] the "shard copied" flags sent / acquired.
+ */
+megacu_status megacu_cuda_allgather_gemm_bf16(
+    megacu_driver_view driver, const void *a_shard, const void *b, void *gathered,
     void *out, void *events, megacu_gemm_ar_problem_v2 problem);
 
 /* ---- tensor-parallel MLP blocks (new, no counterpart in
@@ -326,10 +356,16 @@ megacu_status megacu_b200_plan_info(megacu_gemm_ar_problem_v2 problem,
 /*
  * Where the device task queue sends raster index r (host only): out[0] tile
  * row, out[1] tile column, out[2] owner PE, out[3] index among the owner's
- * tiles. Tile id = out[0] * n_tiles + out[1].
+ * tiles. Tile id = out[0] * n_tiles + out[1]. For MEGACU_MODE_ALLGATHER the
+ * raster depends on the PE (each starts with its own shard): out[2] is the
+ * PE whose shard holds the tile's rows, out[3] the index within that shard;
+ * megacu_b200_plan_tile answers for PE 0, megacu_b200_plan_tile_on for any.
  */
 megacu_status megacu_b200_plan_tile(megacu_gemm_ar_problem_v2 problem,
                                     int32_t n_pes, int32_t r, int32_t out[4]);
+megacu_status megacu_b200_plan_tile_on(megacu_gemm_ar_problem_v2 problem,
+                                       int32_t n_pes, int32_t my_pe, int32_t r,
+                                       int32_t out[4]);
 
 /*
  * Where a CTA pair's GEMM ticket q goes (host only; plans with pairs):

@@ -22,7 +22,7 @@ TEAM_HANDLE_BYTES = 128
 # status codes (megacu::status_code)
 OK, INVALID_ARGUMENT, UNSUPPORTED, BACKEND_ERROR, LAUNCH_ERROR = range(5)
 STATUS_NAMES = ["ok", "invalid_argument", "unsupported", "backend_error", "launch_error"]
-MODE_ALLREDUCE, MODE_REDUCE_SCATTER = 0, 1
+MODE_ALLREDUCE, MODE_REDUCE_SCATTER, MODE_ALLGATHER = 0, 1, 2
 ALGO_AUTO, ALGO_ONE_SHOT, ALGO_TWO_SHOT = 0, 1, 2
 CTA_PAIRS_AUTO, CTA_PAIRS_OFF, CTA_PAIRS_ON = 0, 1, 2
 DTYPE_BF16 = 2
@@ -90,6 +90,8 @@ _PROTOTYPES = {
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
     "megacu_cuda_gemm_reduce_scatter_bf16":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
+    "megacu_cuda_allgather_gemm_bf16":
+        (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
     "megacu_cuda_gemm_allreduce_bf16_orchestrate":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
     "megacu_cuda_gemm_bf16_noalloc":
@@ -100,6 +102,8 @@ _PROTOTYPES = {
     "megacu_b200_plan_info": (Status, [GemmArProblemV2, c_int32, ctypes.POINTER(c_int32)]),
     "megacu_b200_plan_tile":
         (Status, [GemmArProblemV2, c_int32, c_int32, ctypes.POINTER(c_int32)]),
+    "megacu_b200_plan_tile_on":
+        (Status, [GemmArProblemV2, c_int32, c_int32, c_int32, ctypes.POINTER(c_int32)]),
     "megacu_b200_plan_pair":
         (Status, [GemmArProblemV2, c_int32, c_int32, ctypes.POINTER(c_int32)]),
     "megacu_b200_events_status": (Status, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),

@@ -293,10 +293,12 @@ def plan(problem: Problem, n_pes: int) -> Plan:
                 bool(info[8]), info[9])
 
 
-def plan_tile(problem: Problem, n_pes: int, r: int) -> tuple[int, int, int, int]:
-    """(tile_row, tile_col, owner, local index) of raster index ``r``."""
+def plan_tile(problem: Problem, n_pes: int, r: int, pe: int = 0) -> tuple[int, int, int, int]:
+    """(tile_row, tile_col, owner, local index) of raster index ``r`` on PE
+    ``pe`` (the all-gather raster starts with the PE's own shard; the other
+    modes' rasters are the same on every PE)."""
     out = (ctypes.c_int32 * 4)()
-    check(lib().megacu_b200_plan_tile(problem.to_c(), n_pes, r, out))
+    check(lib().megacu_b200_plan_tile_on(problem.to_c(), n_pes, pe, r, out))
     return tuple(out)
 
 
@@ -332,6 +334,21 @@ def gemm_allreduce(a, b, out, *, workspace, events, problem: Problem, stream=Non
 def gemm_reduce_scatter(a, b, out, *, workspace, events, problem: Problem, **kw) -> None:
     problem.mode = _capi.MODE_REDUCE_SCATTER
     gemm_allreduce(a, b, out, workspace=workspace, events=events, problem=problem, **kw)
+
+
+def allgather_gemm(a_shard, b, gathered, out, *, events, problem: Problem, stream=None,
+                   device: int = 0, team: Optional[Team] = None, trace=None) -> None:
+    """Launches the all-gather + GEMM (async): ``gathered`` [m, k] receives
+    every PE's ``a_shard`` [m / tp, k] in PE order and ``out`` [m, n] =
+    gathered @ b. ``a_shard`` and ``events`` lie in the team's heap when the
+    team has more than one PE; ``problem.mode`` is set to MODE_ALLGATHER."""
+    problem.mode = _capi.MODE_ALLGATHER
+    trace_ptr = _ptr(trace)
+    cap = trace.numel() // 4 if trace is not None else 0
+    d = driver_view(stream, device, team)
+    check(lib().megacu_cuda_allgather_gemm_bf16(d, _ptr(a_shard), _ptr(b), _ptr(gathered),
+                                                 _ptr(out), _ptr(events),
+                                                 problem.to_c(trace_ptr, cap)))
 
 
 # ---- tensor-parallel MLP blocks (BASELINE config 5) ----------------------------------

@@ -111,9 +111,26 @@ struct bf16_plan {
   std::int32_t wire_bytes = 2;
   std::int32_t pairs = 0;       // 1: 2-CTA clusters compute 256-row pair tiles
   std::int32_t gemm_units = 0;  // GEMM tickets per call (tiles, or pair tiles)
+  std::int32_t chunk_rows = 0;  // all-gather: rows per copy chunk
+  std::int32_t chunks_per_block = 0;
   std::int64_t workspace_bytes = 0;
   std::int64_t events_bytes = 0;
 };
+
+// The device schedule's mode of a problem's mode.
+std::int32_t sched_mode(std::int32_t mode) {
+  return mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
+         : mode == MEGACU_MODE_ALLGATHER    ? mode_allgather
+                                            : mode_allreduce;
+}
+
+// All-gather copy chunk: whole rows of A, about 64 KiB (a power of two of
+// rows, so that a 128-row tile row is a whole number of chunks).
+std::int32_t gather_chunk_rows(std::int64_t k) {
+  std::int32_t rows = kBlockM;
+  while (rows > 1 && static_cast<std::int64_t>(rows) * k * 2 > 65536) rows /= 2;
+  return rows;
+}
 
 constexpr std::int32_t kPlanSms = 148;  // plans must not depend on the local device
 constexpr std::int32_t kSwitchCommWarps = 1;
@@ -137,7 +154,8 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
   if (p.tile_m != 0 && p.tile_m != kBlockM) {
     return fail(MEGACU_UNSUPPORTED, 22, "tile_m must be 0 or 128");
   }
-  if (p.mode != MEGACU_MODE_ALLREDUCE && p.mode != MEGACU_MODE_REDUCE_SCATTER) {
+  if (p.mode != MEGACU_MODE_ALLREDUCE && p.mode != MEGACU_MODE_REDUCE_SCATTER &&
+      p.mode != MEGACU_MODE_ALLGATHER) {
     return fail(MEGACU_INVALID_ARGUMENT, 1, "unknown mode");
   }
   if (p.algo < MEGACU_ALGO_AUTO || p.algo > MEGACU_ALGO_TWO_SHOT) {
@@ -169,9 +187,10 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
     return fail(MEGACU_UNSUPPORTED, 22, "too many tiles");
   }
   pl.tiles = static_cast<std::int32_t>(tiles);
-  if (p.mode == MEGACU_MODE_REDUCE_SCATTER) {
+  if (p.mode == MEGACU_MODE_REDUCE_SCATTER || p.mode == MEGACU_MODE_ALLGATHER) {
     if (p.m % (static_cast<std::int64_t>(n_pes) * kBlockM) != 0) {
-      return fail(MEGACU_UNSUPPORTED, 26, "reduce-scatter needs m divisible by tp * 128");
+      return fail(MEGACU_UNSUPPORTED, 26,
+                  "reduce-scatter and all-gather need m divisible by tp * 128");
     }
     pl.one_shot = 0;
   } else if (n_pes == 1) {
@@ -185,14 +204,12 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
     // one-shot moves the same NVLink bytes as two-shot without the gather.
     pl.one_shot = (pl.m_tiles == 1 || n_pes == 2) ? 1 : 0;
   }
-  pl.wire_bytes = p.deterministic ? 4 : 2;
+  // All-gather reduces nothing: its output has one rounding whatever the flag.
+  pl.wire_bytes = (p.deterministic && p.mode != MEGACU_MODE_ALLGATHER) ? 4 : 2;
   // CTA pairs halve each SM's shared-memory operand traffic per MMA (256-row
   // MMAs, B split across the pair); they need pair tiles the grid can hold.
   {
-    tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes,
-                              p.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
-                                                                   : mode_allreduce,
-                              pl.group_m};
+    tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, sched_mode(p.mode), pl.group_m};
     bool const can_pair = pl.tile_n >= 128 && pairs_fit(sched);
     if (p.cta_pairs == MEGACU_CTA_PAIRS_ON && !can_pair) {
       return fail(MEGACU_UNSUPPORTED, 27,
@@ -200,6 +217,17 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
     }
     pl.pairs = (can_pair && p.cta_pairs != MEGACU_CTA_PAIRS_OFF) ? 1 : 0;
     pl.gemm_units = pl.pairs ? pl.tiles / 2 : pl.tiles;
+  }
+  if (p.mode == MEGACU_MODE_ALLGATHER) {
+    // No partials: the gathered A is the caller's buffer. Events: one PE's
+    // arrive plane plus the gather flags and counters.
+    pl.slots_per_src = 0;
+    pl.workspace_bytes = 0;
+    pl.chunk_rows = gather_chunk_rows(p.k);
+    pl.chunks_per_block = kBlockM / pl.chunk_rows;
+    pl.events_bytes = events_bytes_for_gather(n_pes, pl.tiles, pl.m_tiles / n_pes);
+    out = pl;
+    return ok_status();
   }
   // Each PE keeps its own partial of every tile (two parity planes); the
   // tile's reducers read it over NVLink.
@@ -216,6 +244,9 @@ bool aligned16(void const *p) { return (reinterpret_cast<std::uintptr_t>(p) & 15
 megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, void *workspace,
                        void *out, void *events, megacu_gemm_ar_problem_v2 problem) {
   std::int32_t const n_pes = driver.team.team_n_pes;
+  if (problem.mode == MEGACU_MODE_ALLGATHER) {
+    return fail(MEGACU_INVALID_ARGUMENT, 1, "all-gather runs through megacu_cuda_allgather_gemm_bf16");
+  }
   bf16_plan pl;
   megacu_status st = make_plan(problem, n_pes, pl);
   if (st.code != MEGACU_OK) return st;
@@ -329,6 +360,104 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   bool const f32 = pl.wire_bytes == 4;
   e = f32 ? launch_gemm_ar<true>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm)
           : launch_gemm_ar<false>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm);
+  if (e != cudaSuccess) return cuda_fail(e, 14);
+  return ok_status();
+}
+
+// All-gather + GEMM: gathered = every PE's a_shard in PE order, out =
+// gathered @ b (this PE's columns). Validation and launch as run_bf16.
+megacu_status run_allgather(megacu_driver_view driver, void const *a_shard, void const *b,
+                            void *gathered, void *out, void *events,
+                            megacu_gemm_ar_problem_v2 problem) {
+  std::int32_t const n_pes = driver.team.team_n_pes;
+  problem.mode = MEGACU_MODE_ALLGATHER;
+  bf16_plan pl;
+  megacu_status st = make_plan(problem, n_pes, pl);
+  if (st.code != MEGACU_OK) return st;
+  if (a_shard == nullptr || b == nullptr || gathered == nullptr || out == nullptr ||
+      events == nullptr) {
+    return fail(MEGACU_INVALID_ARGUMENT, 2, "missing storage");
+  }
+  if (!aligned16(a_shard) || !aligned16(b) || !aligned16(gathered) || !aligned16(out) ||
+      !aligned16(events)) {
+    return fail(MEGACU_INVALID_ARGUMENT, 21, "buffers must be 16-byte aligned");
+  }
+  std::int32_t const my_pe = driver.team.team_my_pe;
+  if (my_pe < 0 || my_pe >= n_pes) {
+    return fail(MEGACU_INVALID_ARGUMENT, 23, "team_my_pe out of range");
+  }
+  std::int64_t const rows_per_pe = problem.m / n_pes;
+  team_impl *team = nullptr;
+  if (n_pes > 1) {
+    team = as_team(driver.team.team);
+    if (team == nullptr) {
+      return fail(MEGACU_UNSUPPORTED, 13, "remote PEs need a megacu_b200 team in team_view.team");
+    }
+    if (!team->connected || team->n_pes != n_pes || team->my_pe != my_pe) {
+      return fail(MEGACU_INVALID_ARGUMENT, 24, "team handle does not match team_view");
+    }
+    if (!team->contains(a_shard, rows_per_pe * problem.k * 2) ||
+        !team->contains(events, pl.events_bytes)) {
+      return fail(MEGACU_INVALID_ARGUMENT, 25,
+                  "a_shard and events must lie in the team's symmetric heap");
+    }
+  }
+  if (!megacu::cuda::has_stream(megacu::cuda::launch_view{driver.launch.stream,
+                                                          driver.launch.device_ordinal})) {
+    return ok_status();
+  }
+  int const device = driver.launch.device_ordinal;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, 10);
+  if (team != nullptr && team->device != device) {
+    return fail(MEGACU_INVALID_ARGUMENT, 24, "team was created on another device");
+  }
+
+  CUtensorMap map_a, map_b, map_g;
+  if (!encode_bf16_map(&map_a, a_shard, rows_per_pe, problem.k, kBlockM) ||
+      !encode_bf16_map(&map_b, b, problem.k, problem.n, kBlockK) ||
+      !encode_bf16_map(&map_g, gathered, problem.m, problem.k, kBlockM)) {
+    return fail(MEGACU_BACKEND_ERROR, 30, "cuTensorMapEncodeTiled failed");
+  }
+
+  gemm_ar_params prm{};
+  prm.m = static_cast<std::int32_t>(problem.m);
+  prm.n = static_cast<std::int32_t>(problem.n);
+  prm.k = static_cast<std::int32_t>(problem.k);
+  prm.m_tiles = pl.m_tiles;
+  prm.n_tiles = pl.n_tiles;
+  prm.tiles = pl.tiles;
+  prm.n_pes = n_pes;
+  prm.my_pe = my_pe;
+  prm.mode = mode_allgather;
+  prm.one_shot = 0;
+  prm.group_m = pl.group_m;
+  // The copy queue: every chunk of every shard (this PE's own last).
+  prm.n_comm = n_pes * (pl.m_tiles / n_pes) * pl.chunks_per_block;
+  // The dedicated worker warps copy from the start; the GEMM needs the rows
+  // well before the epilogue warps would be free to help.
+  prm.comm_warps = kReduceWarps;
+  prm.rows_per_pe = static_cast<std::int32_t>(rows_per_pe);
+  prm.timeout_ns = problem.timeout_ns != 0 ? problem.timeout_ns : 10000000000ull;
+  prm.out = static_cast<__nv_bfloat16 *>(out);
+  prm.workspace = nullptr;
+  prm.events = static_cast<std::uint32_t *>(events);
+  if (team != nullptr) {
+    prm.peers = team->peers;
+  } else {
+    prm.peers.n_pes = 1;
+    prm.peers.my_pe = 0;
+  }
+  prm.trace = reinterpret_cast<unsigned long long *>(problem.trace);
+  prm.trace_capacity = problem.trace != nullptr ? problem.trace_capacity : 0;
+  prm.a_shard = static_cast<__nv_bfloat16 const *>(a_shard);
+  prm.gathered = static_cast<__nv_bfloat16 *>(gathered);
+  prm.chunk_rows = pl.chunk_rows;
+  prm.chunks_per_block = pl.chunks_per_block;
+
+  int grid = problem.num_ctas > 0 ? problem.num_ctas : sm_count(device);
+  auto stream = static_cast<cudaStream_t>(driver.launch.stream);
+  e = launch_allgather(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, map_g, prm);
   if (e != cudaSuccess) return cuda_fail(e, 14);
   return ok_status();
 }
@@ -567,6 +696,13 @@ extern "C" megacu_status megacu_cuda_gemm_reduce_scatter_bf16(
   return run_bf16(driver, a, b, workspace, out, events, problem);
 }
 
+extern "C" megacu_status megacu_cuda_allgather_gemm_bf16(megacu_driver_view driver,
+                                                         void const *a_shard, void const *b,
+                                                         void *gathered, void *out, void *events,
+                                                         megacu_gemm_ar_problem_v2 problem) {
+  return run_allgather(driver, a_shard, b, gathered, out, events, problem);
+}
+
 namespace {
 
 using bf16_gemm_sig = megacu::status(megacu::cuda_nvshmem::driver_view, void const *, void const *,
@@ -698,33 +834,35 @@ extern "C" megacu_status megacu_b200_plan_pair(megacu_gemm_ar_problem_v2 problem
   if (st.code != MEGACU_OK) return st;
   if (!pl.pairs) return fail(MEGACU_UNSUPPORTED, 27, "this plan computes no CTA pairs");
   if (q < 0 || q >= pl.gemm_units) return fail(MEGACU_INVALID_ARGUMENT, 1, "pair ticket out of range");
-  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes,
-                            problem.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
-                                                                       : mode_allreduce,
-                            pl.group_m};
+  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, sched_mode(problem.mode), pl.group_m};
   out[0] = pair_raster(sched, q, 0);
   out[1] = pair_raster(sched, q, 1);
   return ok_status();
 }
 
-extern "C" megacu_status megacu_b200_plan_tile(megacu_gemm_ar_problem_v2 problem,
-                                               std::int32_t n_pes, std::int32_t r,
-                                               std::int32_t out[4]) {
+extern "C" megacu_status megacu_b200_plan_tile_on(megacu_gemm_ar_problem_v2 problem,
+                                                  std::int32_t n_pes, std::int32_t my_pe,
+                                                  std::int32_t r, std::int32_t out[4]) {
   if (out == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing output");
   bf16_plan pl;
   megacu_status st = make_plan(problem, n_pes, pl);
   if (st.code != MEGACU_OK) return st;
   if (r < 0 || r >= pl.tiles) return fail(MEGACU_INVALID_ARGUMENT, 1, "raster index out of range");
-  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes,
-                            problem.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter
-                                                                       : mode_allreduce,
-                            pl.group_m};
+  if (my_pe < 0 || my_pe >= n_pes) return fail(MEGACU_INVALID_ARGUMENT, 23, "PE out of range");
+  tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, sched_mode(problem.mode), pl.group_m,
+                            problem.mode == MEGACU_MODE_ALLGATHER ? my_pe : 0};
   tile_coord const c = locate(sched, r);
   out[0] = c.tile_row;
   out[1] = c.tile_col;
   out[2] = c.owner;
   out[3] = c.local;
   return ok_status();
+}
+
+extern "C" megacu_status megacu_b200_plan_tile(megacu_gemm_ar_problem_v2 problem,
+                                               std::int32_t n_pes, std::int32_t r,
+                                               std::int32_t out[4]) {
+  return megacu_b200_plan_tile_on(problem, n_pes, 0, r, out);
 }
 
 extern "C" megacu_status megacu_b200_events_status(void *events, void *stream, std::int64_t info[4]) {

@@ -28,7 +28,11 @@
 //    under a bounded wait;
 //  * every partial crosses NVLink as a load by its consumer: producers write
 //    only their own memory (so a GPU-scope fence covers them) and send 4-byte
-//    flags.
+//    flags;
+//  * the all-gather variant (kGather) turns the exchange around: the workers
+//    copy the other PEs' A shards over NVLink into a local gathered A while
+//    the GEMM computes the tiles whose rows are already here, each tile
+//    waiting on a counter of its tile row's copied chunks.
 //
 // No loads here use cluster multicast.
 #pragma once
@@ -100,6 +104,14 @@ struct gemm_ar_params {
   megacu::nvshmem::peer_table peers;
   unsigned long long *trace;
   std::int64_t trace_capacity;
+  // All-gather + GEMM (mode_allgather): this PE's A shard [rows_per_pe, k]
+  // (symmetric: the peers copy it), the gathered A [m, k] (local), and the
+  // copy chunking: chunk_rows whole rows per chunk, chunks_per_block chunks
+  // per 128-row tile row (n_comm = n_pes * tile rows per shard * that).
+  __nv_bfloat16 const *a_shard;
+  __nv_bfloat16 *gathered;
+  std::int32_t chunk_rows;
+  std::int32_t chunks_per_block;
 };
 
 namespace detail {
@@ -133,7 +145,9 @@ __device__ __forceinline__ void count(gemm_ar_params const &p, int which,
 // start ns, end ns} (%globaltimer). Kinds: 0 GEMM tile (epilogue span),
 // 2 reduce sub-task (after its acquire), 3 a worker's completion fence
 // (ticket = its place among the finished workers), 4 this PE's done flags
-// stored, 5 the wait for every PE's done flag.
+// stored, 5 the wait for every PE's done flag, 6 an all-gather copy chunk
+// (sub = how many PEs away its shard is, tile = shard * tile rows per
+// shard + tile row).
 __device__ __forceinline__ void trace(gemm_ar_params const &p, std::uint32_t kind,
                                       std::uint32_t sub, std::uint32_t ticket,
                                       std::uint32_t tile, std::uint64_t t0) {
@@ -427,17 +441,147 @@ __device__ __forceinline__ void wait_all_pushes(gemm_ar_params const &p, std::ui
   }
 }
 
+// Waits until the local counter `*counter` reaches `target` (acquire at GPU
+// scope), or gives up when the abort word is set or `timeout_ns` elapses.
+__device__ __forceinline__ bool wait_at_least(std::uint32_t const *counter, std::uint32_t target,
+                                              std::uint32_t const *abort_word,
+                                              std::uint64_t timeout_ns) {
+  if (ptx::ld_acquire_gpu(counter) >= target) {
+    return true;
+  }
+  std::uint64_t const start = ptx::now_ns();
+  for (std::uint32_t spin = 1;; ++spin) {
+    __nanosleep(spin < 64 ? 32 : 256);
+    if (ptx::ld_relaxed_gpu(counter) >= target && ptx::ld_acquire_gpu(counter) >= target) {
+      return true;
+    }
+    if ((spin & 15u) == 0) {
+      if (ptx::ld_relaxed_gpu(abort_word) != 0) {
+        return false;
+      }
+      if (ptx::now_ns() - start > timeout_ns) {
+        return false;
+      }
+    }
+  }
+}
+
+// All-gather worker: one warp takes copy chunks from the gather queue (the
+// reduce ticket) until it is empty. Ticket t = (slot, tile row rb of the
+// shard, chunk j of the row); slot s copies the shard of the PE s + 1 hops
+// away, the last slot this PE's own shard, so peers' rows arrive in the
+// order the GEMM raster needs them and the PEs start on different sources.
+// A chunk is chunk_rows whole rows of the source shard (one contiguous
+// range), loaded over NVLink (or locally) and stored into those rows of the
+// gathered A. The first chunk a warp takes from a shard waits for the
+// shard's ready flag. After each chunk the tile row's counter is raised with
+// a GPU-scope release (this PE's GEMM producer acquires it before its TMA
+// loads), and the warp that completes a peer's shard tells that peer.
+__device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, std::uint32_t epoch,
+                                             std::uint32_t *my_events, gather_words const &gw,
+                                             std::uint32_t const *abort_word,
+                                             std::uint32_t lane) {
+  control_block *ctrl = control(p);
+  std::int32_t const per_block = p.chunks_per_block;
+  std::int32_t const per_shard = gw.mq * per_block;
+  std::int64_t const chunk_vecs = static_cast<std::int64_t>(p.chunk_rows) * p.k / 8;
+  std::uint32_t seen = 0;  // bit src: src's ready flag acquired by this warp
+  for (;;) {
+    std::uint32_t const ticket = draw_ticket(&ctrl->reduce_ticket, lane);
+    if (ticket >= static_cast<std::uint32_t>(p.n_comm)) {
+      break;
+    }
+    std::int32_t const slot = static_cast<std::int32_t>(ticket) / per_shard;
+    std::int32_t const within = static_cast<std::int32_t>(ticket) % per_shard;
+    std::int32_t const rb = within / per_block;
+    std::int32_t const j = within % per_block;
+    std::int32_t const hops = (slot + 1) % p.n_pes;
+    std::int32_t const src = (p.my_pe + hops) % p.n_pes;
+    bool const remote = src != p.my_pe;
+    if (remote && ((seen >> src) & 1u) == 0) {
+      bool ok = true;
+      if (lane == 0) {
+        ok = wait_flag(my_events + gw.ready(src), epoch, abort_word, p.timeout_ns);
+        if (!ok) record_error(p, err_remote_timeout, static_cast<std::uint32_t>(rb),
+                              static_cast<std::uint32_t>(src), 21);
+      }
+      if (__shfl_sync(0xffffffffu, ok ? 1u : 0u, 0) == 0) {
+        break;
+      }
+      seen |= 1u << src;
+    }
+    __syncwarp();  // every lane's loads after lane 0's acquire
+    std::uint64_t const t0 = ptx::now_ns();
+    std::int64_t const row0 = static_cast<std::int64_t>(rb) * kBlockM +
+                              static_cast<std::int64_t>(j) * p.chunk_rows;
+    __nv_bfloat16 const *shard = remote ? p.peers.translate(p.a_shard, src) : p.a_shard;
+    auto const *from = reinterpret_cast<uint4 const *>(shard + row0 * p.k);
+    auto *to = reinterpret_cast<uint4 *>(
+        p.gathered + (static_cast<std::int64_t>(src) * p.rows_per_pe + row0) * p.k);
+    // Eight 512-byte warp loads in flight, then their stores.
+    for (std::int64_t v0 = 0; v0 < chunk_vecs; v0 += 8 * 32) {
+      uint4 w[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        std::int64_t const v = v0 + u * 32 + lane;
+        w[u] = v < chunk_vecs ? ptx::ld_cg_v4(from + v) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        std::int64_t const v = v0 + u * 32 + lane;
+        if (v < chunk_vecs) ptx::st_v4(to + v, w[u]);
+      }
+    }
+    ptx::fence_acq_rel_gpu();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::red_release_gpu_add(my_events + gw.rows(src, rb), 1u);
+      std::uint32_t const done = atomicAdd(my_events + gw.chunks(src), 1u);
+      if (remote && done + 1 == static_cast<std::uint32_t>(per_shard)) {
+        // Every chunk of src's shard is copied (the other warps' loads are
+        // ordered before their counts): src may overwrite its shard after
+        // this call.
+        ptx::fence_acq_rel_sys();
+        ptx::st_relaxed_sys(p.peers.translate(my_events, src) + gw.read_done(p.my_pe), epoch);
+        count(p, ctr_final_publish, 1);
+      }
+      count(p, ctr_reduce_tasks, 1);
+      trace(p, 6, static_cast<std::uint32_t>(hops), ticket,
+            static_cast<std::uint32_t>(src * gw.mq + rb), t0);
+    }
+  }
+}
+
+// All-gather: the call ends only after every peer has copied this PE's
+// shard, so no later write to the shard (stream-ordered after this call)
+// can race a peer's read of it.
+__device__ __forceinline__ void wait_all_reads(gemm_ar_params const &p, std::uint32_t epoch,
+                                               std::uint32_t *my_events, gather_words const &gw,
+                                               std::uint32_t const *abort_word,
+                                               std::uint32_t lane) {
+  bool ok = true;
+  std::int32_t const pe = static_cast<std::int32_t>(lane);
+  if (pe < p.n_pes && pe != p.my_pe) {
+    ok = wait_flag(my_events + gw.read_done(pe), epoch, abort_word, p.timeout_ns);
+    if (!ok) record_error(p, err_remote_timeout, 0xffffffffu, lane, 22);
+  }
+  if (__all_sync(0xffffffffu, ok) && lane == 0) {
+    count(p, ctr_final_acquire, static_cast<unsigned long long>(p.n_pes - 1));
+  }
+}
+
 }  // namespace detail
 
 // Bounded mbarrier wait; CTA-pair kernels wait with cluster-scope acquire
 // because the other CTA of the pair arrives on some of their barriers.
 template <bool kPair>
 __device__ __forceinline__ bool bar_wait(std::uint64_t *bar, std::uint32_t parity,
-                                         std::uint32_t const *abort_word) {
+                                         std::uint32_t const *abort_word,
+                                         std::uint64_t timeout_ns = kLocalTimeoutNs) {
   if constexpr (kPair) {
-    return ptx::mbar_wait_cluster(bar, parity, abort_word, kLocalTimeoutNs);
+    return ptx::mbar_wait_cluster(bar, parity, abort_word, timeout_ns);
   } else {
-    return ptx::mbar_wait(bar, parity, abort_word, kLocalTimeoutNs);
+    return ptx::mbar_wait(bar, parity, abort_word, timeout_ns);
   }
 }
 
@@ -452,19 +596,27 @@ __device__ __forceinline__ bool bar_wait(std::uint64_t *bar, std::uint32_t parit
 // ready, next task) with remote mbarrier arrives; the follower reports back
 // (task taken, accumulator drained) the same way.
 //
+// kGather = true: all-gather + GEMM (mode_allgather). `map_a` is this PE's
+// A shard, `map_b2` the gathered A [m, k]; tiles of this PE's own shard read
+// the shard, the others the gathered rows once their tile row's counter says
+// every chunk is copied. The epilogue stores the tile into this PE's out
+// (local) and marks its quarters in the arrive plane, as one PE would; the
+// workers run the copies (gather_tasks) instead of reductions.
+//
 // kSwiGLU = true (one PE, no exchange): the gate/up projection of an MLP
 // block. A tile's BN accumulator columns are BN/2 gate columns (B panels from
 // `map_b`) followed by the same BN/2 columns of up (`map_b2`; with pairs the
 // leader stages gate, the follower up); the epilogue stores
 // silu(gate) * up as bf16 into out[m, n] (n = the act columns, tiles of
 // BN/2). Otherwise `map_b2` is unused.
-template <int BN, bool kWireF32, bool kPair = false, bool kSwiGLU = false>
+template <int BN, bool kWireF32, bool kPair = false, bool kSwiGLU = false, bool kGather = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_ar_megakernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_b2,
                        const __grid_constant__ gemm_ar_params p) {
   static_assert(!kSwiGLU || (BN == 256 && !kWireF32), "SwiGLU tiles are 128 x (128 + 128)");
+  static_assert(!kGather || (!kSwiGLU && !kWireF32), "all-gather tiles are plain bf16 tiles");
   using cfg = gemm_config<BN, kPair>;
   constexpr int kWireBytes = kWireF32 ? 4 : 2;
   constexpr int kVecCols = 16 / kWireBytes;                   // columns per 16 B wire vector
@@ -491,7 +643,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::uint32_t const lane = threadIdx.x % 32;
   control_block *ctrl = detail::control(p);
   std::uint32_t const *abort_word = &ctrl->error_code;
-  tile_schedule const sched{p.m_tiles, p.n_tiles, p.n_pes, p.mode, p.group_m};
+  tile_schedule const sched{p.m_tiles, p.n_tiles, p.n_pes, p.mode, p.group_m,
+                            kGather ? p.my_pe : 0};
+  gather_words const gw = gather_layout(p.n_pes, p.tiles, p.m_tiles / p.n_pes);
+  // Bound of the GEMM pipeline's waits. All-gather tiles wait for rows that
+  // come from other GPUs, so there a stage may stay empty as long as a
+  // cross-GPU wait may last.
+  std::uint64_t const pipe_timeout = kGather ? p.timeout_ns + kLocalTimeoutNs : kLocalTimeoutNs;
   std::int32_t const k_blocks = (p.k + kBlockK - 1) / kBlockK;
   // GEMM tickets: tiles, or pair tiles.
   std::int32_t const gemm_units = kPair ? p.tiles / 2 : p.tiles;
@@ -524,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *epoch_slot = ptx::ld_relaxed_gpu(&ctrl->launch_count) + 1u;
     ptx::prefetch_tensor_map(&map_a);
     ptx::prefetch_tensor_map(&map_b);
-    if constexpr (kSwiGLU) ptx::prefetch_tensor_map(&map_b2);
+    if constexpr (kSwiGLU || kGather) ptx::prefetch_tensor_map(&map_b2);
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -546,6 +704,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::uint32_t const parity = epoch & 1u;
   std::uint32_t *const my_events = detail::event_words(p.events);
 
+  if constexpr (kGather) {
+    // This PE's shard (written by earlier work in stream order) is readable:
+    // tell every peer, before any worker of this CTA starts copying.
+    if (blockIdx.x == 0 && warp == kReduceWarp0) {
+      ptx::fence_acq_rel_sys();
+      std::int32_t const pe = static_cast<std::int32_t>(lane);
+      if (pe < p.n_pes && pe != p.my_pe) {
+        ptx::st_relaxed_sys(p.peers.translate(my_events, pe) + gw.ready(p.my_pe), epoch);
+      }
+      __syncwarp();
+    }
+  }
+
   if (warp == 0) {
     // ---------------- task fetcher + TMA producer ----------------
     if (lane == 0) {
@@ -557,7 +728,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (leader) {
           // Fetch the next GEMM ticket into this CTA's ring (and the
           // follower's) once every consumer has taken the slot's last one.
-          if (!bar_wait<kPair>(&task_empty[slot], ((n / kTaskRing) & 1u) ^ 1u, abort_word)) {
+          if (!bar_wait<kPair>(&task_empty[slot], ((n / kTaskRing) & 1u) ^ 1u, abort_word,
+                               pipe_timeout)) {
             detail::record_error(p, err_local_timeout, 0, 0, 1);
             break;
           }
@@ -572,7 +744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::mbar_arrive(&task_full[slot]);
         } else {
           // Follower: take the ticket the leader wrote into this CTA's ring.
-          if (!bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word)) {
+          if (!bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word, pipe_timeout)) {
             detail::record_error(p, err_local_timeout, 0, 1, 1);
             break;
           }
@@ -591,9 +763,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             kSwiGLU ? c.tile_col * (BN / 2)
                     : c.tile_col * BN + static_cast<std::int32_t>(cta_rank) * cfg::b_cols;
         CUtensorMap const *pair_b = (kSwiGLU && cta_rank == 1) ? &map_b2 : &map_b;
+        // A rows: this tile's rows of A, or (all-gather) of this PE's shard
+        // or of the gathered A once their tile row is copied.
+        CUtensorMap const *amap = &map_a;
+        std::int32_t a_row = c.tile_row * kBlockM;
+        if constexpr (kGather) {
+          if (c.owner == p.my_pe) {
+            a_row -= p.my_pe * p.rows_per_pe;
+          } else {
+            amap = &map_b2;
+            std::uint32_t const *rows_copied =
+                my_events + gw.rows(c.owner, c.tile_row - c.owner * gw.mq);
+            if (!detail::wait_at_least(rows_copied, static_cast<std::uint32_t>(p.chunks_per_block),
+                                       abort_word, p.timeout_ns + kLocalTimeoutNs)) {
+              detail::record_error(p, err_remote_timeout, static_cast<std::uint32_t>(r),
+                                   static_cast<std::uint32_t>(c.owner), 23);
+              break;
+            }
+            ptx::fence_proxy_async_global();  // the TMA loads read what the acquire made visible
+            if (cta_rank == 0) detail::count(p, ctr_partial_acquire, kPair ? 2 : 1);
+          }
+        }
         for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
           std::uint32_t const s = it % cfg::stages;
-          if (!bar_wait<kPair>(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word)) {
+          if (!bar_wait<kPair>(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word,
+                               pipe_timeout)) {
             detail::record_error(p, err_local_timeout, r, 0, 2);
             ok = false;
             break;
@@ -611,7 +805,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             std::uint32_t const bar = ptx::map_to_rank(&full[s], 0);
             if (leader) ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
-            ptx::tma_load_2d_pair(&map_a, bar, sa, kb * kBlockK, c.tile_row * kBlockM);
+            ptx::tma_load_2d_pair(amap, bar, sa, kb * kBlockK, a_row);
 #pragma unroll
             for (int panel = 0; panel < cfg::b_cols / 64; ++panel) {
               ptx::tma_load_2d_pair(pair_b, bar, sb + panel * cfg::b_panel_bytes,
@@ -619,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
-            ptx::tma_load_2d(&map_a, &full[s], sa, kb * kBlockK, c.tile_row * kBlockM);
+            ptx::tma_load_2d(amap, &full[s], sa, kb * kBlockK, a_row);
 #pragma unroll
             for (int panel = 0; panel < BN / 64; ++panel) {
               constexpr int kHalf = BN / 128;  // panels per half (SwiGLU)
@@ -651,8 +845,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       std::uint32_t it = 0;
       for (std::uint32_t n = 0;; ++n) {
         std::uint32_t const slot = n % kTaskRing;
-        if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word,
-                            kLocalTimeoutNs)) {
+        if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word, pipe_timeout)) {
           detail::record_error(p, err_local_timeout, 0, 0, 3);
           break;
         }
@@ -662,7 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         std::uint32_t const buf = n & 1u;
-        if (!bar_wait<kPair>(&acc_empty[buf], ((n >> 1) & 1u) ^ 1u, abort_word)) {
+        if (!bar_wait<kPair>(&acc_empty[buf], ((n >> 1) & 1u) ^ 1u, abort_word, pipe_timeout)) {
           detail::record_error(p, err_local_timeout, r, 0, 4);
           break;
         }
@@ -671,7 +864,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
           std::uint32_t const s = it % cfg::stages;
-          if (!bar_wait<kPair>(&full[s], (it / cfg::stages) & 1u, abort_word)) {
+          if (!bar_wait<kPair>(&full[s], (it / cfg::stages) & 1u, abort_word, pipe_timeout)) {
             detail::record_error(p, err_local_timeout, r, 0, 5);
             ok = false;
             break;
@@ -729,7 +922,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       std::uint32_t const slot = n % kTaskRing;
       // Warp-uniform decision: every lane waits, the warp acts on the vote.
       if (!__all_sync(0xffffffffu,
-                      bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word))) {
+                      bar_wait<kPair>(&task_full[slot], (n / kTaskRing) & 1u, abort_word,
+                                      pipe_timeout))) {
         if (lane == 0) detail::record_error(p, err_local_timeout, 0, cta_rank, 6);
         break;
       }
@@ -746,7 +940,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       std::int32_t const r = tile_of(q);
       std::uint32_t const buf = n & 1u;
-      if (!__all_sync(0xffffffffu, bar_wait<kPair>(&acc_full[buf], (n >> 1) & 1u, abort_word))) {
+      if (!__all_sync(0xffffffffu,
+                      bar_wait<kPair>(&acc_full[buf], (n >> 1) & 1u, abort_word, pipe_timeout))) {
         if (lane == 0) detail::record_error(p, err_local_timeout, r, cta_rank, 7);
         break;
       }
@@ -810,7 +1005,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         std::uint32_t v[32];
         ptx::tmem_load_32x32b_x32(t_row + ch * 32, v);
         ptx::tmem_wait_load();
-        if (p.n_pes == 1) {
+        if (kGather || p.n_pes == 1) {
           if (grow < p.m) {
             __nv_bfloat16 *dst = p.out + static_cast<std::int64_t>(grow) * p.n;
 #pragma unroll
@@ -868,8 +1063,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // NVLink), so a GPU-scope fence suffices.
       ptx::fence_acq_rel_gpu();
       __syncwarp();
-      if (p.n_pes == 1) {
-        // One PE: the tile is final as written; mark its quarter arrived.
+      if (kGather || p.n_pes == 1) {
+        // One PE (or all-gather): the tile is final as written; mark its
+        // quarter arrived.
         if (lane == 0) {
           ptx::publish_local_data(my_events + arrive_index(parity, 0, tile, quarter, 1, p.tiles),
                                   epoch);
@@ -881,7 +1077,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             flags + arrive_index(parity, p.my_pe, tile, quarter, p.n_pes, p.tiles), epoch);
       }
       if (lane == 0) {
-        detail::count(p, ctr_partial_publish, p.n_pes == 1 ? 1 : n_dst);
+        detail::count(p, ctr_partial_publish, (kGather || p.n_pes == 1) ? 1 : n_dst);
       }
     }
   }
@@ -892,7 +1088,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // `comm_warps` bounds how many requests a CTA keeps in flight over NVLink:
   // more only deepen the fabric's queues once it is saturated.
   int const first_comm_warp = kThreads / 32 - p.comm_warps;
-  if (p.n_pes > 1 && warp >= first_comm_warp) {
+  if constexpr (kGather) {
+    if (warp >= first_comm_warp) {
+      detail::gather_tasks(p, epoch, my_events, gw, abort_word, lane);
+      if (blockIdx.x == 0 && warp == first_comm_warp) {
+        detail::wait_all_reads(p, epoch, my_events, gw, abort_word, lane);
+      }
+    }
+  } else if (p.n_pes > 1 && warp >= first_comm_warp) {
     int const worker = warp - kEpilogueWarp0;  // 0..7
     std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
     detail::comm_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
@@ -930,6 +1133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ctrl->reduce_ticket = 0;
       ctrl->workers_done = 0;
       ctrl->trace_count = 0;
+      if constexpr (kGather) {
+        std::int64_t const first = gw.counters_first();
+        for (std::int64_t i = 0; i < gw.counters_count(); ++i) my_events[first + i] = 0;
+      }
       ctrl->launch_count = epoch;
       atomicAdd(&ctrl->counters[ctr_launches], 1ull);
       __threadfence();

@@ -57,11 +57,11 @@ cudaError_t launch_persistent(int device, int grid, cudaStream_t stream, Args co
   }
 }
 
-template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false>
+template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false, bool kGather = false>
 cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
                            CUtensorMap const &mb, CUtensorMap const &mb2,
                            gemm_ar_params const &prm) {
-  return launch_persistent<&gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU>, kPair,
+  return launch_persistent<&gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU, kGather>, kPair,
                            gemm_config<BN, kPair>::smem_bytes>(device, grid, stream, ma, mb, mb2,
                                                                prm);
 }
@@ -91,6 +91,24 @@ inline cudaError_t launch_swiglu(bool pairs, int device, int grid, cudaStream_t 
                                  CUtensorMap const &mu, gemm_ar_params const &prm) {
   return pairs ? launch_variant<256, false, true, true>(device, grid, stream, ma, mg, mu, prm)
                : launch_variant<256, false, false, true>(device, grid, stream, ma, mg, mu, prm);
+}
+
+// All-gather + GEMM: `ma` is this PE's A shard, `mg` the gathered A (both
+// with 128-row boxes), `mb` the B operand.
+inline cudaError_t launch_allgather(int tile_n, bool pairs, int device, int grid,
+                                    cudaStream_t stream, CUtensorMap const &ma,
+                                    CUtensorMap const &mb, CUtensorMap const &mg,
+                                    gemm_ar_params const &prm) {
+  switch (tile_n) {
+    case 256:
+      return pairs ? launch_variant<256, false, true, false, true>(device, grid, stream, ma, mb, mg, prm)
+                   : launch_variant<256, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
+    case 128:
+      return pairs ? launch_variant<128, false, true, false, true>(device, grid, stream, ma, mb, mg, prm)
+                   : launch_variant<128, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
+    default:
+      return launch_variant<64, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
+  }
 }
 
 }  // namespace megacu_b200

@@ -18,6 +18,20 @@
 //   and no host barrier; the parity plane lets a PE run one call ahead of a
 //   slow owner in reduce-scatter mode.
 //
+// All-gather + GEMM (mode_allgather) uses the arrive plane of a one-PE call
+// (arrive[p][0][t][q] = epoch once this PE's tile quarter is stored) and
+// then, per PE, a gather region of uint32 words:
+//   ready[src]       = epoch once PE `src` has announced that its A shard is
+//                      readable (set by `src` at the start of its call);
+//   read_done[src]   = epoch once PE `src` has copied all of this PE's shard
+//                      (set by `src`; this PE's call ends only after every
+//                      peer's, so the next writer of the shard cannot race
+//                      a peer still reading it);
+//   rows[shard][rb]  local count of copied chunks of tile row rb of `shard`
+//                      (the GEMM's A operand is ready at chunks_per_block);
+//   chunks[src]      local count of copied chunks of `src`'s shard.
+// The two counter arrays are zeroed by the last CTA of every launch.
+//
 // workspace (symmetric when n_pes > 1): this PE's own partial tiles,
 //   slot[p][t] = the tile_m x tile_n partial of tile t (wire dtype), written
 //   by this PE's epilogue into its own memory and read over NVLink by the
@@ -83,6 +97,40 @@ MEGACU_B200_LAYOUT_HD inline std::int64_t done_index(std::int32_t parity, std::i
                                                    std::int32_t n_pes, std::int32_t tiles) {
   return static_cast<std::int64_t>(2) * n_pes * tiles * kQuarters +
          static_cast<std::int64_t>(parity) * n_pes + src;
+}
+
+// Word indices (after the control block) of the all-gather region.
+struct gather_words {
+  std::int64_t base;     // first word of the region
+  std::int32_t n_pes;
+  std::int32_t mq;       // tile rows per shard
+
+  MEGACU_B200_LAYOUT_HD std::int64_t ready(std::int32_t src) const { return base + src; }
+  MEGACU_B200_LAYOUT_HD std::int64_t read_done(std::int32_t src) const {
+    return base + n_pes + src;
+  }
+  MEGACU_B200_LAYOUT_HD std::int64_t rows(std::int32_t shard, std::int32_t rb) const {
+    return base + 2 * n_pes + static_cast<std::int64_t>(shard) * mq + rb;
+  }
+  MEGACU_B200_LAYOUT_HD std::int64_t chunks(std::int32_t src) const {
+    return base + 2 * n_pes + static_cast<std::int64_t>(n_pes) * mq + src;
+  }
+  // Words of the two counter arrays (rows then chunks), zeroed per launch.
+  MEGACU_B200_LAYOUT_HD std::int64_t counters_first() const { return rows(0, 0); }
+  MEGACU_B200_LAYOUT_HD std::int64_t counters_count() const {
+    return static_cast<std::int64_t>(n_pes) * mq + n_pes;
+  }
+  MEGACU_B200_LAYOUT_HD std::int64_t end() const { return chunks(n_pes); }
+};
+
+MEGACU_B200_LAYOUT_HD inline gather_words gather_layout(std::int32_t n_pes, std::int32_t tiles,
+                                                       std::int32_t mq) {
+  return gather_words{static_cast<std::int64_t>(2) * tiles * kQuarters, n_pes, mq};
+}
+
+inline std::int64_t events_bytes_for_gather(std::int32_t n_pes, std::int32_t tiles,
+                                            std::int32_t mq) {
+  return kControlBytes + 4 * gather_layout(n_pes, tiles, mq).end();
 }
 
 inline std::int64_t events_bytes_for(std::int32_t n_pes, std::int32_t tiles) {

@@ -38,6 +38,12 @@ __device__ __forceinline__ std::uint32_t ld_acquire_sys(std::uint32_t const *p) 
   return v;
 }
 
+__device__ __forceinline__ std::uint32_t ld_acquire_gpu(std::uint32_t const *p) {
+  std::uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ std::uint32_t ld_relaxed_gpu(std::uint32_t const *p) {
   std::uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -82,6 +88,12 @@ __device__ __forceinline__ void publish_local_data(std::uint32_t *flag, std::uin
 // acquires the counter's new value.
 __device__ __forceinline__ void red_release_sys_add(std::uint32_t *p, std::uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
+// Adds `v` to a counter in this GPU's memory with release semantics at GPU
+// scope (readers on this GPU only).
+__device__ __forceinline__ void red_release_gpu_add(std::uint32_t *p, std::uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
 
 // Orders this thread's earlier generic-proxy accesses (and the acquires that

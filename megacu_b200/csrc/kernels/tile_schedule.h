@@ -14,7 +14,15 @@
 // tile rows [q * mq, (q + 1) * mq); raster index r then walks PE (r % n_pes)'s
 // block, so ownership still rotates in time.
 //
-// The same arithmetic is restated in C in oracle/oracle.c (oracle_locate).
+// All-gather + GEMM (mode_allgather) has no owner: every PE computes every
+// tile of its own output columns, and the rows of A arrive shard by shard
+// (PE q's shard is the tile rows [q * mq, (q + 1) * mq)). The raster walks
+// whole shards in the order their rows become available on this PE: its own
+// shard first (`first_shard`), then the next PEs' in turn, each shard in the
+// grouped order; `owner` is the shard the tile's A rows come from.
+//
+// The same arithmetic is restated in C in oracle/oracle.c (oracle_locate,
+// oracle_locate_gather).
 #pragma once
 
 #include <cstdint>
@@ -27,7 +35,7 @@
 
 namespace megacu_b200 {
 
-enum : std::int32_t { mode_allreduce = 0, mode_reduce_scatter = 1 };
+enum : std::int32_t { mode_allreduce = 0, mode_reduce_scatter = 1, mode_allgather = 2 };
 
 struct tile_schedule {
   std::int32_t m_tiles = 0;
@@ -35,6 +43,7 @@ struct tile_schedule {
   std::int32_t n_pes = 1;
   std::int32_t mode = mode_allreduce;
   std::int32_t group_m = 16;
+  std::int32_t first_shard = 0;  // mode_allgather: this PE (its shard comes first)
 
   MEGACU_B200_HD std::int32_t tiles() const { return m_tiles * n_tiles; }
 };
@@ -42,7 +51,8 @@ struct tile_schedule {
 struct tile_coord {
   std::int32_t tile_row = 0;
   std::int32_t tile_col = 0;
-  std::int32_t owner = 0;  // PE that reduces this tile (two-shot / RS)
+  std::int32_t owner = 0;  // PE that reduces this tile (two-shot / RS); all-gather:
+                           // the PE whose shard holds the tile's A rows
   std::int32_t local = 0;  // index of this tile among its owner's tiles
 };
 
@@ -62,6 +72,17 @@ MEGACU_B200_HD void grouped_raster(std::int32_t r, std::int32_t rows, std::int32
 
 MEGACU_B200_HD tile_coord locate(tile_schedule const &s, std::int32_t r) {
   tile_coord c;
+  if (s.mode == mode_allgather) {
+    std::int32_t const mq = s.m_tiles / s.n_pes;
+    std::int32_t const per_shard = mq * s.n_tiles;
+    std::int32_t const d = r / per_shard;
+    c.local = r - d * per_shard;
+    c.owner = (s.first_shard + d) % s.n_pes;
+    std::int32_t row = 0;
+    grouped_raster(c.local, mq, s.n_tiles, s.group_m < mq ? s.group_m : mq, row, c.tile_col);
+    c.tile_row = c.owner * mq + row;
+    return c;
+  }
   c.owner = r % s.n_pes;
   c.local = r / s.n_pes;
   if (s.mode == mode_reduce_scatter) {
@@ -83,12 +104,14 @@ MEGACU_B200_HD tile_coord locate(tile_schedule const &s, std::int32_t r) {
 // raster walks a band's rows column by column, so with an even band height
 // r = 2q and 2q + 1 are such neighbours. Reduce-scatter: PE o's tiles have
 // raster indices local * n_pes + o, and locals 2u, 2u + 1 are neighbours in
-// o's row block.
+// o's row block. All-gather: a shard's tiles are walked like an allreduce
+// raster of its mq tile rows, so with mq and the band height even, r = 2q
+// and 2q + 1 are again neighbours (and in the same shard).
 MEGACU_B200_HD bool pairs_fit(tile_schedule const &s) {
   if (s.group_m % 2 != 0) {
     return false;
   }
-  if (s.mode == mode_reduce_scatter) {
+  if (s.mode == mode_reduce_scatter || s.mode == mode_allgather) {
     return (s.m_tiles / s.n_pes) % 2 == 0;
   }
   return s.m_tiles % 2 == 0;

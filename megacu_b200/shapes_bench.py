@@ -1,28 +1,35 @@
-"""Timing of the fused megakernel at BASELINE configs 3 and 4 (bench.py times
-config 2, mlp_bench config 5).
+"""Timing of the fused megakernel at BASELINE configs 3 and 4, and of the
+all-gather + GEMM (bench.py times config 2, mlp_bench config 5).
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \\
         --master-addr 127.0.0.1 --master-port 29700 -m megacu_b200.shapes_bench --config 3
     ... -m megacu_b200.shapes_bench --config 4 [--m 16,32,64,128]
+    ... -m megacu_b200.shapes_bench --config ag
 
 Config 3: GEMM + reduce-scatter along M (sequence-parallel down-projection),
 M = 8192, N = 8192, K = 28672 split over tp; PE p keeps rows [p M/tp, (p+1)
 M/tp). Config 4: decode-shape GEMM + allreduce, M in {16, 32, 64, 128}, N =
-8192, K = 28672 split over tp (one-shot exchange: one tile row). Inputs bf16
-N(0, 0.02^2), seeded per PE and tensor; synthetic data.
+8192, K = 28672 split over tp (one-shot exchange: one tile row). All-gather
+(`ag`, the symmetric counterpart of config 3: the sequence-parallel input of
+the up-projection): M = 8192 rows gathered from M/tp per PE, K = 8192,
+N = 28672/tp columns per PE. Inputs bf16 N(0, 0.02^2), seeded per PE and
+tensor; synthetic data.
 
 Arms, timed interleaved step by step after a common heat-up, with L2 flushed
 (a 256 MiB write) and the PEs aligned by a team barrier before every step,
 outside the CUDA events; every step's time is the max over ranks:
-  fused                    the megakernel (reduce-scatter or allreduce)
+  fused                    the megakernel (reduce-scatter, allreduce or
+                           all-gather + GEMM)
   unfused                  torch.matmul (cuBLAS), then NCCL reduce_scatter /
-                           all_reduce of its output
+                           all_reduce of its output; for `ag` NCCL
+                           all_gather of A, then torch.matmul
   gemm_only                torch.matmul alone
-  kernel_without_exchange  the megakernel on one PE with this PE's K slice
-                           (tp > 1): the fused time minus this is the
-                           exchange time the kernel did not hide
-Config 3 reports the mean per call, config 4 the p50. Prints one JSON line
-per shape on rank 0.
+  kernel_without_exchange  the megakernel's GEMM on one PE (this PE's K
+                           slice; for `ag` the whole gathered A) (tp > 1):
+                           the fused time minus this is the exchange time
+                           the kernel did not hide
+Configs 3 and ag report the mean per call, config 4 the p50. Prints one JSON
+line per shape on rank 0.
 """
 from __future__ import annotations
 
@@ -35,12 +42,14 @@ from .measure import (NVLINK_GBS, ClockSampler, hbm_peak, interleaved, mean, p50
 
 C3 = dict(m=8192, n=8192, k_total=28672)
 C4 = dict(m=(16, 32, 64, 128), n=8192, k_total=28672)
+AG = dict(m=8192, n_total=28672, k=8192)
 
 
 def roofline(config, m, n, k, tp, us):
     """Slower of the GEMM at the measured bf16 peak, the weight stream at the
     measured HBM bandwidth (it bounds the decode shapes) and the exchange's
-    bytes per PE over NVLink at the measured 770 GB/s per direction."""
+    bytes per PE over NVLink at the measured 770 GB/s per direction. m, n, k
+    are one PE's GEMM (for `ag`, m is the gathered rows)."""
     peak, peak_src = peaks()
     hbm, hbm_src = hbm_peak()
     flops = 2.0 * m * n * k
@@ -48,12 +57,17 @@ def roofline(config, m, n, k, tp, us):
     if config == 3:
         link = (tp - 1) / tp * out_bytes          # reduce-scatter bus bytes
         link_kind = "reduce-scatter (tp-1)/tp x output"
+    elif config == "ag":
+        link = (tp - 1) / tp * m * k * 2          # the other PEs' shards of A, received
+        link_kind = "all-gather (tp-1)/tp x A"
     else:
         link = (tp - 1) * out_bytes               # one-shot: every partial to every peer
         link_kind = "one-shot (tp-1) x output"
     # Bytes the GEMM must move through HBM at least once: A, B and the
-    # partial / output tile writes.
+    # partial / output tile writes (for `ag` also the gathered A's write).
     hbm_bytes = 2.0 * (m * k + k * n) + out_bytes
+    if config == "ag":
+        hbm_bytes += 2.0 * m * k
     terms = {"tensor": flops / (peak * 1e12) * 1e6,
              "hbm": hbm_bytes / (hbm * 1e9) * 1e6,
              "nvlink": link / (NVLINK_GBS * 1e9) * 1e6}
@@ -156,6 +170,96 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         print(json.dumps(line), flush=True)
 
 
+def run_allgather(args, rank, world, local, team_cache):
+    import torch
+    import torch.distributed as dist
+
+    import megacu_b200 as mb
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream()
+    tp = world
+    m, k = AG["m"], AG["k"]
+    n = AG["n_total"] // tp
+    rows = m // tp
+    shard_host = seeded(6000 + 10 * rank + 0, (rows, k), 0.02)
+    b = seeded(6000 + 10 * rank + 1, (k, n), 0.02).to(dev)
+    prob = mb.Problem(m, n, k, mode=mb.MODE_ALLGATHER, timeout_ns=30_000_000_000)
+    pl = mb.plan(prob, tp)
+    ev_bytes = mb.events_bytes(prob, tp)
+    team = team_cache(rows * k * 2 + ev_bytes + (64 << 20))
+    shard = team.tensor((rows, k), torch.bfloat16)
+    shard.copy_(shard_host)
+    events = team.tensor((ev_bytes // 4,), torch.int32)
+    gathered = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    g_nccl = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+    c = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def fused():
+        mb.allgather_gemm(shard, b, gathered, out, events=events, problem=prob, stream=stream,
+                          device=local, team=team if tp > 1 else None)
+
+    def unfused():
+        if tp > 1:
+            dist.all_gather_into_tensor(g_nccl, shard)
+        else:
+            g_nccl.copy_(shard)
+        torch.matmul(g_nccl, b, out=c)
+
+    def gemm_only():
+        torch.matmul(g_nccl, b, out=c)
+
+    arms, names = [fused, unfused, gemm_only], ["fused", "unfused", "gemm_only"]
+    solo_events = None
+    if tp > 1:
+        solo_prob = mb.Problem(m, n, k, timeout_ns=30_000_000_000)
+        solo_events = torch.zeros(mb.events_bytes(solo_prob, 1) // 4, dtype=torch.int32,
+                                  device=dev)
+        solo_out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+        def kernel_without_exchange():
+            mb.gemm_allreduce(g_nccl, b, solo_out, workspace=None, events=solo_events,
+                              problem=solo_prob, stream=stream, device=local)
+
+        arms.append(kernel_without_exchange)
+        names.append("kernel_without_exchange")
+
+    def align():
+        flush.fill_(1)
+        if tp > 1:
+            team.barrier(stream)
+
+    heat = args.heat_calls if args.heat_calls >= 0 else 200
+    with ClockSampler(local) as clocks:
+        for _ in range(heat):
+            fused()
+            unfused()
+        torch.cuda.synchronize()
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+    mb.events_status(events, stream)
+    if solo_events is not None:
+        mb.events_status(solo_events, stream)
+    us = {name: mean(v) * 1e3 for name, v in zip(names, ms)}
+    flops_pe = 2.0 * m * n * k
+    line = {
+        "workload": f"all-gather + GEMM M{m} (M/tp per PE) K{k} N{AG['n_total']}/tp bf16",
+        "tp": tp, "m": m, "n_per_pe": n, "k": k, "steps": args.steps, "warmup": args.warmup,
+        "statistic": "mean", "data": "synthetic",
+        "us_per_call": us,
+        "tflops_per_gpu": {name: flops_pe / (u * 1e-6) / 1e12 for name, u in us.items()},
+        "plan": {"tile": [pl.tile_m, pl.tile_n], "tiles": pl.tiles,
+                 "cta_pairs": pl.cta_pairs, "gemm_units": pl.gemm_units},
+        "roofline_call": roofline("ag", m, n, k, tp, us["fused"]),
+        "exposed_comm_us": (us["fused"] - us["kernel_without_exchange"]) if tp > 1 else None,
+        "l2": "flushed (256 MiB write) before every timed step",
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main() -> int:
     import torch
     import torch.distributed as dist
@@ -163,7 +267,7 @@ def main() -> int:
     import megacu_b200 as mb
 
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--config", type=int, choices=(3, 4), required=True)
+    ap.add_argument("--config", choices=("3", "4", "ag"), required=True)
     ap.add_argument("--m", default="", help="config 4: comma-separated token counts")
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -194,7 +298,9 @@ def main() -> int:
         return teams[0]
 
     try:
-        if args.config == 3:
+        if args.config == "ag":
+            run_allgather(args, rank, world, local, team_cache)
+        elif args.config == "3":
             run_shape(args, 3, C3["m"], C3["n"], C3["k_total"], rank, world, local, team_cache)
         else:
             ms = [int(x) for x in args.m.split(",") if x] or list(C4["m"])

@@ -320,6 +320,94 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
   return rc;
 }
 
+/* ---- all-gather + GEMM (a B200 addition; restates tile_schedule.h's
+ *      mode_allgather raster and layout.h's gather words) ------------------ */
+
+void oracle_locate_gather(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t my_pe,
+                          int32_t group_m, int32_t r, int32_t out[4]) {
+  /* Whole shards in the order their rows are present on PE my_pe: its own
+   * first, then the PEs 1, 2, ... hops further; a shard's tiles in the
+   * grouped order of its mq tile rows. */
+  int32_t const mq = m_tiles / n_pes;
+  int32_t const per_shard = mq * n_tiles;
+  int32_t const d = r / per_shard;
+  int32_t row, col;
+  out[3] = r - d * per_shard;
+  out[2] = (my_pe + d) % n_pes;
+  grouped_raster(out[3], mq, n_tiles, group_m < mq ? group_m : mq, &row, &col);
+  out[0] = out[2] * mq + row;
+  out[1] = col;
+}
+
+int32_t oracle_gather_chunk_rows(int64_t k) {
+  int32_t rows = 128;
+  while (rows > 1 && (int64_t)rows * k * 2 > 65536) rows /= 2;
+  return rows;
+}
+
+int64_t oracle_gather_events_words(int32_t n_pes, int32_t tiles, int32_t mq) {
+  /* arrive[2][1][tiles][4], ready[n_pes], read_done[n_pes], rows[n_pes][mq],
+   * chunks[n_pes] */
+  return (int64_t)2 * tiles * 4 + 3 * (int64_t)n_pes + (int64_t)n_pes * mq;
+}
+
+int oracle_allgather_gemm(const oracle_bf16_problem *p, const float *const *a_shard,
+                          const float *const *b, float *const *gathered, float *const *out,
+                          uint32_t *const *events, uint64_t *counters,
+                          int32_t *const *gemm_order) {
+  int32_t const np = p->n_pes;
+  int64_t const m = p->m, n = p->n, k = p->k;
+  int64_t const rows_per_pe = m / np;
+  int32_t const mt = (int32_t)(m / p->tile_m);
+  int32_t const nt = (int32_t)((n + p->tile_n - 1) / p->tile_n);
+  int32_t const tiles = mt * nt;
+  int32_t const mq = mt / np;
+  uint32_t const epoch = p->epoch;
+  int32_t const parity = (int32_t)(epoch & 1u);
+  int32_t const chunks_per_block = p->tile_m / oracle_gather_chunk_rows(k);
+  int64_t const gw = (int64_t)2 * tiles * 4; /* first word of the gather region */
+  uint64_t local_counters[8 * 8];
+  uint64_t *cnt = counters != NULL ? counters : local_counters;
+  if (m % ((int64_t)np * p->tile_m) != 0) return -1;
+  memset(cnt, 0, sizeof(uint64_t) * 8 * (size_t)np);
+
+  for (int32_t pe = 0; pe < np; ++pe) {
+    /* Every PE announces its shard; every other PE copies all of it
+     * (chunks of whole rows), counting chunks per tile row, then tells the
+     * shard's owner; the counters are zeroed at the end of the launch. */
+    for (int32_t src = 0; src < np; ++src) {
+      memcpy(gathered[pe] + src * rows_per_pe * k, a_shard[src],
+             sizeof(float) * (size_t)(rows_per_pe * k));
+      if (events && src != pe) {
+        events[pe][gw + src] = epoch;      /* ready[src], set by src */
+        events[src][gw + np + pe] = epoch; /* read_done[pe] on src, set by pe */
+      }
+    }
+    cnt[pe * 8 + 1] += (uint64_t)np * mq * chunks_per_block;
+    cnt[pe * 8 + 4] += (uint64_t)(np - 1);
+    cnt[pe * 8 + 5] += (uint64_t)(np - 1);
+    if (events) {
+      for (int64_t w = 0; w < (int64_t)np * mq + np; ++w) events[pe][gw + 2 * np + w] = 0;
+    }
+    oracle_gemm_f32(gathered[pe], b[pe], out[pe], m, n, k, p->threads);
+    /* GEMM tiles in PE pe's raster order, each quarter published locally. */
+    for (int32_t r = 0; r < tiles; ++r) {
+      int32_t c[4];
+      oracle_locate_gather(mt, nt, np, pe, p->group_m, r, c);
+      int32_t const t = c[0] * nt + c[1];
+      if (gemm_order) gemm_order[pe][r] = t;
+      cnt[pe * 8 + 0] += 1;
+      if (c[2] != pe) cnt[pe * 8 + 3] += 1;
+      for (int32_t q = 0; q < 4; ++q) {
+        if (events) events[pe][arrive_idx(parity, 0, t, q, 1, tiles)] = epoch;
+        cnt[pe * 8 + 2] += 1;
+      }
+    }
+    cnt[pe * 8 + 6] += 1;
+  }
+  return 0;
+}
+
 /* ---- CPU-baseline sample: a list of output tiles -------------------------- */
 
 typedef struct tile_job {

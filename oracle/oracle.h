@@ -115,6 +115,34 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
                      uint64_t *counters, int32_t *gemm_order, int32_t *const *reduce_order);
 
 /*
+ * All-gather + GEMM (a B200 addition with no counterpart in megacu, pinned by
+ * this restatement): on every PE p of n_pes, gathered[p] = the a_shard of
+ * every PE stacked in PE order ([m, k], m = n_pes * rows per shard) and
+ * out[p] = gathered[p] @ b[p] ([m, n], fp32 with k ascending, not rounded).
+ * p->m must be a multiple of n_pes * tile_m; mode, one_shot and wire_bytes
+ * are ignored. events[p] (optional): the words after the control block —
+ * arrive[2][1][tiles][4], ready[n_pes], read_done[n_pes], rows[n_pes][mq],
+ * chunks[n_pes] — as the device leaves them after the call (the two counter
+ * arrays zeroed). counters[p * 8 + i] receive the per-call deltas;
+ * gemm_order[p] (optional, [tiles]) the tile id of each of PE p's GEMM
+ * tickets. Returns 0, or -1 if m is not a multiple of n_pes * tile_m.
+ */
+int oracle_allgather_gemm(const oracle_bf16_problem *p, const float *const *a_shard,
+                          const float *const *b, float *const *gathered, float *const *out,
+                          uint32_t *const *events, uint64_t *counters,
+                          int32_t *const *gemm_order);
+
+/* All-gather raster of PE my_pe: r -> out[0] tile row, out[1] tile column,
+ * out[2] the PE whose shard holds the rows, out[3] index within that shard. */
+void oracle_locate_gather(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t my_pe,
+                          int32_t group_m, int32_t r, int32_t out[4]);
+
+/* Rows per all-gather copy chunk for a given K (about 64 KiB, a power of two
+ * dividing 128), and the gather event words after the control block. */
+int32_t oracle_gather_chunk_rows(int64_t k);
+int64_t oracle_gather_events_words(int32_t n_pes, int32_t tiles, int32_t mq);
+
+/*
  * CPU-baseline sample: the summed output of the listed tiles only (full K
  * on every PE, PE-order fp32 sum), written into out_full[m, n] at the tiles'
  * positions. Uses `threads` POSIX threads across the listed tiles.

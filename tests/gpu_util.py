@@ -94,3 +94,33 @@ def trace_records(trace: torch.Tensor):
     ticket = (rec[:, 0] >> 32).astype(np.int64)
     return dict(kind=kind, sub=sub, cta=cta, ticket=ticket, tile=rec[:, 1].astype(np.int64),
                 t0=rec[:, 2], t1=rec[:, 3])
+
+
+def same_process_team(devices, heap=1 << 30):
+    """Teams for PEs on `devices`, one process driving them all (handles
+    exchanged in-process)."""
+    n = len(devices)
+    handles = [None] * n
+    teams = []
+    import ctypes
+    from megacu_b200 import _capi
+    lib = _capi.load()
+    raw = []
+    for pe, dev in enumerate(devices):
+        h = ctypes.c_void_p()
+        mb.check(lib.megacu_b200_team_create(pe, n, dev, heap, ctypes.byref(h)))
+        buf = ctypes.create_string_buffer(_capi.TEAM_HANDLE_BYTES)
+        mb.check(lib.megacu_b200_team_export(h.value, buf))
+        raw.append(h.value)
+        handles[pe] = buf.raw
+    blob = ctypes.create_string_buffer(b"".join(handles), n * _capi.TEAM_HANDLE_BYTES)
+    for pe, dev in enumerate(devices):
+        mb.check(lib.megacu_b200_team_connect(raw[pe], blob))
+        t = mb.Team.__new__(mb.Team)
+        t.my_pe, t.n_pes, t.device, t.handle = pe, n, dev, raw[pe]
+        base, size = ctypes.c_void_p(), ctypes.c_int64()
+        mb.check(lib.megacu_b200_team_info(raw[pe], None, None, ctypes.byref(base),
+                                           ctypes.byref(size)))
+        t.heap_base, t.heap_bytes = base.value, size.value
+        teams.append(t)
+    return teams

@@ -59,6 +59,17 @@ def load():
                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _f32p,
                                          ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
                                          ctypes.POINTER(_f32p), _f32p, ctypes.c_int32]
+        lib.oracle_allgather_gemm.argtypes = [ctypes.POINTER(OracleBf16Problem),
+                                              ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
+                                              ctypes.POINTER(_f32p), ctypes.POINTER(_f32p),
+                                              ctypes.POINTER(ctypes.POINTER(ctypes.c_uint32)),
+                                              ctypes.POINTER(ctypes.c_uint64),
+                                              ctypes.POINTER(ctypes.POINTER(ctypes.c_int32))]
+        lib.oracle_locate_gather.argtypes = [ctypes.c_int32] * 6 + [ctypes.POINTER(ctypes.c_int32)]
+        lib.oracle_gather_chunk_rows.argtypes = [ctypes.c_int64]
+        lib.oracle_gather_chunk_rows.restype = ctypes.c_int32
+        lib.oracle_gather_events_words.argtypes = [ctypes.c_int32] * 3
+        lib.oracle_gather_events_words.restype = ctypes.c_int64
         _lib = lib
     return _lib
 
@@ -187,3 +198,48 @@ def event_tensor_words(n_pes: int, tiles: int) -> int:
     """uint32 words of the event tensor after the control block
     (arrive [2][n_pes][tiles][4], then done [2][n_pes])."""
     return 2 * n_pes * tiles * 4 + 2 * n_pes
+
+
+def locate_gather(m_tiles, n_tiles, n_pes, my_pe, group_m, r):
+    out = (ctypes.c_int32 * 4)()
+    load().oracle_locate_gather(m_tiles, n_tiles, n_pes, my_pe, group_m, r, out)
+    return tuple(out)
+
+
+def gather_chunk_rows(k):
+    return load().oracle_gather_chunk_rows(k)
+
+
+def gather_events_words(n_pes, tiles, m_tiles_per_pe):
+    return load().oracle_gather_events_words(n_pes, tiles, m_tiles_per_pe)
+
+
+def allgather_gemm(a_shards, b_list, *, m, n, k, tile_n, group_m=16, epoch=1, events=None,
+                   threads=0):
+    """The all-gather + GEMM graph for one call on len(a_shards) logical PEs.
+
+    Returns dict(gathered=[...], out=[...], events=[...] or None,
+    counters=(n_pes, 8), gemm_order=[[tiles] per PE]).
+    """
+    n_pes = len(a_shards)
+    a_shards = [np.ascontiguousarray(x, np.float32) for x in a_shards]
+    b_list = [np.ascontiguousarray(x, np.float32) for x in b_list]
+    tiles = (m // 128) * -(-n // tile_n)
+    gathered = [np.zeros((m, k), np.float32) for _ in range(n_pes)]
+    outs = [np.zeros((m, n), np.float32) for _ in range(n_pes)]
+    p = OracleBf16Problem(m, n, k, 128, tile_n, n_pes, 2, 0, group_m, 2,
+                          threads or os.cpu_count() or 1, epoch)
+    evp = None
+    if events is not None:
+        events = [np.ascontiguousarray(e, np.uint32) for e in events]
+        evp = (ctypes.POINTER(ctypes.c_uint32) * n_pes)(
+            *[e.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)) for e in events])
+    counters = np.zeros((n_pes, 8), np.uint64)
+    orders = [np.full(tiles, -1, np.int32) for _ in range(n_pes)]
+    op = (ctypes.POINTER(ctypes.c_int32) * n_pes)(
+        *[o.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)) for o in orders])
+    rc = load().oracle_allgather_gemm(ctypes.byref(p), _fp_array(a_shards), _fp_array(b_list),
+                                      _fp_array(gathered), _fp_array(outs), evp,
+                                      counters.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), op)
+    assert rc == 0, rc
+    return dict(gathered=gathered, out=outs, events=events, counters=counters, gemm_order=orders)

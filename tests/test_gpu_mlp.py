@@ -10,8 +10,7 @@ import torch
 import megacu_b200 as mb
 import oracle_lib
 from conftest import gpu_count
-from gpu_util import REL_TOL, f32, rel_error, seeded_bf16
-from test_gpu_team import _same_process_team
+from gpu_util import REL_TOL, f32, rel_error, same_process_team, seeded_bf16
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(gpu_count() < 1, reason="needs a CUDA GPU")]
@@ -116,7 +115,7 @@ def test_mlp_chain_two_gpus_matches_oracle():
     x = seeded_bf16(91, (t, h), 1.0)
     wg, wu, wd = _weights(92, layers, 2, h, i)
     prob = mb.MlpChainProblem(t, h, i, layers=layers, timeout_ns=5_000_000_000)
-    teams = _same_process_team([0, 1])
+    teams = same_process_team([0, 1])
     calls = []
     for pe, team in enumerate(teams):
         with torch.cuda.device(pe):

@@ -17,40 +17,9 @@ import torch
 import megacu_b200 as mb
 import oracle_lib
 from conftest import gpu_count
-from gpu_util import REL_TOL, f32, inputs, rel_error, wire_scale
+from gpu_util import REL_TOL, f32, inputs, rel_error, same_process_team, wire_scale
 
 pytestmark = pytest.mark.gpu
-
-HEAP = 1 << 30
-
-
-def _same_process_team(devices):
-    """Teams for PEs on `devices`, exchanged in-process."""
-    n = len(devices)
-    handles = [None] * n
-    teams = []
-    import ctypes
-    from megacu_b200 import _capi
-    lib = _capi.load()
-    raw = []
-    for pe, dev in enumerate(devices):
-        h = ctypes.c_void_p()
-        mb.check(lib.megacu_b200_team_create(pe, n, dev, HEAP, ctypes.byref(h)))
-        buf = ctypes.create_string_buffer(_capi.TEAM_HANDLE_BYTES)
-        mb.check(lib.megacu_b200_team_export(h.value, buf))
-        raw.append(h.value)
-        handles[pe] = buf.raw
-    blob = ctypes.create_string_buffer(b"".join(handles), n * _capi.TEAM_HANDLE_BYTES)
-    for pe, dev in enumerate(devices):
-        mb.check(lib.megacu_b200_team_connect(raw[pe], blob))
-        t = mb.Team.__new__(mb.Team)
-        t.my_pe, t.n_pes, t.device, t.handle = pe, n, dev, raw[pe]
-        base, size = ctypes.c_void_p(), ctypes.c_int64()
-        mb.check(lib.megacu_b200_team_info(raw[pe], None, None, ctypes.byref(base),
-                                           ctypes.byref(size)))
-        t.heap_base, t.heap_bytes = base.value, size.value
-        teams.append(t)
-    return teams
 
 
 class TeamCall:
@@ -98,7 +67,7 @@ need2 = pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
     (768, 1024, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 256),   # CTA pairs, two-shot
 ])
 def test_two_gpu_matches_oracle(m, n, k, mode, algo, det, tile_n):
-    teams = _same_process_team([0, 1])
+    teams = same_process_team([0, 1])
     prob = mb.Problem(m, n, k, mode=mode, algo=algo, deterministic=det, tile_n=tile_n,
                       timeout_ns=5_000_000_000)
     call = TeamCall(teams, prob)
@@ -131,7 +100,7 @@ def test_two_gpu_matches_oracle(m, n, k, mode, algo, det, tile_n):
 @need2
 def test_two_gpu_f32_kat_twelve():
     """nvshmem_two_rank_smoke.cc: A = pe + 1, B = 1, K = 4 -> 12, on two GPUs."""
-    teams = _same_process_team([0, 1])
+    teams = same_process_team([0, 1])
     m, n, k = 2, 3, 4
     bufs = []
     for pe, t in enumerate(teams):
@@ -158,7 +127,7 @@ def test_two_gpu_f32_kat_twelve():
 @pytest.mark.skipif(gpu_count() < 1, reason="needs a CUDA GPU")
 def test_missing_peer_times_out_with_status():
     """A flag nothing sets: the bounded wait ends the kernel with an error."""
-    teams = _same_process_team([0, 0])  # PE 1 never launches
+    teams = same_process_team([0, 0])  # PE 1 never launches
     m, n, k = 256, 512, 128
     prob = mb.Problem(m, n, k, algo=mb.ALGO_TWO_SHOT, timeout_ns=200_000_000)
     call = TeamCall(teams, prob)

@@ -38,3 +38,11 @@ def test_clock_summary_reads_reasons():
     out = s.summary()
     assert out["sm_mhz"] == 1400 and out["sm_max_mhz"] == 1965
     assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 2
+
+
+def test_allgather_roofline_counts_the_gathered_rows():
+    m, n, k, tp = 8192, 28672 // 8, 8192, 8
+    r = shapes_bench.roofline("ag", m, n, k, tp, us=400.0)
+    assert r["link_bytes_per_pe"] == pytest.approx(7 / 8 * m * k * 2)
+    assert r["hbm_bytes_per_pe"] == 2.0 * (m * k + k * n) + m * n * 2 + 2.0 * m * k
+    assert r["bound"] == "tensor"
