@@ -16,6 +16,10 @@ struct task_ref {
 struct work_item {
   bool active = false;
   std::int64_t tile_id = 0;
+  // B200 addition: the task this work item belongs to, for dispatchers that
+  // hand out (task, tile) units (co-resident progress); -1 where every task
+  // runs on every tile.
+  int task = -1;
 };
 
 }  // namespace megacu::runtime::device

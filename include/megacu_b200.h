@@ -319,6 +319,29 @@ megacu_status megacu_cuda_gemm_allreduce_f32_orchestrate(
     float *out, void *events, megacu_gemm_ar_problem problem);
 
 /*
+ * megacu's fp32 phase with co-resident persistent progress (a B200
+ * extension). megacu declares progress_model::co_resident_persistent
+ * (include/megacu/runtime.h:18) but its scheduler rejects it
+ * (src/scheduler/explicit_asap.cc:34-39). This entry builds the same
+ * three-task phase as cuda_nvshmem_gemm_allreduce_phased_orchestrate with
+ * that progress model, lowers it with megacu/runtime/co_resident.h (GEMM
+ * tiles, then one allreduce unit per event slot waiting for that slot on
+ * every PE) and runs it as ONE cooperative persistent launch of the generic
+ * device loop. Same arguments, buffers, results and event tensor as
+ * megacu_cuda_gemm_allreduce_phased_f32, plus `control`: device memory of
+ * megacu_b200_co_resident_control_bytes() bytes (the graph and the queue
+ * counters, rewritten by every call; one per concurrent call). A wait that
+ * gave up is reported by megacu_b200_co_resident_status (detail 40; info[0]
+ * node, info[1] tile). Lowering errors keep megacu's status convention
+ * (unsupported/8-10, invalid_argument/2 and /6; see co_resident.h).
+ */
+megacu_status megacu_cuda_gemm_allreduce_f32_co_resident(
+    megacu_driver_view driver, const float *a, const float *b, float *partial,
+    float *out, void *events, void *control, megacu_gemm_ar_problem problem);
+megacu_status megacu_b200_co_resident_control_bytes(int64_t *bytes);
+megacu_status megacu_b200_co_resident_status(void *control, void *stream, int64_t info[2]);
+
+/*
  * Allocation-free single-PE form of megacu_cuda_gemm_allreduce_bf16 (no
  * counterpart in megacu). For callers that cannot allocate device memory for
  * the kernel's scratch: plugin hosts that pass an operator only its inputs

@@ -86,6 +86,11 @@ _PROTOTYPES = {
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblem]),
     "megacu_cuda_gemm_allreduce_f32_orchestrate":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblem]),
+    "megacu_cuda_gemm_allreduce_f32_co_resident":
+        (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                  GemmArProblem]),
+    "megacu_b200_co_resident_control_bytes": (Status, [ctypes.POINTER(c_int64)]),
+    "megacu_b200_co_resident_status": (Status, [c_void_p, c_void_p, ctypes.POINTER(c_int64)]),
     "megacu_cuda_gemm_allreduce_bf16":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
     "megacu_cuda_gemm_reduce_scatter_bf16":

@@ -447,3 +447,28 @@ def cuda_nvshmem_gemm_allreduce_phased_orchestrate(driver: DriverView, a, b, par
     return lib().megacu_cuda_gemm_allreduce_f32_orchestrate(
         driver, _ptr(a), _ptr(b), _ptr(partial), _ptr(out), _ptr(events),
         GemmArProblem(m=m, n=n, k=k, tile_m=tile_m, tile_n=tile_n))
+
+
+def co_resident_control_bytes() -> int:
+    out = ctypes.c_int64()
+    check(lib().megacu_b200_co_resident_control_bytes(ctypes.byref(out)))
+    return out.value
+
+
+def megacu_cuda_gemm_allreduce_f32_co_resident(driver: DriverView, a, b, partial, out, events,
+                                               control, m: int, n: int, k: int, tile_m: int,
+                                               tile_n: int) -> Status:
+    """megacu's fp32 phase with co-resident persistent progress (one
+    cooperative persistent launch; ``control`` holds
+    :func:`co_resident_control_bytes` bytes of device memory)."""
+    return lib().megacu_cuda_gemm_allreduce_f32_co_resident(
+        driver, _ptr(a), _ptr(b), _ptr(partial), _ptr(out), _ptr(events), _ptr(control),
+        GemmArProblem(m=m, n=n, k=k, tile_m=tile_m, tile_n=tile_n))
+
+
+def co_resident_status(control, stream=None) -> list[int]:
+    """Synchronises ``stream``; raises MegacuError (detail 40) if a wait of the
+    last co-resident launch gave up; returns [node, tile] of that wait."""
+    info = (ctypes.c_int64 * 2)()
+    check(lib().megacu_b200_co_resident_status(_ptr(control), _stream_handle(stream), info))
+    return list(info)

@@ -83,7 +83,8 @@ def build_library(verbose: bool = False, force: bool = False) -> str:
 def build_harness(verbose: bool = False, force: bool = False) -> str:
     """Builds the host-runtime test harness against this repository's headers."""
     os.makedirs(os.path.dirname(HARNESS_PATH), exist_ok=True)
-    src = [os.path.join(ROOT, "tests", "cpp", "host_runtime_harness.cc")]
+    src = [os.path.join(ROOT, "tests", "cpp", "host_runtime_harness.cc"),
+           os.path.join(ROOT, "tests", "cpp", "co_resident_harness.cc")]
     src += sorted(glob.glob(os.path.join(PKG, "csrc", "runtime", "*.cc")))
     deps = src + glob.glob(os.path.join(ROOT, "include", "**", "*.h"), recursive=True)
     if force or _stale(HARNESS_PATH, deps):

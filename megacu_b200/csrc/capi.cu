@@ -24,7 +24,9 @@
 #include <megacu/gemm_allreduce.h>
 #include <megacu/platform/cuda/megakernel.cuh>
 #include <megacu/runtime.h>
+#include <megacu/runtime/co_resident.h>
 #include <megacu/runtime/device_entry.cuh>
+#include <megacu/scheduler/co_resident_device.cuh>
 #include <megacu/scheduler/explicit_asap_device.cuh>
 #include <megacu/views.h>
 #include <megacu_b200.h>
@@ -590,6 +592,23 @@ struct f32_program {
   }
 };
 
+// The operator table of the co-resident fp32 graph: node 0 is the GEMM tile
+// producer, node 1 the allreduce tile consumer (the phase's operator tasks
+// in submission order; the sync task is no node).
+struct f32_graph_operators {
+  f32_gemm_tile_task producer;
+  f32_allreduce_tile_task consumer;
+
+  template <class Context, class Task, class Work>
+  __device__ void invoke(Context ctx, Task task, Work work) const {
+    if (task.value == 0) {
+      producer(ctx, work.tile_id);
+    } else if (task.value == 1) {
+      consumer(ctx, work.tile_id);
+    }
+  }
+};
+
 }  // namespace
 
 // ============================================================================
@@ -786,6 +805,125 @@ extern "C" megacu_status megacu_cuda_gemm_allreduce_f32_orchestrate(
   std::memcpy(&p, &problem, sizeof(p));
   return to_c(cuda_nvshmem_gemm_allreduce_phased_orchestrate(to_cpp(driver), a, b, partial, out,
                                                             events, p));
+}
+
+// megacu's fp32 phase (the orchestration of
+// gemm_allreduce_orchestrate_common.h:24-76) with co-resident persistent
+// progress: lowered to one unit graph and run as one cooperative persistent
+// launch, GEMM tiles first, each allreduce tile starting as soon as every
+// PE has published its partial of that tile.
+extern "C" megacu_status megacu_cuda_gemm_allreduce_f32_co_resident(
+    megacu_driver_view driver, float const *a, float const *b, float *partial, float *out,
+    void *events, void *control, megacu_gemm_ar_problem problem) {
+  namespace rt = megacu::runtime;
+  namespace co = megacu::runtime::co_resident;
+  if (problem.m <= 0 || problem.n <= 0 || problem.k <= 0 || problem.tile_m <= 0 ||
+      problem.tile_n <= 0) {
+    return fail(MEGACU_INVALID_ARGUMENT, 1, "invalid problem");
+  }
+  if (a == nullptr || b == nullptr || partial == nullptr || out == nullptr || events == nullptr ||
+      control == nullptr) {
+    return fail(MEGACU_INVALID_ARGUMENT, 2, "missing storage");
+  }
+  std::int32_t const n_pes = driver.team.team_n_pes;
+  std::int32_t const my_pe = driver.team.team_my_pe;
+  if (n_pes < 1 || n_pes > megacu::nvshmem::max_team_pes || my_pe < 0 || my_pe >= n_pes) {
+    return fail(MEGACU_INVALID_ARGUMENT, 23, "invalid team shape");
+  }
+  std::int64_t const m_tiles = (problem.m + problem.tile_m - 1) / problem.tile_m;
+  std::int64_t const n_tiles = (problem.n + problem.tile_n - 1) / problem.tile_n;
+  std::int64_t const tiles = m_tiles * n_tiles;
+
+  // The phase, as megacu's orchestration builds it, with the other progress model.
+  using gemm_sig = megacu::status(gemm_ar_driver, float const *, float const *, float *,
+                                  gemm_ar_problem);
+  using reduce_sig = megacu::status(gemm_ar_driver, float *, float *, gemm_ar_problem);
+  auto d = to_cpp(driver);
+  gemm_ar_problem prob;
+  std::memcpy(&prob, &problem, sizeof(prob));
+  auto phase = rt::make_phase(d, rt::progress_model::co_resident_persistent);
+  auto ready = phase.event_tensor(
+      rt::attrs(rt::events::shape(m_tiles, n_tiles),
+                megacu::cuda_nvshmem::events::symmetric_i32_storage(events),
+                megacu::cuda_nvshmem::events::team_scope()));
+  auto gemm = phase.submit(rt::op<gemm_sig>(ops::gemm_tile_produce::name), d, a, b, partial, prob,
+                           rt::attrs(rt::dispatcher::tile_grid(m_tiles, n_tiles),
+                                     rt::events::publish(ready)));
+  auto joined = phase.sync(rt::attrs(rt::scheduler::depends_on(gemm), rt::events::join(ready)));
+  phase.submit(rt::op<reduce_sig>(ops::allreduce_tile_consume::name), d, partial, out, prob,
+               rt::attrs(rt::scheduler::depends_on(joined), rt::events::acquire(ready)));
+  co::graph g;
+  megacu::status lowered = co::lower_phase(g, phase.tasks(), phase.event_tensors(), phase.progress());
+  if (lowered.code != megacu::status_code::ok) return to_c(lowered);
+
+  if (driver.launch.stream == nullptr) {
+    return ok_status();
+  }
+  team_impl *team = nullptr;
+  if (n_pes > 1) {
+    team = as_team(driver.team.team);
+    if (team == nullptr || !team->connected) {
+      return fail(MEGACU_UNSUPPORTED, 13, "device-side remote path needs a megacu_b200 team");
+    }
+    if (team->n_pes != n_pes || team->my_pe != my_pe) {
+      return fail(MEGACU_INVALID_ARGUMENT, 24, "team handle does not match team_view");
+    }
+    if (!team->contains(partial, problem.m * problem.n * 4) ||
+        !team->contains(events, tiles * n_pes * 4)) {
+      return fail(MEGACU_INVALID_ARGUMENT, 25, "partial and events must be symmetric");
+    }
+  }
+  int const device = driver.launch.device_ordinal;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, 10);
+  auto stream = static_cast<cudaStream_t>(driver.launch.stream);
+  e = cudaMemsetAsync(events, 0, tiles * n_pes * sizeof(int), stream);
+  if (e != cudaSuccess) return cuda_fail(e, 11);
+  if (team != nullptr) {
+    megacu_status st = team_barrier(team, stream);
+    if (st.code != MEGACU_OK) return st;
+  }
+  megacu::nvshmem::peer_table peers{};
+  if (team != nullptr) {
+    peers = team->peers;
+  } else {
+    peers.n_pes = 1;
+    peers.my_pe = 0;
+  }
+  f32_graph_operators ops_table{{a, b, partial, prob}, {partial, out, prob, peers}};
+  e = megacu::scheduler::device::launch_co_resident(
+      g, static_cast<megacu::scheduler::device::co_resident_state *>(control), ops_table, peers,
+      10000000000ull, device, 256, stream);
+  if (e != cudaSuccess) return cuda_fail(e, 14);
+  if (team != nullptr) {
+    // As megacu's launcher: no PE returns while a peer may still read its partial.
+    megacu_status st = team_barrier(team, stream);
+    if (st.code != MEGACU_OK) return st;
+  }
+  return ok_status();
+}
+
+extern "C" megacu_status megacu_b200_co_resident_control_bytes(std::int64_t *bytes) {
+  if (bytes == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing output");
+  *bytes = static_cast<std::int64_t>(sizeof(megacu::scheduler::device::co_resident_state));
+  return ok_status();
+}
+
+extern "C" megacu_status megacu_b200_co_resident_status(void *control, void *stream,
+                                                        std::int64_t info[2]) {
+  if (control == nullptr) return fail(MEGACU_INVALID_ARGUMENT, 2, "missing control");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, 12);
+  auto *state = static_cast<megacu::scheduler::device::co_resident_state *>(control);
+  std::uint32_t word[3] = {0, 0, 0};
+  e = cudaMemcpy(word, &state->error, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, 11);
+  if (info != nullptr) {
+    info[0] = word[1];
+    info[1] = word[2];
+  }
+  if (word[0] == 0) return ok_status();
+  return fail(MEGACU_BACKEND_ERROR, 40, "a co-resident wait timed out");
 }
 
 extern "C" megacu_status megacu_b200_workspace_bytes(megacu_gemm_ar_problem_v2 problem,
