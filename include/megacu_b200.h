@@ -64,6 +64,7 @@ typedef struct megacu_status {
  *   35 no multicast region possible (device, driver, one PE, shared process)
  *   36 multicast region set-up out of order, 37 multicast driver call,
  *   38 multicast object export / hand-over
+ *   39 local rendezvous failed or timed out (megacu_b200_exchange_local)
  *   40 a cross-GPU wait timed out, 41 a local pipeline wait timed out
  *      (megacu_b200_events_status)
  *   50 built-in scratch address lookup, 51 more than one PE,
@@ -451,6 +452,27 @@ megacu_status megacu_b200_team_info(void *team, int32_t *my_pe,
 megacu_status megacu_b200_team_barrier(void *team, void *stream);
 /* Collective when the team has a multicast region (see below). */
 megacu_status megacu_b200_team_destroy(void *team);
+
+/*
+ * Launch adapter for processes on one node (a B200 addition; megacu relies on
+ * NVSHMEM's launcher and lists MPI / torch adapters as future work): every
+ * PE calls with the same `session` (1-64 characters, unique per team, the
+ * role of an NVSHMEM unique id) and its own `bytes`-byte blob; `all`
+ * receives n_pes * bytes, every PE's blob in PE order. Runs over an abstract
+ * unix socket served by PE 0 (so the PEs share a network namespace), bounded
+ * by timeout_ms: a PE that does not join, joins twice or sends another size
+ * makes the PEs that notice it return MEGACU_BACKEND_ERROR / 39. Host only,
+ * no GPU needed.
+ */
+megacu_status megacu_b200_exchange_local(const char *session, int32_t my_pe, int32_t n_pes,
+                                         const void *mine, int64_t bytes, void *all,
+                                         int64_t timeout_ms);
+/* megacu_b200_team_create + _export + megacu_b200_exchange_local + _connect,
+ * collective: a connected team in one call. */
+megacu_status megacu_b200_team_create_local(const char *session, int32_t my_pe,
+                                            int32_t n_pes, int32_t device,
+                                            int64_t heap_bytes, int64_t timeout_ms,
+                                            void **team);
 
 /*
  * Optional multicast (NVLS) region of a connected team, one process per PE:

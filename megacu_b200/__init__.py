@@ -6,7 +6,7 @@ plus the in-tree build. Importing it does not need a GPU; calling a launcher
 does, and fails loudly if the native library is missing.
 """
 from .api import (MegacuError, MlpChainProblem, Plan, Problem, Team, allgather_gemm, check,
-                  co_resident_control_bytes, co_resident_status,
+                  co_resident_control_bytes, co_resident_status, env_team, local_exchange,
                   megacu_cuda_gemm_allreduce_f32_co_resident,
                   cuda_nvshmem_gemm_allreduce_phased_orchestrate, gemm_swiglu, mlp_chain,
                   mlp_chain_sizes, swiglu_events_bytes,
@@ -18,7 +18,7 @@ from ._capi import (ALGO_AUTO, ALGO_ONE_SHOT, ALGO_TWO_SHOT, CTA_PAIRS_AUTO, CTA
 
 __all__ = [
     "MegacuError", "MlpChainProblem", "Plan", "Problem", "Team", "allgather_gemm", "check",
-    "co_resident_control_bytes", "co_resident_status",
+    "co_resident_control_bytes", "co_resident_status", "env_team", "local_exchange",
     "megacu_cuda_gemm_allreduce_f32_co_resident",
     "cuda_nvshmem_gemm_allreduce_phased_orchestrate", "gemm_swiglu", "mlp_chain", "mlp_chain_sizes",
     "swiglu_events_bytes",

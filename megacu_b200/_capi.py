@@ -123,6 +123,11 @@ _PROTOTYPES = {
                   ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64)]),
     "megacu_b200_team_barrier": (Status, [c_void_p, c_void_p]),
     "megacu_b200_team_destroy": (Status, [c_void_p]),
+    "megacu_b200_exchange_local":
+        (Status, [ctypes.c_char_p, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64]),
+    "megacu_b200_team_create_local":
+        (Status, [ctypes.c_char_p, c_int32, c_int32, c_int32, c_int64, c_int64,
+                  ctypes.POINTER(c_void_p)]),
     "megacu_b200_team_multicast_export": (Status, [c_void_p, c_int64, c_void_p]),
     "megacu_b200_team_multicast_connect": (Status, [c_void_p, c_void_p]),
     "megacu_b200_team_multicast_malloc": (Status, [c_void_p, c_int64, ctypes.POINTER(c_void_p)]),

@@ -195,6 +195,41 @@ def torch_exchange(group=None) -> Callable[[bytes], Sequence[bytes]]:
     return exchange
 
 
+def local_exchange(session: str, my_pe: int, n_pes: int,
+                   timeout_ms: int = 60_000) -> Callable[[bytes], Sequence[bytes]]:
+    """Handle exchange among the processes of one node without
+    torch.distributed: every PE passes the same ``session`` string
+    (megacu_b200_exchange_local, an abstract unix socket served by PE 0).
+    Each call of the returned function is one collective exchange."""
+    name = session.encode()
+
+    def exchange(mine: bytes) -> Sequence[bytes]:
+        size = len(mine)
+        out = ctypes.create_string_buffer(size * n_pes)
+        check(lib().megacu_b200_exchange_local(name, my_pe, n_pes, mine, size, out, timeout_ms))
+        raw = out.raw
+        return [raw[i * size:(i + 1) * size] for i in range(n_pes)]
+
+    return exchange
+
+
+def env_team(heap_bytes: int, multicast_bytes: int = 0, timeout_ms: int = 60_000) -> "Team":
+    """A team of the processes torchrun (or any launcher setting LOCAL_RANK /
+    LOCAL_WORLD_SIZE) started on this node, one per GPU, PE = local rank,
+    built without torch.distributed. The session is MEGACU_B200_SESSION if
+    set, else derived from MASTER_ADDR, MASTER_PORT and TORCHELASTIC_RUN_ID."""
+    import os
+    env = os.environ
+    my_pe = int(env.get("LOCAL_RANK", env.get("RANK", "0")))
+    n_pes = int(env.get("LOCAL_WORLD_SIZE", env.get("WORLD_SIZE", "1")))
+    session = env.get("MEGACU_B200_SESSION") or "{}.{}.{}".format(
+        env.get("MASTER_ADDR", "local"), env.get("MASTER_PORT", "0"),
+        env.get("TORCHELASTIC_RUN_ID", "none"))
+    return Team(my_pe, n_pes, my_pe, heap_bytes,
+                local_exchange(session[:64], my_pe, n_pes, timeout_ms) if n_pes > 1 else None,
+                multicast_bytes=multicast_bytes)
+
+
 class _CudaArray:
     def __init__(self, ptr, shape, typestr, owner):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
