@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -90,16 +91,17 @@ megacu_driver_view to_c(megacu::cuda_nvshmem::driver_view d) {
 }
 
 int sm_count(int device) {
-  static int cached[kMaxDevices] = {};
+  // Host threads may race here harmlessly: all store the same value.
+  static std::atomic<int> cached[kMaxDevices] = {};
   if (device < 0 || device >= kMaxDevices) return 148;
-  if (cached[device] == 0) {
-    int n = 0;
+  int n = cached[device].load(std::memory_order_relaxed);
+  if (n == 0) {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) {
       n = 148;
     }
-    cached[device] = n;
+    cached[device].store(n, std::memory_order_relaxed);
   }
-  return cached[device];
+  return n;
 }
 
 // ---- plan of one bf16 call ---------------------------------------------------

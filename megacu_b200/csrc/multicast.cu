@@ -112,10 +112,10 @@ megacu_status fail(megacu_status_code code, std::uint16_t detail, char const *ms
   return {static_cast<std::uint8_t>(code), detail, msg};
 }
 
-// The message names the failed call and its CUresult; it lives in a static
-// buffer (never freed; a later failure overwrites it).
+// The message names the failed call and its CUresult; it lives in a
+// per-thread buffer (never freed; the thread's next failure overwrites it).
 megacu_status driver_fail(std::uint16_t detail, char const *call, CUresult r) {
-  static char message[160];
+  static thread_local char message[160];
   std::snprintf(message, sizeof(message), "%s failed (CUresult %d) in the multicast set-up", call,
                 static_cast<int>(r));
   return fail(MEGACU_BACKEND_ERROR, detail, message);
