@@ -44,3 +44,28 @@ def test_reference_orchestration_validates_through_our_runtime():
     bad = _capi.GemmArProblem(m=0, n=512, k=512, tile_m=128, tile_n=128)
     st = fn(d, FAKE, FAKE, FAKE, FAKE, FAKE, bad)
     assert (st.code, st.detail) == (_capi.INVALID_ARGUMENT, 1)
+
+
+REF_DIR = os.path.join(ROOT, "oracle", "_ref")
+
+
+def run_reference_program(name, **env):
+    """Runs one of megacu's own test programs, built unchanged against this
+    repository's headers and libmegacu_b200.so by oracle/Makefile."""
+    import subprocess
+    path = os.path.join(REF_DIR, name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not built here (no reference tree)")
+    proc = subprocess.run([path], env=dict(os.environ, **env), capture_output=True, text=True,
+                          timeout=120)
+    return proc.returncode, proc.stdout + proc.stderr
+
+
+@pytest.mark.parametrize("name", [
+    "ref_test_components",          # tests/build/runtime_components_contracts.cc
+    "ref_test_surface",             # tests/build/runtime_linked_surface_contract.cc
+    "ref_test_direct_orchestrate",  # tests/runtime/direct_orchestrate_smoke.cc
+])
+def test_reference_host_programs_pass(name):
+    code, out = run_reference_program(name)
+    assert code == 0, out

@@ -40,3 +40,20 @@ def test_reference_orchestration_runs_the_kat():
     want = np.array(kat["expected"], np.float32).reshape(m, n)
     assert np.max(np.abs(out.cpu().numpy() - want)) < kat["tolerance"]
     assert events[:tiles].cpu().tolist() == list(range(1, tiles + 1))
+
+
+def test_reference_cuda_orchestrate_smoke_passes():
+    """tests/runtime/cuda_orchestrate_smoke.cc, unchanged, on our library."""
+    from test_dropin import run_reference_program
+    code, out = run_reference_program("ref_test_cuda_orchestrate", MEGACU_TEST_CUDA_DEVICE="0")
+    assert code == 0, out
+
+
+def test_reference_cuda_multicard_smoke_passes():
+    """tests/runtime/cuda_multicard_smoke.cc, unchanged (exit 77 = fewer than
+    two GPUs, megacu's skip code)."""
+    from test_dropin import run_reference_program
+    code, out = run_reference_program("ref_test_cuda_multicard")
+    if code == 77:
+        pytest.skip("megacu's multicard smoke needs two GPUs")
+    assert code == 0, out
