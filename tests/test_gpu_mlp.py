@@ -3,6 +3,8 @@ CPU oracle: the SwiGLU gate/up projection alone, and chains of blocks on one
 PE and on a two-GPU team (one process, peer exchange)."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -109,12 +111,21 @@ def test_mlp_chain_one_pe_matches_oracle(layers, single, pairs):
     _check_chain(x, wg, wu, wd, out, bufs["x_work"])
 
 
+# The single-launch chain's cross-GPU exchange has not had its first two-GPU
+# run yet: that case runs only with MEGACU_B200_UNVERIFIED=1 until it has.
+_UNVERIFIED = pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
+                                 reason="single-launch chain on two GPUs awaiting its first run "
+                                        "(set MEGACU_B200_UNVERIFIED=1)")
+
+
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-def test_mlp_chain_two_gpus_matches_oracle():
+@pytest.mark.parametrize("single", [False, pytest.param(True, marks=_UNVERIFIED)])
+def test_mlp_chain_two_gpus_matches_oracle(single):
     t, h, i, layers = 256, 256, 192, 2
     x = seeded_bf16(91, (t, h), 1.0)
     wg, wu, wd = _weights(92, layers, 2, h, i)
-    prob = mb.MlpChainProblem(t, h, i, layers=layers, timeout_ns=5_000_000_000)
+    prob = mb.MlpChainProblem(t, h, i, layers=layers, single_launch=single,
+                              timeout_ns=5_000_000_000)
     teams = same_process_team([0, 1])
     calls = []
     for pe, team in enumerate(teams):
