@@ -14,6 +14,11 @@ microseconds from the first traced event of the PE (the first GEMM tile's
 epilogue): GEMM tiles end (median, last), reduce sub-tasks (first start, last
 end, median duration), the workers' completion fences, the done-flag store
 and the final wait (trace kinds 0, 2, 3, 4, 5).
+
+``--allgather`` traces the all-gather + GEMM instead (M = --m rows gathered
+from M/tp per PE, K = --k-total, N = --n columns per PE): GEMM tiles, and the
+copy chunks (kind 6: first start, last end, median duration, and the last end
+per shard distance, so one sees whether the copies stay ahead of the GEMM).
 """
 from __future__ import annotations
 
@@ -42,6 +47,16 @@ def _summary(tr, np):
         out["reduce_first_start_us"] = us(t0[r].min())
         out["reduce_end_us"] = us(t1[r].max())
         out["reduce_task_p50_us"] = round(float(np.percentile(t1[r] - t0[r], 50)) / 1e3, 1)
+    c = tr["kind"] == 6
+    if c.any():
+        out["copy_chunks"] = int(c.sum())
+        out["copy_first_start_us"] = us(t0[c].min())
+        out["copy_end_us"] = us(t1[c].max())
+        out["copy_chunk_p50_us"] = round(float(np.percentile(t1[c] - t0[c], 50)) / 1e3, 1)
+        if "sub" in tr:
+            hops = tr["sub"][c]
+            out["copy_end_by_hops_us"] = {int(h): us(t1[c][hops == h].max())
+                                          for h in sorted(set(hops.tolist()))}
     for kind, name in ((3, "fence"), (4, "done_flags"), (5, "final_wait")):
         k = tr["kind"] == kind
         if k.any():
@@ -63,6 +78,7 @@ def main() -> int:
     ap.add_argument("--k-total", type=int, default=8192)
     ap.add_argument("--calls", type=int, default=200)
     ap.add_argument("--no-multicast", action="store_true")
+    ap.add_argument("--allgather", action="store_true")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", 0))
@@ -71,27 +87,47 @@ def main() -> int:
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
-    m, n, k = args.m, args.n, args.k_total // world
     gen = torch.Generator().manual_seed(100 + rank)
-    a = (torch.randn(m, k, generator=gen) * 0.02).to(torch.bfloat16).cuda()
-    b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
-    prob = mb.Problem(m, n, k, timeout_ns=20_000_000_000)
-    plan = mb.plan(prob, world)
-    ws_bytes, ev_bytes = mb.workspace_bytes(prob, world), mb.events_bytes(prob, world)
-    want_mc = world > 1 and not plan.one_shot and not args.no_multicast
-    team = mb.Team(rank, world, local, ws_bytes + ev_bytes + m * n * 2 + (64 << 20),
-                   mb.torch_exchange() if world > 1 else None,
-                   multicast_bytes=(ws_bytes + m * n * 2 + (1 << 20)) if want_mc else 0)
-    use_mc = want_mc and team.multicast
-    ws = team.tensor((max(ws_bytes, 16),), torch.uint8, multicast=use_mc)
-    events = team.tensor((ev_bytes // 4,), torch.int32)
-    out = team.tensor((m, n), torch.bfloat16, multicast=use_mc)
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    if args.allgather:
+        m, n, k = args.m, args.n, args.k_total
+        prob = mb.Problem(m, n, k, mode=mb.MODE_ALLGATHER, timeout_ns=20_000_000_000)
+        plan = mb.plan(prob, world)
+        ev_bytes = mb.events_bytes(prob, world)
+        team = mb.Team(rank, world, local, (m // world) * k * 2 + ev_bytes + (64 << 20),
+                       mb.torch_exchange() if world > 1 else None)
+        use_mc = False
+        shard = team.tensor((m // world, k), torch.bfloat16)
+        shard.copy_((torch.randn(m // world, k, generator=gen) * 0.02).to(torch.bfloat16))
+        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+        events = team.tensor((ev_bytes // 4,), torch.int32)
+        gathered = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
+        out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
 
-    def call(trace=None):
-        mb.gemm_allreduce(a, b, out, workspace=ws, events=events, problem=prob, stream=stream,
-                          device=local, team=team if world > 1 else None, trace=trace)
+        def call(trace=None):
+            mb.allgather_gemm(shard, b, gathered, out, events=events, problem=prob, stream=stream,
+                              device=local, team=team if world > 1 else None, trace=trace)
+    else:
+        m, n, k = args.m, args.n, args.k_total // world
+        a = (torch.randn(m, k, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+        prob = mb.Problem(m, n, k, timeout_ns=20_000_000_000)
+        plan = mb.plan(prob, world)
+        ws_bytes, ev_bytes = mb.workspace_bytes(prob, world), mb.events_bytes(prob, world)
+        want_mc = world > 1 and not plan.one_shot and not args.no_multicast
+        team = mb.Team(rank, world, local, ws_bytes + ev_bytes + m * n * 2 + (64 << 20),
+                       mb.torch_exchange() if world > 1 else None,
+                       multicast_bytes=(ws_bytes + m * n * 2 + (1 << 20)) if want_mc else 0)
+        use_mc = want_mc and team.multicast
+        ws = team.tensor((max(ws_bytes, 16),), torch.uint8, multicast=use_mc)
+        events = team.tensor((ev_bytes // 4,), torch.int32)
+        out = team.tensor((m, n), torch.bfloat16, multicast=use_mc)
+
+        def call(trace=None):
+            mb.gemm_allreduce(a, b, out, workspace=ws, events=events, problem=prob,
+                              stream=stream, device=local, team=team if world > 1 else None,
+                              trace=trace)
 
     def timed(trace=None):
         flush.fill_(1)
@@ -106,14 +142,20 @@ def main() -> int:
     for _ in range(args.calls):
         call()
     times = [timed() for _ in range(10)]
-    trace = torch.zeros(plan.tiles * 64 * 4, dtype=torch.int64, device="cuda")
+    # records: GEMM tiles, reduce sub-tasks (16 per tile at most) or copy
+    # chunks (up to 128 per tile row and shard), and a few per worker
+    trace = torch.zeros((plan.tiles * 64 + plan.m_tiles * 128) * 4, dtype=torch.int64,
+                        device="cuda")
     traced_us = timed(trace)
     mb.events_status(events, stream)
     rec = trace.view(-1, 4).cpu().numpy().astype(np.uint64)
     rec = rec[rec[:, 3] != 0]
-    tr = {"kind": (rec[:, 0] & 0xFF).astype(np.int64), "t0": rec[:, 2], "t1": rec[:, 3]}
-    info = {"pe": rank, "tp": world, "exchange": "in-switch" if use_mc else
-            ("peer" if world > 1 else "none"), "call_us_median": round(float(np.median(times)), 1),
+    tr = {"kind": (rec[:, 0] & 0xFF).astype(np.int64), "sub": ((rec[:, 0] >> 8) & 0xFF).astype(
+        np.int64), "t0": rec[:, 2], "t1": rec[:, 3]}
+    exchange = ("all-gather copies" if args.allgather else "in-switch" if use_mc else
+                "peer" if world > 1 else "none")
+    info = {"pe": rank, "tp": world, "exchange": exchange,
+            "call_us_median": round(float(np.median(times)), 1),
             "traced_call_us": round(traced_us, 1)}
     info.update(_summary(tr, np))
     infos = [info]
