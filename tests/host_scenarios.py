@@ -48,7 +48,7 @@ def scenarios() -> list[dict]:
                   mode=1),
     ]
     rng = random.Random(20261201)
-    for i in range(24):
+    for i in range(150):
         n = rng.randint(1, 20)
         kinds = [1 if rng.random() < 0.3 else 0 for _ in range(n)]
         deps = []
@@ -60,8 +60,11 @@ def scenarios() -> list[dict]:
         ev_attr = [rng.randint(0, 7) for _ in range(n)]
         n_events = rng.randint(0, 3)
         events = [[rng.randint(1, 9), rng.randint(1, 9)] for _ in range(n_events)]
+        # from the 25th on, also a rejected progress model or a failing body
+        progress = 1 if i >= 24 and rng.random() < 0.1 else 0
+        fail_at = rng.randrange(n) if i >= 24 and rng.random() < 0.15 else -1
         out.append(_scenario(f"random_{i}", kinds, deps, grids, ev_attr, events,
-                             mode=rng.randint(0, 1)))
+                             mode=rng.randint(0, 1), progress=progress, fail_at=fail_at))
     return out
 
 
