@@ -496,7 +496,7 @@ megacu_status megacu_b200_team_multicast_malloc(void *team, int64_t bytes, void 
 /* base = NULL and bytes = 0 when the team has no multicast region. */
 megacu_status megacu_b200_team_multicast_info(void *team, void **base, int64_t *bytes);
 
-/* ---- component link anchors (megacu src/*: last line of each file) ------- */
+/* ---- component link anchors (last line of each megacu component source) -- */
 
 int megacu_dispatcher_explicit_attrs_component(void);
 int megacu_scheduler_explicit_asap_component(void);

@@ -4,6 +4,7 @@ stream means "validate only", megacu_gemm_allreduce_phased.cu:160-165)."""
 from __future__ import annotations
 
 import ctypes
+import os
 
 import pytest
 
@@ -115,3 +116,29 @@ def test_status_layout_matches_cpp():
     assert ctypes.sizeof(_capi.Status) == 16
     assert ctypes.sizeof(_capi.DriverView) == 64
     assert ctypes.sizeof(_capi.GemmArProblem) == 32
+
+
+def test_header_is_plain_c_and_links():
+    """include/megacu_b200.h is a C header: a C99 translation unit that calls
+    every declared function compiles warning-free and links against the
+    library (the binding a C, cgo or FFI host would make)."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    from megacu_b200 import build
+    names = _capi.declared_functions()
+    body = "\n".join(f"  (void)&{n};" for n in names)
+    src = f"#include <megacu_b200.h>\nint main(void) {{\n{body}\n  return 0;\n}}\n"
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "abi.c")
+        with open(path, "w") as f:
+            f.write(src)
+        cmd = [cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror",
+               "-I" + os.path.join(build.ROOT, "include"), path, "-L" + build.LIB_DIR,
+               "-lmegacu_b200", "-o", os.path.join(tmp, "abi")]
+        proc = subprocess.run(cmd, capture_output=True, text=True)
+        assert proc.returncode == 0, proc.stderr
