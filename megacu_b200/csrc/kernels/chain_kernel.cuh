@@ -79,40 +79,44 @@ struct chain_params {
   std::int64_t trace_capacity;
 };
 
-// Event words after the control block: arrive[l][src][DN tile][quarter],
-// then act_ready[l][row], then x_ready[l][row].
+// Event words after the control block: arrive[l][src][DN tile][quarter]
+// (DN tile = row * dn_tiles_n + column, m_tiles * dn_tiles_n of them), then
+// act_ready[l][row], then x_ready[l][row].
 MEGACU_B200_CHAIN_HD std::int64_t chain_arrive_index(std::int32_t l, std::int32_t src,
                                                      std::int32_t tile, std::int32_t q,
-                                                     std::int32_t n_pes, std::int32_t dn_tiles) {
+                                                     std::int32_t n_pes, std::int32_t dn_tiles_n,
+                                                     std::int32_t m_tiles) {
+  std::int64_t const dn_tiles = static_cast<std::int64_t>(m_tiles) * dn_tiles_n;
   return ((static_cast<std::int64_t>(l) * n_pes + src) * dn_tiles + tile) * 4 + q;
 }
 
 MEGACU_B200_CHAIN_HD std::int64_t chain_counters_base(std::int32_t layers, std::int32_t n_pes,
-                                                      std::int32_t dn_tiles) {
-  return static_cast<std::int64_t>(layers) * n_pes * dn_tiles * 4;
+                                                      std::int32_t dn_tiles_n,
+                                                      std::int32_t m_tiles) {
+  return static_cast<std::int64_t>(layers) * n_pes * m_tiles * dn_tiles_n * 4;
 }
 
 MEGACU_B200_CHAIN_HD std::int64_t chain_act_ready_index(std::int32_t l, std::int32_t row,
                                                         std::int32_t layers, std::int32_t n_pes,
-                                                        std::int32_t dn_tiles,
+                                                        std::int32_t dn_tiles_n,
                                                         std::int32_t m_tiles) {
-  return chain_counters_base(layers, n_pes, dn_tiles) + static_cast<std::int64_t>(l) * m_tiles +
-         row;
+  return chain_counters_base(layers, n_pes, dn_tiles_n, m_tiles) +
+         static_cast<std::int64_t>(l) * m_tiles + row;
 }
 
 MEGACU_B200_CHAIN_HD std::int64_t chain_x_ready_index(std::int32_t l, std::int32_t row,
                                                       std::int32_t layers, std::int32_t n_pes,
-                                                      std::int32_t dn_tiles,
+                                                      std::int32_t dn_tiles_n,
                                                       std::int32_t m_tiles) {
-  return chain_counters_base(layers, n_pes, dn_tiles) +
+  return chain_counters_base(layers, n_pes, dn_tiles_n, m_tiles) +
          static_cast<std::int64_t>(layers + l) * m_tiles + row;
 }
 
 MEGACU_B200_CHAIN_HD std::int64_t chain_events_bytes(std::int32_t layers, std::int32_t n_pes,
-                                                     std::int32_t dn_tiles,
+                                                     std::int32_t dn_tiles_n,
                                                      std::int32_t m_tiles) {
   return kControlBytes +
-         4 * (chain_counters_base(layers, n_pes, dn_tiles) +
+         4 * (chain_counters_base(layers, n_pes, dn_tiles_n, m_tiles) +
               2 * static_cast<std::int64_t>(layers) * m_tiles);
 }
 
@@ -235,8 +239,9 @@ __device__ __forceinline__ void exchange(chain_params const &p, tile_schedule co
     bool ok = true;
     if (static_cast<std::int32_t>(lane) < p.n_pes) {
       ok = detail::wait_flag(
-          my_events + chain_arrive_index(layer, lane, tile, quarter, p.n_pes, p.dn_tiles_n), epoch,
-          abort_word, p.timeout_ns);
+          my_events + chain_arrive_index(layer, lane, tile, quarter, p.n_pes, p.dn_tiles_n,
+                                         p.m_tiles),
+          epoch, abort_word, p.timeout_ns);
       if (!ok) record_error(p, err_remote_timeout, tile, lane, 18);
     }
     if (!__all_sync(0xffffffffu, ok)) break;
@@ -741,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           std::uint32_t *flags = p.peers.translate(my_events, c.owner);
           ptx::publish_local_data(flags + chain_arrive_index(j.layer, p.my_pe, dn_tile, quarter,
-                                                             p.n_pes, p.dn_tiles_n),
+                                                             p.n_pes, p.dn_tiles_n, p.m_tiles),
                                   epoch);
         }
         chain_detail::count(p, ctr_partial_publish, 1);

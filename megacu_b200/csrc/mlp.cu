@@ -309,7 +309,8 @@ megacu_status run_chain_single_launch(megacu_driver_view driver, void const *x,
   auto stream = static_cast<cudaStream_t>(driver.launch.stream);
   // The dependency counters start at zero in every launch; no peer reaches
   // this PE's counters before this launch has published its own partials.
-  std::int64_t const counters = chain_counters_base(problem.layers, n_pes, pl.dn_tiles_n);
+  std::int64_t const counters =
+      chain_counters_base(problem.layers, n_pes, pl.dn_tiles_n, pl.m_tiles);
   e = cudaMemsetAsync(static_cast<char *>(events) + kControlBytes + 4 * counters, 0,
                       4 * 2 * static_cast<std::int64_t>(problem.layers) * pl.m_tiles, stream);
   if (e != cudaSuccess) return cuda_fail(e, 11);

@@ -82,6 +82,7 @@ def test_single_launch_chain_limits_and_sizes():
         two = mb.mlp_chain_sizes(mb.MlpChainProblem(t, h, i, layers=layers), n_pes)
         m_tiles, dn = t // 128, h // 256
         ws = 0 if n_pes == 1 else m_tiles * dn * 128 * 256 * 2
-        ev = 256 + 4 * (layers * n_pes * dn * 4 + 2 * layers * m_tiles)
+        # arrive flags per (block, source PE, DN tile of the whole grid, quarter)
+        ev = 256 + 4 * (layers * n_pes * m_tiles * dn * 4 + 2 * layers * m_tiles)
         assert one["workspace"] == max(two["workspace"], ws)
         assert one["events_down"] == max(two["events_down"], ev)
