@@ -30,7 +30,8 @@
 // publishing or acquiring more than one event tensor, or an event tensor
 // published by two tasks -> unsupported/9; an acquired event tensor that no
 // task publishes, or whose slots differ from the acquiring or publishing
-// task's tiles -> invalid_argument/6; unit count overflow -> unsupported/10.
+// task's tiles, or that is published or acquired without storage ->
+// invalid_argument/6; unit count overflow -> unsupported/10.
 #pragma once
 
 #include <cstdint>

@@ -188,6 +188,16 @@ status lower(graph &out, std::span<linked_task const> tasks,
     }
   }
 
+  // A tensor that is published or acquired on the device needs its storage.
+  for (std::int32_t e = 0; e < g.event_count; ++e) {
+    bool used = g.events[e].publisher >= 0;
+    for (std::int32_t n = 0; n < g.node_count; ++n) used = used || g.nodes[n].acquire == e;
+    if (used && g.events[e].storage == nullptr) {
+      return fail(status_code::invalid_argument, 6,
+                  "an event tensor used on the device needs symmetric_i32_storage");
+    }
+  }
+
   // Waits: per tile for the acquired tensor, per node for the rest.
   for (std::int32_t n = 0; n < g.node_count; ++n) {
     node &nd = g.nodes[n];

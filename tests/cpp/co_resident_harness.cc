@@ -23,24 +23,30 @@ extern "C" {
 // 1 sync task; deps: 8 per task, -1 = none; tile_grid[i * 2 + {0,1}] when
 // > 0 in the first entry) with `n_events` event tensors of shape
 // event_shape[e * 2 + {0, 1}]; ev[i * 3 + {0, 1, 2}]: the event tensor task
-// i publishes / acquires / joins, -1 = none. progress 0 asap, 1
+// i publishes / acquires / joins, -1 = none; bit e of storage_mask gives
+// event tensor e a (never dereferenced) storage attribute. progress 0 asap, 1
 // co_resident_persistent. Lowers it; outputs the status (code, detail), the
 // graph header (node_count, units, event_count) and per node (8 int64 each):
 // phase task, publish, acquire, wait mask, units, first unit, queue position,
 // and per event (2 int64): slots, publisher.
 int harness_co_resident(int n, const std::int32_t *kinds, const std::int32_t *deps,
                         const std::int64_t *tile_grid, const std::int32_t *ev, int n_events,
-                        const std::int64_t *event_shape, int progress, std::int32_t status_out[2],
+                        const std::int64_t *event_shape, std::uint32_t storage_mask,
+                        int progress, std::int32_t status_out[2],
                         std::int64_t header[3], std::int64_t *nodes, std::int64_t *events) {
   namespace rt = megacu::runtime;
   namespace co = megacu::runtime::co_resident;
   fake_driver driver{};
   auto phase = rt::make_phase(driver, progress == 0 ? rt::progress_model::asap
                                                     : rt::progress_model::co_resident_persistent);
+  static int storage[1];
   rt::event_tensor_ref evs[16];
   for (int e = 0; e < n_events && e < 16; ++e) {
-    evs[e] = phase.event_tensor(
-        rt::attrs(rt::events::shape(event_shape[2 * e], event_shape[2 * e + 1])));
+    auto set = rt::attrs(rt::events::shape(event_shape[2 * e], event_shape[2 * e + 1]));
+    if ((storage_mask >> e) & 1u) {
+      set.push(megacu::cuda_nvshmem::events::symmetric_i32_storage(storage));
+    }
+    evs[e] = phase.event_tensor(set);
   }
   for (int i = 0; i < n; ++i) {
     rt::attr_set set;

@@ -18,7 +18,7 @@ def lib():
     return ctypes.CDLL(build.build_harness())
 
 
-def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1):
+def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1, storage=0xFFFF):
     n = len(kinds)
     grids = grids or [[0, 0]] * n
     ev = ev or [[-1, -1, -1]] * n
@@ -34,7 +34,8 @@ def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1):
         n, (i32 * max(n, 1))(*kinds), (i32 * max(len(flat), 1))(*flat),
         (i64 * max(2 * n, 1))(*[v for g in grids for v in g]),
         (i32 * max(3 * n, 1))(*[v for e in ev for v in e]), len(events),
-        (i64 * max(2 * len(events), 1))(*[v for e in events for v in e]), progress, status,
+        (i64 * max(2 * len(events), 1))(*[v for e in events for v in e]), storage, progress,
+        status,
         header, nodes, evs)
     out = dict(status=list(status), node_count=header[0], units=header[1])
     out["nodes"] = [dict(task=nodes[8 * k], publish=nodes[8 * k + 1], acquire=nodes[8 * k + 2],
@@ -108,6 +109,14 @@ def test_unit_ranges_follow_the_asap_order(lib):
 ])
 def test_rejections(lib, kinds, deps, grids, ev, events, want):
     assert lower(lib, kinds, deps, grids, ev, events)["status"] == want
+
+
+def test_device_event_tensors_need_storage(lib):
+    args = ([0, 0], [[], [0]], [[1, 2], [1, 2]], [[0, -1, -1], [-1, 0, -1]], [[1, 2]])
+    assert lower(lib, *args)["status"] == [0, 0]
+    assert lower(lib, *args, storage=0)["status"] == [1, 6]
+    # a tensor nobody publishes or acquires on the device may go without
+    assert lower(lib, [0], [[]], events=[[1, 2]], storage=0)["status"] == [0, 0]
 
 
 def test_node_capacity(lib):
