@@ -128,13 +128,7 @@ std::int32_t sched_mode(std::int32_t mode) {
                                             : mode_allreduce;
 }
 
-// All-gather copy chunk: whole rows of A, about 64 KiB (a power of two of
-// rows, so that a 128-row tile row is a whole number of chunks).
-std::int32_t gather_chunk_rows(std::int64_t k) {
-  std::int32_t rows = kBlockM;
-  while (rows > 1 && static_cast<std::int64_t>(rows) * k * 2 > 65536) rows /= 2;
-  return rows;
-}
+
 
 constexpr std::int32_t kPlanSms = 148;  // plans must not depend on the local device
 constexpr std::int32_t kSwitchCommWarps = 1;

@@ -483,7 +483,7 @@ __device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, std::uint3
                                              std::uint32_t lane) {
   control_block *ctrl = control(p);
   std::int32_t const per_block = p.chunks_per_block;
-  std::int32_t const per_shard = gw.mq * per_block;
+  std::int32_t const per_shard = gw.mq * per_block;  // chunks of one shard
   std::int64_t const chunk_vecs = static_cast<std::int64_t>(p.chunk_rows) * p.k / 8;
   std::uint32_t seen = 0;  // bit src: src's ready flag acquired by this warp
   for (;;) {
@@ -491,12 +491,11 @@ __device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, std::uint3
     if (ticket >= static_cast<std::uint32_t>(p.n_comm)) {
       break;
     }
-    std::int32_t const slot = static_cast<std::int32_t>(ticket) / per_shard;
-    std::int32_t const within = static_cast<std::int32_t>(ticket) % per_shard;
-    std::int32_t const rb = within / per_block;
-    std::int32_t const j = within % per_block;
-    std::int32_t const hops = (slot + 1) % p.n_pes;
-    std::int32_t const src = (p.my_pe + hops) % p.n_pes;
+    gather_chunk const ch = locate_gather_chunk(static_cast<std::int32_t>(ticket), p.n_pes,
+                                                p.my_pe, gw.mq, per_block, p.chunk_rows);
+    std::int32_t const rb = ch.rb;
+    std::int32_t const hops = ch.hops;
+    std::int32_t const src = ch.src;
     bool const remote = src != p.my_pe;
     if (remote && ((seen >> src) & 1u) == 0) {
       bool ok = true;
@@ -512,8 +511,7 @@ __device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, std::uint3
     }
     __syncwarp();  // every lane's loads after lane 0's acquire
     std::uint64_t const t0 = ptx::now_ns();
-    std::int64_t const row0 = static_cast<std::int64_t>(rb) * kBlockM +
-                              static_cast<std::int64_t>(j) * p.chunk_rows;
+    std::int64_t const row0 = ch.row0;
     __nv_bfloat16 const *shard = remote ? p.peers.translate(p.a_shard, src) : p.a_shard;
     auto const *from = reinterpret_cast<uint4 const *>(shard + row0 * p.k);
     auto *to = reinterpret_cast<uint4 *>(

@@ -125,6 +125,40 @@ MEGACU_B200_HD std::int32_t pair_raster(tile_schedule const &s, std::int32_t q,
   return 2 * q + rank;
 }
 
+// All-gather copy chunk: whole rows of A, about 64 KiB (a power of two of
+// rows, so that a 128-row tile row is a whole number of chunks).
+MEGACU_B200_HD std::int32_t gather_chunk_rows(std::int64_t k) {
+  std::int32_t rows = 128;
+  while (rows > 1 && static_cast<std::int64_t>(rows) * k * 2 > 65536) rows /= 2;
+  return rows;
+}
+
+// All-gather copy ticket t of PE my_pe -> the chunk it copies. Tickets walk
+// shard slots (slot s = the shard of the PE s + 1 hops away; the last slot
+// this PE's own shard), then tile rows of the shard, then chunks of
+// chunk_rows rows within the tile row (chunks_per_block of them).
+struct gather_chunk {
+  std::int32_t hops = 0;  // PEs away from my_pe (0: this PE's own shard)
+  std::int32_t src = 0;   // PE whose shard the chunk belongs to
+  std::int32_t rb = 0;    // tile row within the shard
+  std::int32_t row0 = 0;  // first row of the chunk within the shard
+};
+
+MEGACU_B200_HD gather_chunk locate_gather_chunk(std::int32_t ticket, std::int32_t n_pes,
+                                                std::int32_t my_pe, std::int32_t mq,
+                                                std::int32_t chunks_per_block,
+                                                std::int32_t chunk_rows) {
+  std::int32_t const per_shard = mq * chunks_per_block;
+  std::int32_t const slot = ticket / per_shard;
+  std::int32_t const within = ticket - slot * per_shard;
+  gather_chunk g;
+  g.rb = within / chunks_per_block;
+  g.hops = (slot + 1) % n_pes;
+  g.src = (my_pe + g.hops) % n_pes;
+  g.row0 = g.rb * 128 + (within - g.rb * chunks_per_block) * chunk_rows;
+  return g;
+}
+
 // Number of tiles PE q reduces under the two-shot / reduce-scatter split.
 MEGACU_B200_HD std::int32_t owned_tiles(tile_schedule const &s, std::int32_t q) {
   std::int32_t const t = s.tiles();
