@@ -408,6 +408,67 @@ int oracle_allgather_gemm(const oracle_bf16_problem *p, const float *const *a_sh
   return 0;
 }
 
+/* ---- single-launch MLP chain: event words and counters (a B200 addition;
+ *      restates chain_kernel.cuh's layout and publish rules) ------------- */
+
+static int32_t chain_quarters(int32_t row, int64_t tokens) {
+  int64_t const left = tokens - (int64_t)row * 128;
+  int64_t const q = (left + 31) / 32;
+  return (int32_t)(q < 4 ? q : 4);
+}
+
+int64_t oracle_chain_events_words(int32_t layers, int32_t n_pes, int64_t tokens,
+                                  int64_t hidden) {
+  int64_t const mt = (tokens + 127) / 128, dn = (hidden + 255) / 256;
+  return (int64_t)layers * n_pes * mt * dn * 4 + 2 * (int64_t)layers * mt;
+}
+
+void oracle_chain_events(int32_t layers, int32_t n_pes, int64_t tokens, int64_t hidden,
+                         int64_t inter, int32_t group_m, uint32_t epoch,
+                         uint32_t *const *events, uint64_t *counters) {
+  int32_t const mt = (int32_t)((tokens + 127) / 128);
+  int32_t const gn = (int32_t)((inter + 127) / 128);  /* act columns per GU tile: 128 */
+  int32_t const dn = (int32_t)((hidden + 255) / 256); /* hidden columns per DN tile: 256 */
+  int32_t const tiles = mt * dn;
+  int64_t const counters_base = (int64_t)layers * n_pes * tiles * 4;
+  int64_t quarters = 0;
+  for (int32_t row = 0; row < mt; ++row) quarters += chain_quarters(row, tokens);
+  memset(counters, 0, sizeof(uint64_t) * 8 * (size_t)n_pes);
+  for (int32_t pe = 0; pe < n_pes; ++pe) {
+    uint64_t *c = counters + 8 * pe;
+    c[0] = (uint64_t)layers * mt * (gn + dn);                 /* GEMM tiles */
+    c[2] = (uint64_t)layers * (uint64_t)quarters * (gn + dn); /* quarter publishes */
+    c[6] = 1;
+    for (int32_t l = 0; l < layers; ++l) {
+      for (int32_t row = 0; row < mt; ++row) {
+        int32_t const aq = chain_quarters(row, tokens);
+        /* act_ready: every GU quarter of the row; x_ready: every (DN tile,
+         * quarter) of the row, counted by its owner (or the epilogue on one
+         * PE). The host zeroes both before the launch. */
+        events[pe][counters_base + (int64_t)l * mt + row] = (uint32_t)(aq * gn);
+        events[pe][counters_base + (int64_t)(layers + l) * mt + row] = (uint32_t)(aq * dn);
+      }
+    }
+    if (n_pes == 1) continue;
+    c[5] = (uint64_t)n_pes; /* the final wait, once per call */
+    for (int32_t r = 0; r < tiles; ++r) {
+      int32_t loc[4];
+      oracle_locate(mt, dn, n_pes, 0, group_m, r, loc);
+      if (loc[2] != pe) continue;
+      int32_t const t = loc[0] * dn + loc[1];
+      int32_t const aq = chain_quarters(loc[0], tokens);
+      c[1] += (uint64_t)layers * aq;          /* exchange sub-tasks */
+      c[3] += (uint64_t)layers * aq * n_pes;  /* partial acquires */
+      c[4] += (uint64_t)layers * aq * n_pes;  /* final stores counted per PE */
+      /* every PE's partial of every active quarter of an owned tile */
+      for (int32_t l = 0; l < layers; ++l)
+        for (int32_t src = 0; src < n_pes; ++src)
+          for (int32_t q = 0; q < aq; ++q)
+            events[pe][(((int64_t)l * n_pes + src) * tiles + t) * 4 + q] = epoch;
+    }
+  }
+}
+
 /* ---- CPU-baseline sample: a list of output tiles -------------------------- */
 
 typedef struct tile_job {

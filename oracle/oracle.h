@@ -77,6 +77,20 @@ void oracle_mlp_chain(int64_t t, int64_t h, int64_t i, int32_t layers, int32_t n
                       const float *const *wu, const float *const *wd, float *out,
                       int32_t threads);
 
+/*
+ * Event words and completion counters of one single-launch MLP chain call
+ * (a B200 addition; restates chain_kernel.cuh): events[pe] holds the words
+ * after the control block, oracle_chain_events_words() of them; arrive flags
+ * [layer][src][DN tile][quarter] of the tiles PE pe owns are set to `epoch`
+ * (other words are left as they are), the act_ready / x_ready counters hold
+ * their values after the call. counters[pe * 8 + i] receive the per-call
+ * deltas of the device counters. group_m is the DN raster's band height.
+ */
+int64_t oracle_chain_events_words(int32_t layers, int32_t n_pes, int64_t tokens, int64_t hidden);
+void oracle_chain_events(int32_t layers, int32_t n_pes, int64_t tokens, int64_t hidden,
+                         int64_t inter, int32_t group_m, uint32_t epoch,
+                         uint32_t *const *events, uint64_t *counters);
+
 /* CTA-pair schedule restatement (a B200 addition with no counterpart in
  * megacu): GEMM pair ticket q -> out[0], out[1] = raster indices of the
  * upper and lower 128-row tiles the two CTAs of a cluster compute. */

@@ -70,6 +70,14 @@ def load():
         lib.oracle_gather_chunk_rows.restype = ctypes.c_int32
         lib.oracle_gather_events_words.argtypes = [ctypes.c_int32] * 3
         lib.oracle_gather_events_words.restype = ctypes.c_int64
+        lib.oracle_chain_events_words.argtypes = [ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_int64, ctypes.c_int64]
+        lib.oracle_chain_events_words.restype = ctypes.c_int64
+        lib.oracle_chain_events.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                            ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                            ctypes.c_uint32,
+                                            ctypes.POINTER(ctypes.POINTER(ctypes.c_uint32)),
+                                            ctypes.POINTER(ctypes.c_uint64)]
         _lib = lib
     return _lib
 
@@ -243,3 +251,18 @@ def allgather_gemm(a_shards, b_list, *, m, n, k, tile_n, group_m=16, epoch=1, ev
                                       counters.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), op)
     assert rc == 0, rc
     return dict(gathered=gathered, out=outs, events=events, counters=counters, gemm_order=orders)
+
+
+def chain_events(layers, n_pes, tokens, hidden, inter, *, epoch=1, events=None, group_m=16):
+    """The single-launch chain's event words (per PE, after the control block)
+    and per-call counter deltas. `events` (optional) is updated in place."""
+    words = load().oracle_chain_events_words(layers, n_pes, tokens, hidden)
+    if events is None:
+        events = [np.zeros(words, np.uint32) for _ in range(n_pes)]
+    events = [np.ascontiguousarray(e, np.uint32) for e in events]
+    evp = (ctypes.POINTER(ctypes.c_uint32) * n_pes)(
+        *[e.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)) for e in events])
+    counters = np.zeros((n_pes, 8), np.uint64)
+    load().oracle_chain_events(layers, n_pes, tokens, hidden, inter, group_m, epoch, evp,
+                               counters.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)))
+    return dict(events=events, counters=counters, words=words)

@@ -146,3 +146,55 @@ def test_mlp_chain_two_gpus_matches_oracle(single):
     assert torch.equal(calls[0][2].cpu(), calls[1][2].cpu())  # every PE holds the same bits
     for team, *_rest in calls:
         team.close()
+
+
+def _check_chain_events(prob, events_list, n_pes):
+    """Two single-launch calls were made: every PE's event words (the chain's
+    region after the control block) and counters match the oracle's graph."""
+    ref1 = oracle_lib.chain_events(prob.layers, n_pes, prob.tokens, prob.hidden, prob.inter,
+                                   epoch=1)
+    ref2 = oracle_lib.chain_events(prob.layers, n_pes, prob.tokens, prob.hidden, prob.inter,
+                                   epoch=2, events=ref1["events"])
+    words = ref2["words"]
+    for pe, ev in enumerate(events_list):
+        got = ev[64:64 + words].cpu().numpy().view(np.uint32)
+        assert np.array_equal(got, ref2["events"][pe]), f"PE {pe}: event words"
+        want = (ref1["counters"][pe] + ref2["counters"][pe]).tolist()
+        assert mb.events_counters(ev) == want, f"PE {pe}: counters"
+
+
+@_UNVERIFIED
+@pytest.mark.parametrize("n_pes", [1, 2])
+def test_single_launch_chain_events_match_oracle(n_pes):
+    if gpu_count() < n_pes:
+        pytest.skip("needs two GPUs")
+    t, h, i, layers = 200, 512, 384, 2
+    x = seeded_bf16(95, (t, h), 1.0)
+    wg, wu, wd = _weights(96, layers, n_pes, h, i)
+    prob = mb.MlpChainProblem(t, h, i, layers=layers, single_launch=True,
+                              timeout_ns=5_000_000_000)
+    teams = same_process_team(list(range(n_pes))) if n_pes > 1 else [None]
+    calls = []
+    try:
+        for pe, team in enumerate(teams):
+            with torch.cuda.device(pe):
+                bufs, out = _chain_buffers(prob, n_pes, team, pe)
+                ws = lambda w: [layer[pe].to(f"cuda:{pe}") for layer in w]
+                calls.append((team, bufs, out, x.to(f"cuda:{pe}"), ws(wg), ws(wu), ws(wd),
+                              torch.cuda.Stream(device=pe)))
+        for _ in range(2):
+            for pe, (team, bufs, out, xd, g, u, d, stream) in enumerate(calls):
+                with torch.cuda.device(pe):
+                    mb.mlp_chain(xd, g, u, d, out, problem=prob, stream=stream, device=pe,
+                                 team=team, **bufs)
+        for team, bufs, *_rest, stream in calls:
+            mb.events_status(bufs["events_down"], stream)
+        _check_chain_events(prob, [c[1]["events_down"] for c in calls], n_pes)
+        for team, bufs, out, *_rest in calls:
+            _check_chain(x, wg, wu, wd, out, bufs["x_work"])
+    finally:
+        for pe in range(n_pes):
+            torch.cuda.synchronize(pe)
+        for team, *_rest in calls:
+            if team is not None:
+                team.close()

@@ -248,3 +248,26 @@ def test_mlp_chain_matches_float64_restatement():
         scale = np.abs(cur).max()
         assert np.max(np.abs(got - cur)) < 1e-2 * scale, wire
         assert np.all(np.isfinite(got))
+
+
+@pytest.mark.parametrize("layers,n_pes,tokens,hidden,inter", [
+    (1, 1, 128, 256, 128), (2, 2, 200, 512, 384), (3, 8, 1000, 1024, 640)])
+def test_chain_event_oracle_is_consistent(layers, n_pes, tokens, hidden, inter):
+    """The single-launch chain's event words: every owner holds every PE's
+    flag for each active quarter of its tiles; counters add up across PEs."""
+    r = oracle_lib.chain_events(layers, n_pes, tokens, hidden, inter, epoch=5)
+    mt, dn, gn = -(-tokens // 128), -(-hidden // 256), -(-inter // 128)
+    aq = [min(4, -(-(tokens - 128 * row) // 32)) for row in range(mt)]
+    quarters = sum(aq)
+    base = layers * n_pes * mt * dn * 4
+    flags = sum(int((e[:base] == 5).sum()) for e in r["events"])
+    assert flags == (layers * n_pes * dn * quarters if n_pes > 1 else 0)
+    c = r["counters"]
+    for pe in range(n_pes):
+        e = r["events"][pe]
+        assert e[base:base + layers * mt].tolist() == [q * gn for q in aq] * layers
+        assert e[base + layers * mt:].tolist() == [q * dn for q in aq] * layers
+        assert c[pe, 0] == layers * mt * (gn + dn) and c[pe, 2] == layers * quarters * (gn + dn)
+    if n_pes > 1:
+        assert int(c[:, 1].sum()) == layers * dn * quarters    # every (tile, quarter) reduced once
+        assert (c[:, 3] == c[:, 1] * n_pes).all() and (c[:, 5] == n_pes).all()
