@@ -65,8 +65,9 @@ typedef struct megacu_status {
  *   36 multicast region set-up out of order, 37 multicast driver call,
  *   38 multicast object export / hand-over
  *   39 local rendezvous failed or timed out (megacu_b200_exchange_local)
- *   40 a cross-GPU wait timed out, 41 a local pipeline wait timed out
- *      (megacu_b200_events_status)
+ *   40 a cross-GPU wait timed out, 41 a local pipeline wait timed out,
+ *   42 a kernel bounds check failed (only in the bounds-checked build,
+ *      libmegacu_b200_checked.so) (megacu_b200_events_status)
  *   50 built-in scratch address lookup, 51 more than one PE,
  *   52 tile grid larger than the built-in scratch (megacu_cuda_gemm_bf16_noalloc)
  */

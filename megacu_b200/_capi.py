@@ -10,7 +10,7 @@ import ctypes
 import os
 import re
 
-from .build import LIB_PATH, ROOT
+from .build import CHECKED_LIB_PATH, LIB_PATH, ROOT
 
 c_int32, c_int64, c_uint8, c_uint16, c_uint64 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint8,
                                                  ctypes.c_uint16, ctypes.c_uint64)
@@ -144,11 +144,18 @@ _PROTOTYPES = {
 _lib = None
 
 
-def load(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Loads libmegacu_b200.so (once). Raises if it has not been built."""
+def library_path() -> str:
+    """libmegacu_b200.so, or its bounds-checked build when
+    MEGACU_B200_LIBRARY=checked."""
+    return CHECKED_LIB_PATH if os.environ.get("MEGACU_B200_LIBRARY") == "checked" else LIB_PATH
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Loads the native library (once). Raises if it has not been built."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or library_path()
     if not os.path.exists(path):
         raise ImportError(
             f"megacu_b200 native library missing at {path}: run "

@@ -25,6 +25,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "megacu_b200")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libmegacu_b200.so")
+# The same library with the kernels' bounds checks compiled in
+# (-DMEGACU_B200_DEBUG_BOUNDS): loaded instead of the regular one when
+# MEGACU_B200_LIBRARY=checked, for first runs of new kernel code.
+CHECKED_LIB_PATH = os.path.join(LIB_DIR, "libmegacu_b200_checked.so")
 HARNESS_PATH = os.path.join(ROOT, "tests", "_build", "libhost_harness.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -68,16 +72,19 @@ def _run(cmd: list[str], verbose: bool) -> None:
         raise RuntimeError(f"build failed: {' '.join(cmd)}\n{proc.stdout}\n{proc.stderr}")
 
 
-def build_library(verbose: bool = False, force: bool = False) -> str:
-    """Builds libmegacu_b200.so for sm_100a (skipped when up to date)."""
+def build_library(verbose: bool = False, force: bool = False, checked: bool = False) -> str:
+    """Builds libmegacu_b200.so (or, with `checked`, the bounds-checked
+    libmegacu_b200_checked.so) for sm_100a, skipped when up to date."""
     os.makedirs(LIB_DIR, exist_ok=True)
-    if force or _stale(LIB_PATH, _deps()):
-        tmp = LIB_PATH + ".tmp"
-        cmd = [_nvcc(), *NVCC_FLAGS, "-shared", "-I" + os.path.join(ROOT, "include"),
+    path = CHECKED_LIB_PATH if checked else LIB_PATH
+    if force or _stale(path, _deps()):
+        tmp = path + ".tmp"
+        cmd = [_nvcc(), *NVCC_FLAGS, *(["-DMEGACU_B200_DEBUG_BOUNDS"] if checked else []),
+               "-shared", "-I" + os.path.join(ROOT, "include"),
                "-I" + os.path.join(PKG, "csrc"), *_sources(), "-o", tmp]
         _run(cmd, verbose)
-        os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+        os.replace(tmp, path)
+    return path
 
 
 def build_harness(verbose: bool = False, force: bool = False) -> str:
@@ -116,6 +123,7 @@ def build_oracle(verbose: bool = False) -> None:
 
 def build_all(verbose: bool = False, force: bool = False) -> None:
     build_library(verbose, force)
+    build_library(verbose, force, checked=True)
     build_harness(verbose, force)
     build_oracle(verbose)
 

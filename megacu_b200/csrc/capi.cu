@@ -1019,8 +1019,9 @@ extern "C" megacu_status megacu_b200_events_status(void *events, void *stream, s
                  cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return cuda_fail(e, 11);
   return fail(MEGACU_BACKEND_ERROR, static_cast<std::uint16_t>(cb.error_code),
-              cb.error_code == err_remote_timeout ? "a cross-GPU wait timed out"
-                                                  : "an on-chip pipeline wait timed out");
+              cb.error_code == err_remote_timeout  ? "a cross-GPU wait timed out"
+              : cb.error_code == err_local_timeout ? "an on-chip pipeline wait timed out"
+                                                   : "a bounds check failed (checked build)");
 }
 
 extern "C" megacu_status megacu_b200_events_counters(void *events, void *stream,

@@ -235,6 +235,21 @@ __device__ __forceinline__ void exchange(chain_params const &p, tile_schedule co
     std::int32_t const tile = c.tile_row * p.dn_tiles_n + c.tile_col;
     std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
     if (row0 >= p.tokens) continue;  // a quarter without tokens: nothing to reduce or count
+    if constexpr (kCheckBounds) {
+      std::int64_t const dn_tiles = static_cast<std::int64_t>(p.m_tiles) * p.dn_tiles_n;
+      std::int64_t const words =
+          (chain_events_bytes(p.layers, p.n_pes, p.dn_tiles_n, p.m_tiles) - kControlBytes) / 4;
+      bool const in =
+          layer < p.layers && tile >= 0 && tile < dn_tiles && c.owner == p.my_pe &&
+          chain_arrive_index(layer, p.n_pes - 1, tile, 3, p.n_pes, p.dn_tiles_n, p.m_tiles) <
+              chain_counters_base(p.layers, p.n_pes, p.dn_tiles_n, p.m_tiles) &&
+          chain_x_ready_index(layer, c.tile_row, p.layers, p.n_pes, p.dn_tiles_n, p.m_tiles) <
+              words;
+      if (!in) {
+        if (lane == 0) record_error(p, err_bounds, ticket, static_cast<std::uint32_t>(tile), 32);
+        continue;  // nothing reduced or counted: the waiting PEs time out
+      }
+    }
 
     bool ok = true;
     if (static_cast<std::int32_t>(lane) < p.n_pes) {
@@ -462,6 +477,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           dep = my_events + chain_act_ready_index(j.layer, c.tile_row, p.layers, p.n_pes,
                                                   p.dn_tiles_n, p.m_tiles);
           target = static_cast<std::uint32_t>(aq * p.gu_tiles_n);
+        }
+        if constexpr (kCheckBounds) {
+          if (j.layer >= p.layers || c.tile_row < 0 || c.tile_row >= p.m_tiles) {
+            chain_detail::record_error(p, err_bounds, static_cast<std::uint32_t>(t), cta_rank, 35);
+            break;
+          }
         }
         if (dep != nullptr) {
           if (!chain_detail::wait_count(dep, target, abort_word, p.timeout_ns)) {
@@ -734,6 +755,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // fence covers it (its readers acquire the counter or flag).
       ptx::fence_acq_rel_gpu();
       __syncwarp();
+      if constexpr (kCheckBounds) {
+        bool const in = j.layer < p.layers && c.tile_row < p.m_tiles &&
+                        (j.kind == 0 || (dn_tile < p.m_tiles * p.dn_tiles_n && c.owner >= 0 &&
+                                         c.owner < p.n_pes));
+        if (!in) {
+          if (lane == 0) {
+            chain_detail::record_error(p, err_bounds, static_cast<std::uint32_t>(t),
+                                       static_cast<std::uint32_t>(dn_tile), 34);
+          }
+          continue;  // not published: its consumers time out
+        }
+      }
       if (lane == 0) {
         if (j.kind == 0) {
           atomicAdd(my_events + chain_act_ready_index(j.layer, c.tile_row, p.layers, p.n_pes,

@@ -497,6 +497,17 @@ __device__ __forceinline__ void gather_tasks(gemm_ar_params const &p, std::uint3
     std::int32_t const hops = ch.hops;
     std::int32_t const src = ch.src;
     bool const remote = src != p.my_pe;
+    if constexpr (kCheckBounds) {
+      bool const in = src >= 0 && src < p.n_pes && rb >= 0 && rb < gw.mq && ch.row0 >= 0 &&
+                      ch.row0 + p.chunk_rows <= p.rows_per_pe &&
+                      static_cast<std::int64_t>(src) * p.rows_per_pe + ch.row0 + p.chunk_rows <=
+                          p.m &&
+                      gw.chunks(src) < gw.end();
+      if (!in) {
+        if (lane == 0) record_error(p, err_bounds, ticket, static_cast<std::uint32_t>(src), 30);
+        continue;  // nothing copied or counted: the tiles waiting on it time out
+      }
+    }
     if (remote && ((seen >> src) & 1u) == 0) {
       bool ok = true;
       if (lane == 0) {
@@ -770,6 +781,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             a_row -= p.my_pe * p.rows_per_pe;
           } else {
             amap = &map_b2;
+          }
+          if constexpr (kCheckBounds) {
+            bool const own = c.owner == p.my_pe;
+            std::int64_t const rows = own ? p.rows_per_pe : p.m;
+            std::int32_t const rb = c.tile_row - c.owner * gw.mq;
+            if (a_row < 0 || a_row + kBlockM > rows || c.owner < 0 || c.owner >= p.n_pes ||
+                rb < 0 || rb >= gw.mq) {
+              detail::record_error(p, err_bounds, static_cast<std::uint32_t>(r),
+                                   static_cast<std::uint32_t>(c.owner), 31);
+              break;
+            }
+          }
+          if (c.owner != p.my_pe) {
             std::uint32_t const *rows_copied =
                 my_events + gw.rows(c.owner, c.tile_row - c.owner * gw.mq);
             if (!detail::wait_at_least(rows_copied, static_cast<std::uint32_t>(p.chunks_per_block),

@@ -72,7 +72,20 @@ enum : std::uint32_t {
   err_none = 0,
   err_remote_timeout = 40,  // a cross-GPU flag never arrived
   err_local_timeout = 41,   // an on-chip pipeline wait timed out
+  err_bounds = 42,          // a bounds check of the checked build failed
 };
+
+// The bounds-checked build (-DMEGACU_B200_DEBUG_BOUNDS, libmegacu_b200_checked.so):
+// the kernels check the index of each access whose arithmetic is theirs (copy
+// chunks, exchange slots and rows, event words, TMA row coordinates) against
+// the extent of its buffer; a failed check records err_bounds with the site
+// and skips the access instead of making it. The regular build compiles the
+// checks away.
+#if defined(MEGACU_B200_DEBUG_BOUNDS)
+inline constexpr bool kCheckBounds = true;
+#else
+inline constexpr bool kCheckBounds = false;
+#endif
 
 enum : std::int32_t {
   ctr_gemm_tasks = 0,

@@ -21,6 +21,17 @@ def test_library_exports_every_declared_symbol():
     assert lib.megacu_b200_version().startswith(b"megacu_b200")
 
 
+def test_checked_build_exports_the_same_symbols():
+    """The bounds-checked library (MEGACU_B200_LIBRARY=checked) is the same
+    C ABI."""
+    from megacu_b200 import build
+    if not os.path.exists(build.CHECKED_LIB_PATH):
+        pytest.skip("checked library not built")
+    lib = ctypes.CDLL(build.CHECKED_LIB_PATH)
+    for name in _capi.declared_functions():
+        assert hasattr(lib, name), name
+
+
 def test_component_link_anchors():
     """tests/build/runtime_components_contracts.cc:60-64."""
     lib = _capi.load()
