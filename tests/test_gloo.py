@@ -3,8 +3,8 @@
 * The team handle exchange (`megacu_b200.torch_exchange`) delivers every
   PE's handle in PE order.
 * The product's tile plan (`plan_tile`, the device queue's schedule) drives a
-  CPU emulation of the two-shot allreduce and the reduce-scatter across real
-  processes: each rank sends its partial tiles to their owners, owners reduce
+  CPU emulation of the two-shot allreduce, the reduce-scatter and the
+  all-gather + GEMM (each rank's own raster) across real processes: each rank sends its partial tiles to their owners, owners reduce
   in PE order, two-shot owners send the sums back to everyone. The result
   must equal the oracle's n-PE graph bit for bit, and the owners must
   partition the tiles with dense local indices.
@@ -80,6 +80,51 @@ def _emulate(rank, world, m, n, k, mode):
     assert out.tobytes() == ref["out"][rank].tobytes()
 
 
+def _emulate_allgather(rank, world, m, n, k):
+    """The all-gather + GEMM across real processes, driven by the product's
+    per-PE plan: each rank fetches the shards in its copy order (the shared
+    chunk decode), computes its tiles in its own raster order from the rows
+    it has, and must match the oracle bit for bit (gathered A and output)."""
+    import sys
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import megacu_b200 as mb
+    import oracle_lib
+
+    prob = mb.Problem(m, n, k, mode=mb.MODE_ALLGATHER)
+    pl = mb.plan(prob, world)
+    rows = m // world
+    rng = np.random.default_rng(77)
+    shards = [oracle_lib.round_bf16(rng.normal(0, 1, (rows, k)).astype(np.float32))
+              for _ in range(world)]
+    b = [oracle_lib.round_bf16(rng.normal(0, 0.1, (k, n)).astype(np.float32))
+         for _ in range(world)]
+    everyone = [None] * world
+    dist.all_gather_object(everyone, shards[rank])          # what the peers expose
+    gathered = np.full((m, k), np.nan, np.float32)
+    gathered[rank * rows:(rank + 1) * rows] = everyone[rank]  # own shard: read in place
+    have = {rank}
+    out = np.full((m, n), np.nan, np.float32)
+    tn = pl.tile_n
+    last_hops = 0
+    for r in range(pl.tiles):
+        row, col, shard, _ = mb.plan_tile(prob, world, r, rank)
+        hops = (shard - rank) % world
+        assert hops >= last_hops     # whole shards, own first, then 1, 2, ... PEs away
+        last_hops = hops
+        if shard not in have:                                 # the copy of the next shard
+            gathered[shard * rows:(shard + 1) * rows] = everyone[shard]
+            have.add(shard)
+        a = gathered[row * 128:(row + 1) * 128]
+        assert not np.isnan(a).any()
+        w = min(tn, n - col * tn)
+        out[row * 128:(row + 1) * 128, col * tn:col * tn + w] = oracle_lib.gemm_f32(
+            a, b[rank][:, col * tn:col * tn + w], threads=2)
+    ref = oracle_lib.allgather_gemm(shards, b, m=m, n=n, k=k, tile_n=tn, threads=2)
+    assert gathered.tobytes() == ref["gathered"][rank].tobytes()
+    assert out.tobytes() == ref["out"][rank].tobytes()
+
+
 def _worker(rank, world, port, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -94,6 +139,7 @@ def _worker(rank, world, port, result_dir):
         assert [g[0] for g in got] == list(range(world)) and all(len(g) == 128 for g in got)
         _emulate(rank, world, 300, 520, 64, mb.MODE_ALLREDUCE)
         _emulate(rank, world, 512, 256, 48, mb.MODE_REDUCE_SCATTER)
+        _emulate_allgather(rank, world, 512, 200, 72)
     except Exception as exc:  # reported through the result file
         status = f"fail: {exc!r}"
     finally:
