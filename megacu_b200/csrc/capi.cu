@@ -104,6 +104,23 @@ int sm_count(int device) {
   return n;
 }
 
+}  // namespace
+
+namespace megacu_b200 {
+
+cudaError_t launch_bf16_plan(bool wire_f32, int tile_n, bool pairs, int device, int grid,
+                             cudaStream_t stream, CUtensorMap const &ma, CUtensorMap const &mb,
+                             gemm_ar_params const &prm) {
+  return wire_f32 ? launch_gemm_ar<true>(tile_n, pairs, device, grid, stream, ma, mb, prm)
+                  : launch_gemm_ar<false>(tile_n, pairs, device, grid, stream, ma, mb, prm);
+}
+
+}  // namespace megacu_b200
+
+namespace {
+
+using namespace megacu_b200;
+
 // ---- plan of one bf16 call ---------------------------------------------------
 
 struct bf16_plan {
@@ -239,6 +256,27 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
 
 bool aligned16(void const *p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
+// All-gather + GEMM: `ma` is this PE's A shard, `mg` the gathered A (both
+// with 128-row boxes), `mb` the B operand.
+cudaError_t launch_allgather(int tile_n, bool pairs, int device, int grid, cudaStream_t stream,
+                             CUtensorMap const &ma, CUtensorMap const &mb, CUtensorMap const &mg,
+                             gemm_ar_params const &prm) {
+  switch (tile_n) {
+    case 256:
+      return pairs ? launch_variant<256, false, true, false, true>(device, grid, stream, ma, mb,
+                                                                   mg, prm)
+                   : launch_variant<256, false, false, false, true>(device, grid, stream, ma, mb,
+                                                                    mg, prm);
+    case 128:
+      return pairs ? launch_variant<128, false, true, false, true>(device, grid, stream, ma, mb,
+                                                                   mg, prm)
+                   : launch_variant<128, false, false, false, true>(device, grid, stream, ma, mb,
+                                                                    mg, prm);
+    default:
+      return launch_variant<64, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
+  }
+}
+
 megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, void *workspace,
                        void *out, void *events, megacu_gemm_ar_problem_v2 problem) {
   std::int32_t const n_pes = driver.team.team_n_pes;
@@ -356,8 +394,7 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   int grid = problem.num_ctas > 0 ? problem.num_ctas : sm_count(device);
   auto stream = static_cast<cudaStream_t>(driver.launch.stream);
   bool const f32 = pl.wire_bytes == 4;
-  e = f32 ? launch_gemm_ar<true>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm)
-          : launch_gemm_ar<false>(pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm);
+  e = launch_bf16_plan(f32, pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm);
   if (e != cudaSuccess) return cuda_fail(e, 14);
   return ok_status();
 }

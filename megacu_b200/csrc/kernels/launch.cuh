@@ -84,31 +84,10 @@ cudaError_t launch_gemm_ar(int tile_n, bool pairs, int device, int grid, cudaStr
   }
 }
 
-// The gate/up projection with the SiLU * up epilogue (one PE): `mg` and `mu`
-// are the gate and up weights [k, n] with 64 x 64 boxes.
-inline cudaError_t launch_swiglu(bool pairs, int device, int grid, cudaStream_t stream,
-                                 CUtensorMap const &ma, CUtensorMap const &mg,
-                                 CUtensorMap const &mu, gemm_ar_params const &prm) {
-  return pairs ? launch_variant<256, false, true, true>(device, grid, stream, ma, mg, mu, prm)
-               : launch_variant<256, false, false, true>(device, grid, stream, ma, mg, mu, prm);
-}
-
-// All-gather + GEMM: `ma` is this PE's A shard, `mg` the gathered A (both
-// with 128-row boxes), `mb` the B operand.
-inline cudaError_t launch_allgather(int tile_n, bool pairs, int device, int grid,
-                                    cudaStream_t stream, CUtensorMap const &ma,
-                                    CUtensorMap const &mb, CUtensorMap const &mg,
-                                    gemm_ar_params const &prm) {
-  switch (tile_n) {
-    case 256:
-      return pairs ? launch_variant<256, false, true, false, true>(device, grid, stream, ma, mb, mg, prm)
-                   : launch_variant<256, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
-    case 128:
-      return pairs ? launch_variant<128, false, true, false, true>(device, grid, stream, ma, mb, mg, prm)
-                   : launch_variant<128, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
-    default:
-      return launch_variant<64, false, false, false, true>(device, grid, stream, ma, mb, mg, prm);
-  }
-}
+// Launches of the bf16 plans, defined once in capi.cu (so that the kernel
+// variants are compiled in one translation unit only).
+cudaError_t launch_bf16_plan(bool wire_f32, int tile_n, bool pairs, int device, int grid,
+                             cudaStream_t stream, CUtensorMap const &ma, CUtensorMap const &mb,
+                             gemm_ar_params const &prm);
 
 }  // namespace megacu_b200

@@ -25,6 +25,15 @@ namespace {
 
 using namespace megacu_b200;
 
+// The gate/up projection with the SiLU * up epilogue (one PE): `mg` and `mu`
+// are the gate and up weights [k, n] with 64 x 64 boxes.
+cudaError_t launch_swiglu(bool pairs, int device, int grid, cudaStream_t stream,
+                          CUtensorMap const &ma, CUtensorMap const &mg, CUtensorMap const &mu,
+                          gemm_ar_params const &prm) {
+  return pairs ? launch_variant<256, false, true, true>(device, grid, stream, ma, mg, mu, prm)
+               : launch_variant<256, false, false, true>(device, grid, stream, ma, mg, mu, prm);
+}
+
 constexpr std::int32_t kActTile = 128;  // act columns per tile (128 gate + 128 up)
 constexpr std::int32_t kMaxLayers = 64;
 

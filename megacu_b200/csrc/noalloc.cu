@@ -145,7 +145,7 @@ extern "C" megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return na_cuda(e, 10);
   int const grid = problem.num_ctas > 0 ? problem.num_ctas : sms;
-  e = launch_gemm_ar<false>(tile_n, info[8] != 0, device, grid, stream, map_a, map_b, prm);
+  e = launch_bf16_plan(false, tile_n, info[8] != 0, device, grid, stream, map_a, map_b, prm);
   if (e != cudaSuccess) return na_cuda(e, 14);
   return na_ok();
 }
