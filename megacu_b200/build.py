@@ -121,6 +121,35 @@ def build_oracle(verbose: bool = False) -> None:
     _run(cmd, verbose)
 
 
+def kernel_resources() -> list[dict]:
+    """ptxas' resource report of every kernel the library compiles (registers,
+    spills, static shared memory), from `nvcc -Xptxas -v` of each source."""
+    import re
+    rows = []
+    for src in sorted(glob.glob(os.path.join(PKG, "csrc", "*.cu"))):
+        cmd = [_nvcc(), *NVCC_FLAGS, "-Xptxas", "-v", "-I" + os.path.join(ROOT, "include"),
+               "-I" + os.path.join(PKG, "csrc"), "-c", src, "-o", os.devnull]
+        proc = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+        if proc.returncode != 0:
+            raise RuntimeError(proc.stderr)
+        name = None
+        for line in proc.stderr.splitlines():
+            m = re.search(r"Compiling entry function '([^']+)'", line)
+            if m:
+                name = m.group(1)
+                rows.append({"source": os.path.basename(src), "kernel": name})
+                continue
+            m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+            if m and name and rows and rows[-1]["kernel"] == name:
+                rows[-1]["spill_bytes"] = int(m.group(1)) + int(m.group(2))
+            m = re.search(r"Used (\d+) registers", line)
+            if m and name and rows and rows[-1]["kernel"] == name:
+                rows[-1]["registers"] = int(m.group(1))
+                sm = re.search(r"(\d+) bytes smem", line)
+                rows[-1]["static_smem_bytes"] = int(sm.group(1)) if sm else 0
+    return rows
+
+
 def build_all(verbose: bool = False, force: bool = False) -> None:
     build_library(verbose, force)
     build_library(verbose, force, checked=True)
@@ -129,4 +158,10 @@ def build_all(verbose: bool = False, force: bool = False) -> None:
 
 
 if __name__ == "__main__":
-    build_all(verbose=True, force="--force" in sys.argv)
+    if "--resources" in sys.argv:
+        for r in kernel_resources():
+            print(f"{r['source']:12s} {r.get('registers', '?'):>4} regs "
+                  f"{r.get('spill_bytes', 0):>4} B spill {r.get('static_smem_bytes', 0):>6} B smem "
+                  f"{r['kernel']}")
+    else:
+        build_all(verbose=True, force="--force" in sys.argv)
