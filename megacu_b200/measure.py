@@ -155,14 +155,18 @@ class NvlinkCounters:
             return None
 
 
-def interleaved(bodies, steps, warmup, align, stream, world):
+def interleaved(bodies, steps, warmup, align, stream, world, device=None):
     """Times each body ``steps`` times with CUDA events on ``stream``,
     interleaved step by step (body 0, body 1, ..., then the next step) so that
     every arm sees the same clocks and temperature. ``align()`` runs before
     every step outside the events (an L2 flush and a team barrier). Returns,
-    per body, the list of per-step milliseconds, each the max over ranks."""
+    per body, the list of per-step milliseconds, each the max over ranks
+    (reduced on ``device``, the current CUDA device by default)."""
     import torch
     import torch.distributed as dist
+
+    if device is None:
+        device = torch.device("cuda", torch.cuda.current_device())
 
     for _ in range(warmup):
         for body in bodies:
@@ -181,7 +185,7 @@ def interleaved(bodies, steps, warmup, align, stream, world):
             evs[i][1].record(stream)
     torch.cuda.synchronize()
     ms = torch.tensor([[s.elapsed_time(e) for s, e in evs] for evs in ev], dtype=torch.float64,
-                      device=torch.device("cuda", torch.cuda.current_device()))
+                      device=device)
     if world > 1:
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.barrier()

@@ -46,3 +46,48 @@ def test_allgather_roofline_counts_the_gathered_rows():
     assert r["link_bytes_per_pe"] == pytest.approx(7 / 8 * m * k * 2)
     assert r["hbm_bytes_per_pe"] == 2.0 * (m * k + k * n) + m * n * 2 + 2.0 * m * k
     assert r["bound"] == "tensor"
+
+
+def test_interleaved_orders_arms_and_takes_the_max_over_ranks(monkeypatch):
+    """The timing loop with fake CUDA events: warm-up untimed, arms
+    interleaved step by step with align() before each, one value per step and
+    arm, the max over ranks (two gloo ranks emulated by a fake all_reduce)."""
+    import torch
+    import torch.distributed as dist
+
+    log = []
+    clock = [0.0]
+
+    class FakeEvent:
+        def __init__(self, enable_timing=False):
+            self.t = None
+
+        def record(self, stream=None):
+            self.t = clock[0]
+
+        def elapsed_time(self, end):
+            return end.t - self.t
+
+    def body(i):
+        def run():
+            log.append(("body", i))
+            clock[0] += 1.0 + i   # arm i takes 1 + i ms
+        return run
+
+    monkeypatch.setattr(torch.cuda, "Event", FakeEvent)
+    monkeypatch.setattr(torch.cuda, "synchronize", lambda *a: None)
+    reduced = []
+
+    def fake_all_reduce(t, op=None):
+        reduced.append(op)
+        t.mul_(2.0)           # the other rank was twice as slow
+    monkeypatch.setattr(dist, "all_reduce", fake_all_reduce)
+    monkeypatch.setattr(dist, "barrier", lambda *a, **k: None)
+    ms = measure.interleaved([body(0), body(1)], steps=3, warmup=2,
+                             align=lambda: log.append(("align",)), stream=None, world=2,
+                             device="cpu")
+    assert ms == [[2.0] * 3, [4.0] * 3]
+    assert reduced == [dist.ReduceOp.MAX]
+    bodies = [x[1] for x in log if x[0] == "body"]
+    assert bodies == [0, 1] * 5                      # 2 warm-up + 3 timed rounds
+    assert sum(1 for x in log if x[0] == "align") == 10
