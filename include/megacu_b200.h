@@ -405,8 +405,23 @@ megacu_status megacu_b200_plan_pair(megacu_gemm_ar_problem_v2 problem,
  * Reads the device status word of `events` after the stream has finished
  * (synchronises the stream). code MEGACU_OK if the last calls completed;
  * MEGACU_BACKEND_ERROR with detail 40 if a cross-GPU wait timed out
- * (info[0] = tile, info[1] = peer PE, info[2] = which wait) and 41 if a local
- * pipeline wait timed out. The word is cleared by the call.
+ * (info[0] = tile, info[1] = peer PE, info[2] = which wait), 41 if a local
+ * pipeline wait timed out and 42 if a bounds check of the checked build
+ * failed; info[3] = the detail. The word is cleared by the call.
+ * Which wait (info[2]):
+ *   fused GEMM + exchange kernel: 1 producer's task ring, 2 producer's free
+ *     stage, 3 MMA's task ring, 4 MMA's free accumulator, 5 MMA's full stage,
+ *     6 epilogue's task ring, 7 epilogue's full accumulator, 8 a PE's partial
+ *     flag (exchange), 9 a PE's done flag (two-shot completion);
+ *   all-gather: 21 a peer's shard-ready flag, 22 a peer's shard-copied flag,
+ *     23 the GEMM producer's wait for copied rows;
+ *   single-launch MLP chain: 11 producer's task ring, 12 a dependency
+ *     counter (act_ready / x_ready), 13 producer's free stage, 14-16 MMA's
+ *     task ring / free accumulator / full stage, 17 epilogue's task ring,
+ *     19 epilogue's full accumulator, 18 a PE's partial flag, 20 the final
+ *     wait for the last block's rows;
+ *   checked build: 30 all-gather copy chunk, 31 all-gather A row, 32 chain
+ *     exchange indices, 34 chain publish indices, 35 chain dependency index.
  */
 megacu_status megacu_b200_events_status(void *events, void *stream,
                                         int64_t info[4]);
