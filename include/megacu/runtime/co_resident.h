@@ -10,12 +10,13 @@
 // (megacu/scheduler/co_resident_device.cuh) executes:
 //
 //  * every operator task is a node with `units` work units: the tiles of its
-//    dispatcher::tile_grid, or one without a grid; sync tasks have none;
+//    dispatcher::tile_grid, or without a grid one per slot of the event
+//    tensors it acquires, or one; sync tasks have none;
 //  * the device queue hands out the units node by node in the phase's ASAP
 //    order (lowest ready task index first), tile by tile within a node;
-//  * a node that acquires an event tensor published by another node waits
-//    per tile: its tile t starts once the publisher's tile t has published
-//    (on every PE for a team-scope tensor). A sync task joining that tensor,
+//  * a node that acquires event tensors published by other nodes waits per
+//    tile: its tile t starts once each publisher's tile t has published (on
+//    every PE for a team-scope tensor). A sync task joining such a tensor,
 //    and a direct dependency on its publisher, are covered by this per-tile
 //    wait: the phase's barrier becomes tile-level dataflow;
 //  * every other dependency waits for the whole node: its units start once
@@ -26,12 +27,13 @@
 //
 // Errors: progress other than co_resident_persistent -> unsupported/1; a
 // dependency cycle or dangling dependency -> invalid_argument/2 (as the ASAP
-// scheduler); more than `max_nodes` operator tasks -> unsupported/8; a task
-// publishing or acquiring more than one event tensor, or an event tensor
-// published by two tasks -> unsupported/9; an acquired event tensor that no
-// task publishes, or whose slots differ from the acquiring or publishing
-// task's tiles, or that is published or acquired without storage ->
-// invalid_argument/6; unit count overflow -> unsupported/10.
+// scheduler); more than `max_nodes` operator tasks -> unsupported/8; more
+// than `max_events` event tensors, or an event tensor published by two
+// tasks -> unsupported/9; an acquired event tensor that no task publishes,
+// is published later in the queue or by the acquiring task itself, a
+// published or acquired tensor whose slots differ from the task's tiles, or
+// one without storage -> invalid_argument/6; unit count overflow ->
+// unsupported/10.
 #pragma once
 
 #include <cstdint>
@@ -43,14 +45,13 @@ namespace megacu::runtime::co_resident {
 
 inline constexpr int max_nodes = 16;
 inline constexpr int max_events = 16;
-inline constexpr std::int32_t no_event = -1;
 
 // One operator task of the phase. Nodes are indexed by the task's position
 // among the phase's operator tasks (its slot in the device operator table).
 struct node {
   std::int32_t phase_task = -1;   // index of the task in the phase
-  std::int32_t publish = no_event;
-  std::int32_t acquire = no_event;
+  std::uint32_t publish = 0;      // bit e: tile t publishes slot t of event tensor e
+  std::uint32_t acquire = 0;      // bit e: tile t waits for slot t of event tensor e
   std::uint32_t wait_nodes = 0;   // bit j: every unit of node j completes first
   std::int64_t units = 0;
   std::int64_t first_unit = 0;    // queue index of the node's first unit

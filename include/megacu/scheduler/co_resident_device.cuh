@@ -8,11 +8,12 @@
 //    holds it (work_item.task = that node);
 //  * co_resident (scheduler): one task per unit, the unit's node;
 //  * co_resident_events (backend): before a unit, thread 0 waits until every
-//    node it depends on has completed all its units and, for a node that
-//    acquires an event tensor, until slot `tile` holds tile + 1 on every PE
+//    node it depends on has completed all its units and, for each event
+//    tensor the node acquires, until slot `tile` holds tile + 1 on every PE
 //    of the tensor's scope (megacu's ready value,
 //    backends/nvshmem/cuda_event_tensor.cuh:41-59); after it, it publishes
-//    the node's event tensor for the tile and counts the unit done. Every
+//    slot `tile` of each tensor the node publishes and counts the unit
+//    done. Every
 //    wait is bounded: one that gives up sets the state's error word and
 //    ends the CTA's loop.
 // The launcher copies the graph into `co_resident_state` and zeroes the
@@ -150,10 +151,12 @@ struct co_resident_events {
         __nanosleep(spin < 64 ? 64 : 256);
       }
     }
-    if (nd.acquire != co::no_event &&
-        !tensor(nd.acquire).acquire(work.tile_id, static_cast<int>(work.tile_id + 1))) {
-      give_up(task.value, work.tile_id);
-      return false;
+    for (int e = 0; e < g.event_count; ++e) {
+      if (((nd.acquire >> e) & 1u) != 0 &&
+          !tensor(e).acquire(work.tile_id, static_cast<int>(work.tile_id + 1))) {
+        give_up(task.value, work.tile_id);
+        return false;
+      }
     }
     return true;
   }
@@ -161,9 +164,12 @@ struct co_resident_events {
   template <class Context, class Task, class Work>
   __device__ bool after(Context ctx, Task task, Work work) const {
     if (ctx.thread_id() != 0) return true;
-    co::node const &nd = state->graph.nodes[task.value];
-    if (nd.publish != co::no_event) {
-      tensor(nd.publish).publish(work.tile_id, static_cast<int>(work.tile_id + 1));
+    co::graph const &g = state->graph;
+    co::node const &nd = g.nodes[task.value];
+    for (int e = 0; e < g.event_count; ++e) {
+      if (((nd.publish >> e) & 1u) != 0) {
+        tensor(e).publish(work.tile_id, static_cast<int>(work.tile_id + 1));
+      }
     }
     __threadfence();  // the CTA's writes of this unit (ordered by the block barrier) first
     atomicAdd(&state->done[task.value], 1u);

@@ -12,14 +12,15 @@ constexpr std::int64_t kMaxUnits = (std::int64_t(1) << 31) - 1;  // device ticke
 
 status fail(status_code code, std::uint16_t detail, char const *msg) { return {code, detail, msg}; }
 
-bool joins(linked_task const &t, std::int32_t ev) {
-  if (ev == no_event) return false;
+// Event tensors a task joins, as a bit mask.
+std::uint32_t join_mask(linked_task const &t) {
+  std::uint32_t mask = 0;
   for (attr const &a : t.attributes.entries()) {
-    if (a.kind == attr_kind::event_join && static_cast<std::int32_t>(a.event.value) == ev) {
-      return true;
+    if (a.kind == attr_kind::event_join && a.event.value < static_cast<std::uint32_t>(max_events)) {
+      mask |= 1u << a.event.value;
     }
   }
-  return false;
+  return mask;
 }
 
 // The phase's ASAP order (lowest-index ready task first), as the explicit
@@ -49,27 +50,29 @@ bool asap_order(std::span<linked_task const> tasks, std::vector<std::int32_t> &o
 struct lowering {
   std::span<linked_task const> tasks;
   std::vector<std::int32_t> node_of;  // phase task -> node, -1 for sync tasks
-  graph *g;
+  graph const *g;
 
-  // Adds to `wait` the nodes that `x` stands for as a dependency of a node
-  // that acquires `ev` (published by node `pub`): an operator task is itself,
-  // a sync task its own dependencies. The publisher is left out when every
-  // sync on the way joins `ev` (its tiles are waited for one by one).
-  void expand(std::int32_t x, bool joined, std::int32_t ev, std::int32_t pub,
-              std::uint32_t &wait, std::vector<std::uint8_t> &seen) const {
-    std::uint8_t const mark = joined ? 2 : 1;
-    if (seen[x] & mark) return;
-    seen[x] |= mark;
+  // Adds to `wait` the nodes that `x` stands for as a dependency of a node:
+  // an operator task is itself, a sync task its own dependencies. `joined`
+  // holds the acquiring node's event tensors that every sync on the way so
+  // far joins; a publisher of one of them is waited for tile by tile, so it
+  // is left out.
+  void expand(std::int32_t x, std::uint32_t joined, std::uint32_t &wait,
+              std::vector<std::vector<std::uint32_t>> &seen) const {
+    for (std::uint32_t m : seen[x]) {
+      if (m == joined) return;
+    }
+    seen[x].push_back(joined);
     linked_task const &t = tasks[x];
     if (t.kind == task_kind::operator_body) {
       std::int32_t const n = node_of[x];
-      if (!(joined && n == pub)) wait |= 1u << n;
+      if ((g->nodes[n].publish & joined) == 0) wait |= 1u << n;
       return;
     }
-    bool const still = joined && joins(t, ev);
+    std::uint32_t const still = joined & join_mask(t);
     for (attr const &a : t.attributes.entries()) {
       if (a.kind == attr_kind::dependency) {
-        expand(static_cast<std::int32_t>(a.task.value), still, ev, pub, wait, seen);
+        expand(static_cast<std::int32_t>(a.task.value), still, wait, seen);
       }
     }
   }
@@ -120,7 +123,7 @@ status lower(graph &out, std::span<linked_task const> tasks,
     linked_task const &t = tasks[i];
     std::int64_t tiles = 0;
     bool has_grid = false;
-    std::int32_t publish = no_event, acquire = no_event;
+    std::uint32_t publish = 0, acquire = 0;
     for (attr const &a : t.attributes.entries()) {
       if (a.kind == attr_kind::dispatch_tile_grid) {
         if (a.first < 0 || a.second < 0) {
@@ -132,13 +135,7 @@ status lower(graph &out, std::span<linked_task const> tasks,
         if (a.event.value >= events.size()) {
           return fail(status_code::invalid_argument, 6, "event tensor reference out of range");
         }
-        std::int32_t &slot = a.kind == attr_kind::event_publish ? publish : acquire;
-        std::int32_t const ev = static_cast<std::int32_t>(a.event.value);
-        if (slot != no_event && slot != ev) {
-          return fail(status_code::unsupported, 9,
-                      "a co-resident task publishes / acquires at most one event tensor");
-        }
-        slot = ev;
+        (a.kind == attr_kind::event_publish ? publish : acquire) |= 1u << a.event.value;
       }
     }
     grid_tiles += tiles;
@@ -152,17 +149,22 @@ status lower(graph &out, std::span<linked_task const> tasks,
     nd.phase_task = static_cast<std::int32_t>(i);
     nd.publish = publish;
     nd.acquire = acquire;
-    // Without a tile grid, a task that acquires an event tensor has one unit
+    // Without a tile grid, a task that acquires event tensors has one unit
     // per slot (it consumes each tile as it is published); else one unit.
-    nd.units = has_grid ? tiles : (acquire != no_event ? g.events[acquire].slots : 1);
+    std::int32_t first_acquired = -1;
+    for (std::int32_t e = 0; e < g.event_count && first_acquired < 0; ++e) {
+      if ((acquire >> e) & 1u) first_acquired = e;
+    }
+    nd.units = has_grid ? tiles : (first_acquired >= 0 ? g.events[first_acquired].slots : 1);
     if (nd.units > kMaxUnits) {
       return fail(status_code::unsupported, 10, "too many work units");
     }
-    if (publish != no_event) {
-      if (g.events[publish].publisher >= 0) {
+    for (std::int32_t e = 0; e < g.event_count; ++e) {
+      if (((publish >> e) & 1u) == 0) continue;
+      if (g.events[e].publisher >= 0) {
         return fail(status_code::unsupported, 9, "an event tensor is published by two tasks");
       }
-      g.events[publish].publisher = n;
+      g.events[e].publisher = n;
     }
   }
   if (grid_tiles != dispatch.total_tile_count) {
@@ -188,34 +190,37 @@ status lower(graph &out, std::span<linked_task const> tasks,
     }
   }
 
-  // A tensor that is published or acquired on the device needs its storage.
-  for (std::int32_t e = 0; e < g.event_count; ++e) {
-    bool used = g.events[e].publisher >= 0;
-    for (std::int32_t n = 0; n < g.node_count; ++n) used = used || g.nodes[n].acquire == e;
-    if (used && g.events[e].storage == nullptr) {
-      return fail(status_code::invalid_argument, 6,
-                  "an event tensor used on the device needs symmetric_i32_storage");
+  // Every tensor a node publishes or acquires has one slot per unit (tile t
+  // uses slot t), storage, and for an acquire an earlier publisher.
+  for (std::int32_t n = 0; n < g.node_count; ++n) {
+    node const &nd = g.nodes[n];
+    for (std::int32_t e = 0; e < g.event_count; ++e) {
+      bool const pub = (nd.publish >> e) & 1u, acq = (nd.acquire >> e) & 1u;
+      if (!pub && !acq) continue;
+      event const &ev = g.events[e];
+      if (ev.slots != nd.units) {
+        return fail(status_code::invalid_argument, 6,
+                    "a published or acquired event tensor needs one slot per tile of the task");
+      }
+      if (ev.storage == nullptr) {
+        return fail(status_code::invalid_argument, 6,
+                    "an event tensor used on the device needs symmetric_i32_storage");
+      }
+      if (acq && (ev.publisher < 0 || ev.publisher == n || position[ev.publisher] > position[n])) {
+        return fail(status_code::invalid_argument, 6,
+                    "an acquired event tensor needs a publisher earlier in the queue");
+      }
     }
   }
 
-  // Waits: per tile for the acquired tensor, per node for the rest.
+  // Waits: per tile for the acquired tensors, per node for the rest.
   for (std::int32_t n = 0; n < g.node_count; ++n) {
     node &nd = g.nodes[n];
-    std::int32_t pub = -1;
-    if (nd.acquire != no_event) {
-      event const &ev = g.events[nd.acquire];
-      pub = ev.publisher;
-      if (pub < 0 || pub == n || position[pub] > position[n] || ev.slots != nd.units ||
-          ev.slots != g.nodes[pub].units) {
-        return fail(status_code::invalid_argument, 6,
-                    "an acquired event tensor needs an earlier publisher with one tile per slot");
-      }
-    }
-    std::vector<std::uint8_t> seen(tasks.size(), 0);
+    std::vector<std::vector<std::uint32_t>> seen(tasks.size());
     std::uint32_t wait = 0;
     for (attr const &a : tasks[nd.phase_task].attributes.entries()) {
       if (a.kind == attr_kind::dependency) {
-        low.expand(static_cast<std::int32_t>(a.task.value), true, nd.acquire, pub, wait, seen);
+        low.expand(static_cast<std::int32_t>(a.task.value), nd.acquire, wait, seen);
       }
     }
     nd.wait_nodes = wait;

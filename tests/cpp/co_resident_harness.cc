@@ -27,10 +27,12 @@ extern "C" {
 // event tensor e a (never dereferenced) storage attribute. progress 0 asap, 1
 // co_resident_persistent. Lowers it; outputs the status (code, detail), the
 // graph header (node_count, units, event_count) and per node (8 int64 each):
-// phase task, publish, acquire, wait mask, units, first unit, queue position,
-// and per event (2 int64): slots, publisher.
+// phase task, publish mask, acquire mask, wait mask, units, first unit, queue
+// position, and per event (2 int64): slots, publisher. ev[i * 3 + 1] may name
+// a second acquired tensor through ev2[i] (-1 = none).
 int harness_co_resident(int n, const std::int32_t *kinds, const std::int32_t *deps,
-                        const std::int64_t *tile_grid, const std::int32_t *ev, int n_events,
+                        const std::int64_t *tile_grid, const std::int32_t *ev,
+                        const std::int32_t *ev2, int n_events,
                         const std::int64_t *event_shape, std::uint32_t storage_mask,
                         int progress, std::int32_t status_out[2],
                         std::int64_t header[3], std::int64_t *nodes, std::int64_t *events) {
@@ -57,6 +59,7 @@ int harness_co_resident(int n, const std::int32_t *kinds, const std::int32_t *de
     if (tile_grid[2 * i] > 0) set.push(rt::dispatcher::tile_grid(tile_grid[2 * i], tile_grid[2 * i + 1]));
     if (ev[3 * i + 0] >= 0) set.push(rt::events::publish(evs[ev[3 * i + 0]]));
     if (ev[3 * i + 1] >= 0) set.push(rt::events::acquire(evs[ev[3 * i + 1]]));
+    if (ev2[i] >= 0) set.push(rt::events::acquire(evs[ev2[i]]));
     if (ev[3 * i + 2] >= 0) set.push(rt::events::join(evs[ev[3 * i + 2]]));
     if (kinds[i] == 1) {
       phase.sync(set);

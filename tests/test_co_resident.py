@@ -18,10 +18,13 @@ def lib():
     return ctypes.CDLL(build.build_harness())
 
 
-def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1, storage=0xFFFF):
+def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1, storage=0xFFFF, ev2=None):
+    """ev[i] = [published, acquired, joined] event tensor of task i (-1 = none);
+    ev2[i] = a second acquired tensor. Node publish / acquire come back as bit masks."""
     n = len(kinds)
     grids = grids or [[0, 0]] * n
     ev = ev or [[-1, -1, -1]] * n
+    ev2 = ev2 or [-1] * n
     flat = []
     for d in deps:
         flat += list(d) + [-1] * (MAX_DEPS - len(d))
@@ -33,7 +36,7 @@ def lower(lib, kinds, deps, grids=None, ev=None, events=(), progress=1, storage=
     lib.harness_co_resident(
         n, (i32 * max(n, 1))(*kinds), (i32 * max(len(flat), 1))(*flat),
         (i64 * max(2 * n, 1))(*[v for g in grids for v in g]),
-        (i32 * max(3 * n, 1))(*[v for e in ev for v in e]), len(events),
+        (i32 * max(3 * n, 1))(*[v for e in ev for v in e]), (i32 * max(n, 1))(*ev2), len(events),
         (i64 * max(2 * len(events), 1))(*[v for e in events for v in e]), storage, progress,
         status,
         header, nodes, evs)
@@ -57,9 +60,9 @@ def test_reference_orchestration_becomes_tile_level(lib):
               ev=[[0, -1, -1], [-1, -1, 0], [-1, 0, -1]], events=[[4, 3]])
     assert g["status"] == [0, 0] and g["node_count"] == 2 and g["units"] == 24
     gemm, red = g["nodes"]
-    assert (gemm["task"], gemm["units"], gemm["first"], gemm["publish"]) == (0, 12, 0, 0)
+    assert (gemm["task"], gemm["units"], gemm["first"], gemm["publish"]) == (0, 12, 0, 0b1)
     # one unit per slot, waited for tile by tile: no whole-task wait
-    assert (red["task"], red["units"], red["first"], red["acquire"], red["wait"]) == (2, 12, 12, 0, 0)
+    assert (red["task"], red["units"], red["first"], red["acquire"], red["wait"]) == (2, 12, 12, 0b1, 0)
     assert g["events"] == [dict(slots=12, publisher=0)]
 
 
@@ -117,6 +120,39 @@ def test_device_event_tensors_need_storage(lib):
     assert lower(lib, *args, storage=0)["status"] == [1, 6]
     # a tensor nobody publishes or acquires on the device may go without
     assert lower(lib, [0], [[]], events=[[1, 2]], storage=0)["status"] == [0, 0]
+
+
+def test_two_acquired_tensors_are_both_tile_level(lib):
+    # P0 publishes E0, P1 publishes E1 (same shape); C acquires both and
+    # depends on both directly: no whole-node wait, one unit per slot.
+    g = lower(lib, [0, 0, 0], [[], [], [0, 1]], grids=[[2, 3], [2, 3], [0, 0]],
+              ev=[[0, -1, -1], [1, -1, -1], [-1, 0, -1]], ev2=[-1, -1, 1],
+              events=[[2, 3], [2, 3]])
+    assert g["status"] == [0, 0]
+    c = g["nodes"][2]
+    assert (c["acquire"], c["units"], c["wait"]) == (0b11, 6, 0)
+    # different slot counts cannot both be one per tile
+    g = lower(lib, [0, 0, 0], [[], [], [0, 1]], grids=[[2, 3], [1, 3], [0, 0]],
+              ev=[[0, -1, -1], [1, -1, -1], [-1, 0, -1]], ev2=[-1, -1, 1],
+              events=[[2, 3], [1, 3]])
+    assert g["status"] == [1, 6]
+
+
+def test_a_sync_joining_one_of_two_tensors(lib):
+    # S joins E0 only: through S, P0 is tile-level but P1 is a whole-node wait.
+    g = lower(lib, [0, 0, 1, 0], [[], [], [0, 1], [2]], grids=[[1, 4], [1, 4], [0, 0], [0, 0]],
+              ev=[[0, -1, -1], [1, -1, -1], [-1, -1, 0], [-1, 0, -1]], ev2=[-1, -1, -1, 1],
+              events=[[1, 4], [1, 4]])
+    assert g["status"] == [0, 0]
+    assert g["nodes"][2]["wait"] == 0b10
+
+
+def test_published_tensor_needs_one_slot_per_tile(lib):
+    # 8 tiles publishing into 4 slots would write past the tensor
+    assert lower(lib, [0], [[]], grids=[[2, 4]], ev=[[0, -1, -1]],
+                 events=[[2, 2]])["status"] == [1, 6]
+    assert lower(lib, [0], [[]], grids=[[2, 4]], ev=[[0, -1, -1]],
+                 events=[[2, 4]])["status"] == [0, 0]
 
 
 def test_node_capacity(lib):
@@ -203,13 +239,14 @@ def test_random_graphs_cover_every_dependency(lib, seed):
         need = {node_of[x] for x in _reachable_ops(t, kinds, deps)}
         waits = {j for j in range(len(ops)) if (nd["wait"] >> j) & 1}
         assert waits <= need                                   # no spurious waits
-        pub = g["events"][nd["acquire"]]["publisher"] if nd["acquire"] >= 0 else None
-        assert need - waits <= ({pub} if pub is not None else set())
-        for j in waits | ({pub} if pub is not None else set()):
+        acquired = [e for e in range(len(shapes)) if (nd["acquire"] >> e) & 1]
+        pubs = {g["events"][e]["publisher"] for e in acquired}
+        assert need - waits <= pubs                            # the rest: tile by tile
+        for j in waits | pubs:
             assert g["nodes"][j]["pos"] < nd["pos"]             # waits target earlier units
-        if nd["acquire"] >= 0:
-            assert g["nodes"][pub]["units"] == nd["units"] == shapes[nd["acquire"]][0] * \
-                shapes[nd["acquire"]][1]
+        for e in acquired:
+            pub = g["events"][e]["publisher"]
+            assert g["nodes"][pub]["units"] == nd["units"] == shapes[e][0] * shapes[e][1]
 
 
 FAKE = 0x100000  # never dereferenced: validation-only calls
