@@ -269,3 +269,30 @@ def test_f32_entry_validation_only():
     assert (st.code, st.detail) == (1, 1)
     # the state holds the graph (16 nodes, 16 event tensors) and the counters
     assert mb.co_resident_control_bytes() >= 16 * 32 + 16 * 24 + 4 * (4 + 16)
+
+
+def build_example(out_dir):
+    """Compiles tests/cpp/co_resident_example.cu (a three-task phase with
+    per-tile dataflow and its own device operators, built on the public
+    headers) against libmegacu_b200.so; returns the executable's path."""
+    import os
+    import shutil
+    import subprocess
+
+    from megacu_b200 import build
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("nvcc not found")
+    exe = os.path.join(out_dir, "co_resident_example")
+    cmd = [nvcc, "-std=c++20", "-O2", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-I" + os.path.join(build.ROOT, "include"),
+           os.path.join(build.ROOT, "tests", "cpp", "co_resident_example.cu"),
+           "-L" + build.LIB_DIR, "-lmegacu_b200", "-Xlinker", "-rpath=" + build.LIB_DIR,
+           "-o", exe]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    return exe
+
+
+def test_example_program_builds(tmp_path):
+    assert build_example(str(tmp_path))

@@ -105,3 +105,14 @@ def test_two_pes_match_oracle():
             torch.cuda.synchronize(pe)
         for t in teams:
             t.close()
+
+
+def test_three_task_example_with_two_acquired_tensors(tmp_path):
+    """tests/cpp/co_resident_example.cu: fill -> scale -> sum, the last task
+    acquiring both tensors, one persistent launch, checked on the host."""
+    import subprocess
+
+    from test_co_resident import build_example
+    exe = build_example(str(tmp_path))
+    proc = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0 and proc.stdout.strip() == "ok", proc.stdout + proc.stderr
