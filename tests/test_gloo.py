@@ -1,7 +1,8 @@
 """World-size-2 gloo runs on the CPU: the host side of the N > 1 path.
 
 * The team handle exchange (`megacu_b200.torch_exchange`) delivers every
-  PE's handle in PE order.
+  PE's handle in PE order, and ends with an error (not a hang) when a rank
+  has died.
 * The product's tile plan (`plan_tile`, the device queue's schedule) drives a
   CPU emulation of the two-shot allreduce, the reduce-scatter and the
   all-gather + GEMM (each rank's own raster) across real processes: each rank sends its partial tiles to their owners, owners reduce
@@ -162,3 +163,43 @@ def test_two_rank_gloo(tmp_path):
     results = [open(tmp_path / f"rank{r}").read() if (tmp_path / f"rank{r}").exists() else "missing"
                for r in range(world)]
     assert results == ["ok"] * world, results
+
+
+def _dying_worker(rank, world, port, result_dir):
+    """Rank 1 leaves right after joining; rank 0's handle exchange must end
+    with an error (within the process group's timeout), not hang."""
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    status = "ok"
+    try:
+        if rank == 1:
+            os._exit(0)  # a rank that dies between steps
+        import sys
+        sys.path.insert(0, os.path.dirname(HERE))
+        import megacu_b200 as mb
+        try:
+            mb.torch_exchange()(bytes(128))
+            status = "exchange returned without the peer"
+        except Exception as exc:  # noqa: BLE001 - any error is the expected outcome
+            status = f"error: {type(exc).__name__}"
+    finally:
+        with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
+            f.write(status)
+
+
+def test_exchange_fails_when_a_rank_dies(tmp_path):
+    world = 2
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, world, port, str(tmp_path)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    result = (tmp_path / "rank0").read_text() if (tmp_path / "rank0").exists() else "missing"
+    assert result.startswith("error:"), result
