@@ -29,7 +29,9 @@ outside the CUDA events; every step's time is the max over ranks:
                            the fused time minus this is the exchange time
                            the kernel did not hide
 Configs 3 and ag report the mean per call, config 4 the p50. Prints one JSON
-line per shape on rank 0.
+line per shape on rank 0. ``--graph`` times every arm as the replay of a CUDA
+graph captured from it (launch overhead out of the measurement; an arm whose
+capture fails is timed as launched and marked so).
 """
 from __future__ import annotations
 
@@ -76,6 +78,28 @@ def roofline(config, m, n, k, tp, us):
             "frac": terms[bound] / us, "flops_per_pe": flops, "hbm_bytes_per_pe": hbm_bytes,
             "link_bytes_per_pe": link, "link": link_kind, "peak_tflops": peak,
             "peak_source": peak_src, "hbm_gbs": hbm, "hbm_source": hbm_src}
+
+
+def as_graphs(arms, names, stream):
+    """CUDA-graph versions of the arms (each captured from one call after the
+    warm-up); an arm that cannot be captured stays as it is. Returns the arms
+    and, per arm, whether it is a graph replay."""
+    import torch
+
+    out, graphed = [], {}
+    for arm, name in zip(arms, names):
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                arm()
+            torch.cuda.synchronize()
+            out.append(g.replay)
+            graphed[name] = True
+        except Exception:  # noqa: BLE001 - the arm is then timed as launched
+            torch.cuda.synchronize()
+            out.append(arm)
+            graphed[name] = False
+    return out, graphed
 
 
 def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
@@ -140,11 +164,14 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
             team.barrier(stream)
 
     heat = args.heat_calls if args.heat_calls >= 0 else (200 if config == 3 else 2000)
+    graphed = None
     with ClockSampler(local) as clocks:
         for _ in range(heat):
             fused()
             unfused()
         torch.cuda.synchronize()
+        if args.graph:
+            arms, graphed = as_graphs(arms, names, stream)
         ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
     mb.events_status(events, stream)
     if solo_events is not None:
@@ -164,6 +191,7 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         "roofline_call": roofline(config, m, n, k, tp, us["fused"]),
         "exposed_comm_us": (us["fused"] - us["kernel_without_exchange"]) if tp > 1 else None,
         "l2": "flushed (256 MiB write) before every timed step",
+        "cuda_graph_replay": graphed,
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -271,6 +299,8 @@ def main() -> int:
     ap.add_argument("--m", default="", help="config 4: comma-separated token counts")
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--graph", action="store_true",
+                    help="time each arm as the replay of a CUDA graph captured from it")
     ap.add_argument("--heat-calls", type=int, default=-1,
                     help="untimed calls of the fused and unfused arms before timing "
                          "(default: about two seconds of work)")
