@@ -5,7 +5,6 @@ import numpy as np
 import torch
 
 import megacu_b200 as mb
-import oracle_lib
 
 # Tolerance of the bf16 path (north star: max relative error 1e-2, bf16 inputs,
 # fp32 accumulate). Per element, the error is taken relative to |want| plus
