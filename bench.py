@@ -32,7 +32,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from megacu_b200.measure import NVLINK_GBS, ClockSampler, NvlinkCounters, peaks, seeded  # noqa: E402
+from megacu_b200.measure import (NVLINK_GBS, ClockSampler, NvlinkCounters, interleaved,  # noqa: E402
+                                  mean, peaks, seeded)
 
 M, N, K_TOTAL = 4096, 8192, 8192
 WORKLOAD = "C2 row-parallel GEMM+allreduce M4096 N8192 K8192/tp bf16"
@@ -163,36 +164,12 @@ def run_gpu(args, rank, world, local_rank):
         if tp > 1:
             team.barrier(stream)
 
-    def sync_all():
-        torch.cuda.synchronize()
-        if tp > 1:
-            dist.barrier()
-
     def timed_steps(bodies, steps, warmup):
-        """Times each body `steps` times, interleaved step by step (body 0,
-        body 1, ..., then the next step), so that every arm sees the same
-        clocks and temperature; returns the mean ms per step of each body,
-        the max over ranks."""
-        for _ in range(warmup):
-            for body in bodies:
-                align()
-                body()
-        sync_all()
-        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(steps)] for _ in bodies]
-        for i in range(steps):
-            for body, evs in zip(bodies, ev):
-                align()
-                evs[i][0].record(stream)
-                body()
-                evs[i][1].record(stream)
-        torch.cuda.synchronize()
-        total = torch.tensor([sum(s.elapsed_time(e) for s, e in evs) for evs in ev],
-                             dtype=torch.float64, device=dev)
-        if tp > 1:
-            dist.all_reduce(total, op=dist.ReduceOp.MAX)
-        sync_all()
-        return [float(x) / steps for x in total.tolist()]
+        """Times each body `steps` times with CUDA events, interleaved step by
+        step (body 0, body 1, ..., then the next step) so that every arm sees
+        the same clocks and temperature; returns, per body, the ms of every
+        step, each the max over ranks (megacu_b200.measure.interleaved)."""
+        return interleaved(bodies, steps, warmup, align, stream, tp, device=dev)
 
     # ---- fused megakernel (inputs resident) and the unfused baseline ----
     # Unfused baseline: cuBLAS GEMM, then NCCL allreduce of its output.
@@ -235,9 +212,14 @@ def run_gpu(args, rank, world, local_rank):
             fused()
             unfused()
         torch.cuda.synchronize()
-        times = timed_steps(arms, args.steps, args.warmup)
+        step_ms = timed_steps(arms, args.steps, args.warmup)
+    times = [mean(x) for x in step_ms]
     ms_fused, ms_unfused, ms_gemm = times[:3]
     ms_solo = times[3] if tp > 1 else None
+    fused_sorted = sorted(step_ms[0])
+    last = len(fused_sorted) - 1
+    fused_stats = {q: fused_sorted[min(last, int(frac * len(fused_sorted)))] * 1e3
+                   for q, frac in (("p10", 0.1), ("p50", 0.5), ("p90", 0.9))}
     mb.events_status(events, stream)
     if tp > 1:
         mb.events_status(solo_events, stream)
@@ -283,7 +265,8 @@ def run_gpu(args, rank, world, local_rank):
         call(a, b)
         out_host.copy_(out[rank * rows_back:(rank + 1) * rows_back], non_blocking=True)
 
-    (ms_e2e,) = timed_steps([e2e_body], max(3, args.steps // 2), max(1, args.warmup // 2))
+    (e2e_steps,) = timed_steps([e2e_body], max(3, args.steps // 2), max(1, args.warmup // 2))
+    ms_e2e = mean(e2e_steps)
     h2d = a_host.numel() * 2 + b_host.numel() * 2
     d2h = out_host.numel() * 2
 
@@ -324,6 +307,8 @@ def run_gpu(args, rank, world, local_rank):
                        "exchange": exchange_kind,
                        "l2": "flushed (256 MiB write) before every timed step"},
             "us_per_call": ms_fused * 1e3,
+            "us_per_call_stats": dict(fused_stats, steps=args.steps,
+                                      note="per-step max over ranks; us_per_call is their mean"),
             "tflops_per_gpu": achieved,
             "e2e": {"value": flops_total / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
