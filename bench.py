@@ -41,6 +41,15 @@ METRIC = "GEMM+allreduce TFLOP/s (whole job), C2 M4096 N8192 K8192 split over tp
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 
 
+def traffic_for(key):
+    """DRAM bytes of one launch from profiles/traffic.json (an ncu capture), or None."""
+    try:
+        with open(TRAFFIC_PATH) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
 def env_int(name, default):
     try:
         return int(os.environ.get(name, default))
