@@ -36,3 +36,48 @@ def undefined_globals(path):
 @pytest.mark.parametrize("rel", FILES)
 def test_no_undefined_names(rel):
     assert undefined_globals(os.path.join(ROOT, rel)) == []
+
+
+# Module aliases whose attributes the GPU-only code paths use; every
+# attribute read through them must exist (run on the CPU, these paths never
+# execute, so a misspelt or removed name would only show on a B200).
+MODULES = {"megacu_b200": "megacu_b200", "mb": "megacu_b200", "_capi": "megacu_b200._capi",
+           "oracle_lib": "oracle_lib", "measure": "megacu_b200.measure",
+           "build": "megacu_b200.build", "timeline": "megacu_b200.timeline",
+           "shapes_bench": "megacu_b200.shapes_bench", "gpu_util": "gpu_util"}
+
+
+def missing_attributes(path):
+    import ast
+    import importlib
+
+    tree = ast.parse(open(path).read())
+    aliases = {}
+    for node in ast.walk(tree):
+        if isinstance(node, ast.Import):
+            for a in node.names:
+                name = a.asname or a.name
+                if a.name in MODULES.values():
+                    aliases[name] = a.name
+        elif isinstance(node, ast.ImportFrom) and node.module:
+            for a in node.names:
+                full = f"{node.module}.{a.name}"
+                if full in MODULES.values():
+                    aliases[a.asname or a.name] = full
+    missing = []
+    for node in ast.walk(tree):
+        if (isinstance(node, ast.Attribute) and isinstance(node.value, ast.Name)
+                and node.value.id in aliases):
+            mod = importlib.import_module(aliases[node.value.id])
+            if not hasattr(mod, node.attr):
+                missing.append(f"{node.value.id}.{node.attr} (line {node.lineno})")
+    return missing
+
+
+SOURCES = FILES + [os.path.join("tests", f) for f in sorted(os.listdir(os.path.join(ROOT, "tests")))
+                   if f.endswith(".py")]
+
+
+@pytest.mark.parametrize("rel", SOURCES)
+def test_module_attributes_exist(rel):
+    assert missing_attributes(os.path.join(ROOT, rel)) == []
