@@ -33,7 +33,12 @@ def undefined_globals(path):
     return missing
 
 
-@pytest.mark.parametrize("rel", FILES)
+def _sources():
+    tests = sorted(f for f in os.listdir(os.path.join(ROOT, "tests")) if f.endswith(".py"))
+    return FILES + [os.path.join("tests", f) for f in tests]
+
+
+@pytest.mark.parametrize("rel", _sources())
 def test_no_undefined_names(rel):
     assert undefined_globals(os.path.join(ROOT, rel)) == []
 
@@ -74,10 +79,6 @@ def missing_attributes(path):
     return missing
 
 
-SOURCES = FILES + [os.path.join("tests", f) for f in sorted(os.listdir(os.path.join(ROOT, "tests")))
-                   if f.endswith(".py")]
-
-
-@pytest.mark.parametrize("rel", SOURCES)
+@pytest.mark.parametrize("rel", _sources())
 def test_module_attributes_exist(rel):
     assert missing_attributes(os.path.join(ROOT, rel)) == []
