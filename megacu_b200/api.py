@@ -173,6 +173,12 @@ class Team:
             check(lib().megacu_b200_team_destroy(self.handle))
             self.handle = None
 
+    def __enter__(self) -> "Team":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
     def view(self) -> _capi.TeamView:
         return _capi.TeamView(team=self.handle, team_my_pe=self.my_pe, team_n_pes=self.n_pes,
                               world_my_pe=self.my_pe, world_n_pes=self.n_pes,

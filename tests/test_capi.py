@@ -153,3 +153,14 @@ def test_header_is_plain_c_and_links():
                "-lmegacu_b200", "-o", os.path.join(tmp, "abi")]
         proc = subprocess.run(cmd, capture_output=True, text=True)
         assert proc.returncode == 0, proc.stderr
+
+
+def test_team_context_manager_closes_once():
+    """`with Team(...) as t:` closes the team on exit; close() is idempotent
+    (a team object without a handle, as after close(), does nothing)."""
+    t = mb.Team.__new__(mb.Team)
+    t.handle = None
+    with t as same:
+        assert same is t
+    t.close()
+    assert t.handle is None
