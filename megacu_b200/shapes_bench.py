@@ -31,7 +31,10 @@ outside the CUDA events; every step's time is the max over ranks:
 Configs 3 and ag report the mean per call, config 4 the p50. Prints one JSON
 line per shape on rank 0. ``--graph`` times every arm as the replay of a CUDA
 graph captured from it (launch overhead out of the measurement; an arm whose
-capture fails is timed as launched and marked so).
+capture fails is timed as launched and marked so). ``--algo one|two`` forces
+the allreduce exchange of config 4 (auto picks one-shot for one tile row),
+and ``--multicast`` puts a two-shot call's workspace and output in the team's
+multicast region (the in-switch reduction).
 """
 from __future__ import annotations
 
@@ -47,7 +50,7 @@ C4 = dict(m=(16, 32, 64, 128), n=8192, k_total=28672)
 AG = dict(m=8192, n_total=28672, k=8192)
 
 
-def roofline(config, m, n, k, tp, us):
+def roofline(config, m, n, k, tp, us, one_shot=True, in_switch=False):
     """Slower of the GEMM at the measured bf16 peak, the weight stream at the
     measured HBM bandwidth (it bounds the decode shapes) and the exchange's
     bytes per PE over NVLink at the measured 770 GB/s per direction. m, n, k
@@ -62,9 +65,15 @@ def roofline(config, m, n, k, tp, us):
     elif config == "ag":
         link = (tp - 1) / tp * m * k * 2          # the other PEs' shards of A, received
         link_kind = "all-gather (tp-1)/tp x A"
-    else:
+    elif one_shot:
         link = (tp - 1) * out_bytes               # one-shot: every partial to every peer
         link_kind = "one-shot (tp-1) x output"
+    elif in_switch:
+        link = (1 + 1 / tp) * out_bytes           # NVLS: each PE's slots and sums once
+        link_kind = "in-switch two-shot (1 + 1/tp) x output"
+    else:
+        link = 2 * (tp - 1) / tp * out_bytes      # two-shot bus bytes
+        link_kind = "two-shot 2 (tp-1)/tp x output"
     # Bytes the GEMM must move through HBM at least once: A, B and the
     # partial / output tile writes (for `ag` also the gathered A's write).
     hbm_bytes = 2.0 * (m * k + k * n) + out_bytes
@@ -113,17 +122,22 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
     tp = world
     k = k_total // tp
     mode = mb.MODE_REDUCE_SCATTER if config == 3 else mb.MODE_ALLREDUCE
+    algo = {"auto": mb.ALGO_AUTO, "one": mb.ALGO_ONE_SHOT, "two": mb.ALGO_TWO_SHOT}[args.algo]
     a = seeded(1000 * config + 10 * rank + 0, (m, k), 0.02).to(dev)
     b = seeded(1000 * config + 10 * rank + 1, (k, n), 0.02).to(dev)
-    prob = mb.Problem(m, n, k, mode=mode, timeout_ns=30_000_000_000)
+    prob = mb.Problem(m, n, k, mode=mode, algo=algo if config == 4 else mb.ALGO_AUTO,
+                      timeout_ns=30_000_000_000)
     pl = mb.plan(prob, tp)
     ws_bytes = max(mb.workspace_bytes(prob, tp), 16)
     ev_bytes = mb.events_bytes(prob, tp)
     rows = m // tp if config == 3 else m
-    team = team_cache(ws_bytes + ev_bytes + rows * n * 2 + (64 << 20))
-    ws = team.tensor((ws_bytes,), torch.uint8)
+    want_mc = (args.multicast and tp > 1 and mode == mb.MODE_ALLREDUCE and not pl.one_shot)
+    team = team_cache(ws_bytes + ev_bytes + rows * n * 2 + (64 << 20),
+                      (ws_bytes + rows * n * 2 + (1 << 20)) if want_mc else 0)
+    use_mc = want_mc and team.multicast
+    ws = team.tensor((ws_bytes,), torch.uint8, multicast=use_mc)
     events = team.tensor((ev_bytes // 4,), torch.int32)
-    out = team.tensor((rows, n), torch.bfloat16)
+    out = team.tensor((rows, n), torch.bfloat16, multicast=use_mc)
     c = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     c_rs = torch.empty((rows, n), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -187,8 +201,10 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         "us_per_call": us,
         "tflops_per_gpu": {name: flops_job / tp / (u * 1e-6) / 1e12 for name, u in us.items()},
         "plan": {"tile": [pl.tile_m, pl.tile_n], "tiles": pl.tiles, "one_shot": pl.one_shot,
-                 "cta_pairs": pl.cta_pairs, "gemm_units": pl.gemm_units},
-        "roofline_call": roofline(config, m, n, k, tp, us["fused"]),
+                 "cta_pairs": pl.cta_pairs, "gemm_units": pl.gemm_units,
+                 "in_switch": use_mc},
+        "roofline_call": roofline(config, m, n, k, tp, us["fused"], one_shot=pl.one_shot,
+                                  in_switch=use_mc),
         "exposed_comm_us": (us["fused"] - us["kernel_without_exchange"]) if tp > 1 else None,
         "l2": "flushed (256 MiB write) before every timed step",
         "cuda_graph_replay": graphed,
@@ -299,6 +315,10 @@ def main() -> int:
     ap.add_argument("--m", default="", help="config 4: comma-separated token counts")
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--algo", choices=("auto", "one", "two"), default="auto",
+                    help="config 4: the allreduce exchange (auto: one-shot for one tile row)")
+    ap.add_argument("--multicast", action="store_true",
+                    help="two-shot calls reduce in the switch (team multicast region)")
     ap.add_argument("--graph", action="store_true",
                     help="time each arm as the replay of a CUDA graph captured from it")
     ap.add_argument("--heat-calls", type=int, default=-1,
@@ -317,14 +337,15 @@ def main() -> int:
                                 device_id=torch.device("cuda", local))
     teams = []
 
-    def team_cache(heap_bytes):
+    def team_cache(heap_bytes, multicast_bytes=0):
         # One team per shape (a team's heap is sized once); the previous one
         # is closed first, collectively.
         for t in teams:
             t.close()
         teams.clear()
         teams.append(mb.Team(rank, world, local, heap_bytes,
-                             mb.torch_exchange() if world > 1 else None))
+                             mb.torch_exchange() if world > 1 else None,
+                             multicast_bytes=multicast_bytes))
         return teams[0]
 
     try:

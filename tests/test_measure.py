@@ -91,3 +91,16 @@ def test_interleaved_orders_arms_and_takes_the_max_over_ranks(monkeypatch):
     bodies = [x[1] for x in log if x[0] == "body"]
     assert bodies == [0, 1] * 5                      # 2 warm-up + 3 timed rounds
     assert sum(1 for x in log if x[0] == "align") == 10
+
+
+def test_decode_link_bytes_by_exchange():
+    m, n, k, tp = 128, 8192, 3584, 8
+    out = m * n * 2
+    one = shapes_bench.roofline(4, m, n, k, tp, us=20.0)
+    two = shapes_bench.roofline(4, m, n, k, tp, us=20.0, one_shot=False)
+    nvls = shapes_bench.roofline(4, m, n, k, tp, us=20.0, one_shot=False, in_switch=True)
+    assert one["link_bytes_per_pe"] == 7 * out
+    assert two["link_bytes_per_pe"] == pytest.approx(2 * 7 / 8 * out)
+    assert nvls["link_bytes_per_pe"] == pytest.approx(9 / 8 * out)
+    # at M = 128 the one-shot exchange, not the weight stream, bounds the call
+    assert one["bound"] == "nvlink" and two["bound"] == "hbm"
