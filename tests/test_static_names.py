@@ -82,3 +82,45 @@ def missing_attributes(path):
 @pytest.mark.parametrize("rel", _sources())
 def test_module_attributes_exist(rel):
     assert missing_attributes(os.path.join(ROOT, rel)) == []
+
+
+def bad_calls(path):
+    """Calls `alias.f(...)` into the modules above whose keyword names or
+    positional count do not fit f's signature (classes: their __init__)."""
+    import ast
+    import importlib
+    import inspect
+
+    tree = ast.parse(open(path).read())
+    aliases = {}
+    for node in ast.walk(tree):
+        if isinstance(node, ast.Import):
+            for a in node.names:
+                if a.name in MODULES.values():
+                    aliases[a.asname or a.name] = a.name
+    bad = []
+    for node in ast.walk(tree):
+        if not (isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute)
+                and isinstance(node.func.value, ast.Name) and node.func.value.id in aliases):
+            continue
+        mod = importlib.import_module(aliases[node.func.value.id])
+        fn = getattr(mod, node.func.attr, None)
+        if fn is None or not callable(fn):
+            continue
+        try:
+            sig = inspect.signature(fn)
+        except (TypeError, ValueError):
+            continue  # ctypes functions and builtins
+        if any(isinstance(a, ast.Starred) for a in node.args) or any(
+                k.arg is None for k in node.keywords):
+            continue
+        try:
+            sig.bind_partial(*range(len(node.args)), **{k.arg: None for k in node.keywords})
+        except TypeError as exc:
+            bad.append(f"{node.func.value.id}.{node.func.attr} line {node.lineno}: {exc}")
+    return bad
+
+
+@pytest.mark.parametrize("rel", _sources())
+def test_calls_fit_signatures(rel):
+    assert bad_calls(os.path.join(ROOT, rel)) == []
