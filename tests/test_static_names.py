@@ -115,7 +115,7 @@ def bad_calls(path):
                 k.arg is None for k in node.keywords):
             continue
         try:
-            sig.bind_partial(*range(len(node.args)), **{k.arg: None for k in node.keywords})
+            sig.bind(*range(len(node.args)), **{k.arg: None for k in node.keywords})
         except TypeError as exc:
             bad.append(f"{node.func.value.id}.{node.func.attr} line {node.lineno}: {exc}")
     return bad
