@@ -124,3 +124,16 @@ def bad_calls(path):
 @pytest.mark.parametrize("rel", _sources())
 def test_calls_fit_signatures(rel):
     assert bad_calls(os.path.join(ROOT, rel)) == []
+
+
+@pytest.mark.parametrize("argv", [["bench.py", "--help"],
+                                  ["-m", "megacu_b200.shapes_bench", "--help"],
+                                  ["-m", "megacu_b200.mlp_bench", "--help"],
+                                  ["-m", "megacu_b200.timeline", "--help"]])
+def test_tools_parse_their_arguments(argv):
+    """The timing tools start and parse their options without a GPU."""
+    import subprocess
+    import sys
+    proc = subprocess.run([sys.executable, *argv], cwd=ROOT, capture_output=True, text=True,
+                          timeout=300)
+    assert proc.returncode == 0 and "usage" in proc.stdout.lower(), proc.stderr[-2000:]
