@@ -126,6 +126,118 @@ def test_calls_fit_signatures(rel):
     assert bad_calls(os.path.join(ROOT, rel)) == []
 
 
+_NO_DEFAULT = object()
+
+
+def _ast_signature(fn):
+    """inspect.Signature of an ast.FunctionDef (defaults as placeholders)."""
+    import inspect
+    P = inspect.Parameter
+    a = fn.args
+    positional = [(x, P.POSITIONAL_ONLY) for x in a.posonlyargs] + \
+                 [(x, P.POSITIONAL_OR_KEYWORD) for x in a.args]
+    first_default = len(positional) - len(a.defaults)
+    params = [P(x.arg, kind, default=None if i >= first_default else P.empty)
+              for i, (x, kind) in enumerate(positional)]
+    if a.vararg:
+        params.append(P(a.vararg.arg, P.VAR_POSITIONAL))
+    for x, d in zip(a.kwonlyargs, a.kw_defaults):
+        params.append(P(x.arg, P.KEYWORD_ONLY, default=P.empty if d is None else None))
+    if a.kwarg:
+        params.append(P(a.kwarg.arg, P.VAR_KEYWORD))
+    return inspect.Signature(params)
+
+
+def _importable(module):
+    """Modules the check may import: this package and the test helpers."""
+    return (module == "megacu_b200" or module.startswith("megacu_b200.")
+            or os.path.exists(os.path.join(ROOT, "tests", module + ".py")))
+
+
+def bad_bare_calls(path):
+    """Calls `f(...)` by a bare name whose arguments do not fit f: f imported
+    by `from <module> import f` (this package, relative imports included, or
+    a test helper) or a function defined once in the file itself outside a
+    class."""
+    import ast
+    import importlib
+    import inspect
+
+    tree = ast.parse(open(path).read())
+    rel_dir = os.path.relpath(os.path.dirname(path), ROOT)
+    package = "" if rel_dir in (".", "tests") else rel_dir.replace(os.sep, ".")
+    sigs, assigned, defined = {}, set(), {}
+
+    def visit(node, in_class):
+        for child in ast.iter_child_nodes(node):
+            if isinstance(child, (ast.FunctionDef, ast.AsyncFunctionDef)) and not in_class:
+                defined.setdefault(child.name, []).append(child)
+            if isinstance(child, ast.Name) and isinstance(child.ctx, ast.Store):
+                assigned.add(child.id)
+            if isinstance(child, ast.arg):
+                assigned.add(child.arg)
+            visit(child, isinstance(child, ast.ClassDef))
+
+    visit(tree, False)
+    for name, defs in defined.items():
+        if len(defs) == 1 and name not in assigned and not defs[0].decorator_list:
+            sigs[name] = _ast_signature(defs[0])
+    for node in ast.walk(tree):
+        if not isinstance(node, ast.ImportFrom):
+            continue
+        module = node.module or ""
+        if node.level:
+            base = package.split(".")[:len(package.split(".")) - (node.level - 1)]
+            module = ".".join([*base, module] if module else base)
+        if not _importable(module):
+            continue
+        mod = importlib.import_module(module)
+        for a in node.names:
+            obj = getattr(mod, a.name, None)
+            name = a.asname or a.name
+            if callable(obj) and not inspect.ismodule(obj) and name not in assigned:
+                try:
+                    sigs[name] = inspect.signature(obj)
+                except (TypeError, ValueError):
+                    pass
+    bad = []
+    for node in ast.walk(tree):
+        if not (isinstance(node, ast.Call) and isinstance(node.func, ast.Name)
+                and node.func.id in sigs):
+            continue
+        if any(isinstance(a, ast.Starred) for a in node.args) or any(
+                k.arg is None for k in node.keywords):
+            continue
+        try:
+            sigs[node.func.id].bind(*range(len(node.args)),
+                                    **{k.arg: None for k in node.keywords})
+        except TypeError as exc:
+            bad.append(f"{node.func.id} line {node.lineno}: {exc}")
+    return bad
+
+
+@pytest.mark.parametrize("rel", _sources())
+def test_bare_calls_fit_signatures(rel):
+    assert bad_bare_calls(os.path.join(ROOT, rel)) == []
+
+
+def test_bare_call_check_catches_a_mismatch(tmp_path):
+    """The check itself: a wrong keyword, a missing argument and a surplus
+    positional are each found, in a local function and an imported one."""
+    src = tmp_path / "probe.py"
+    src.write_text(
+        "from megacu_b200.measure import interleaved\n"
+        "def f(a, b=1, *, c):\n    return a\n"
+        "f(1, c=2)\n"            # fits
+        "f(1, d=2)\n"            # unknown keyword, c missing
+        "f(c=1)\n"               # a missing
+        "f(1, 2, 3, c=4)\n"      # surplus positional
+        "interleaved([], 1, 1, None, None, 1, device=None)\n"   # fits
+        "interleaved([], 1, 1, None, None)\n")                  # world missing
+    found = bad_bare_calls(str(src))
+    assert [x.split(" line ")[1].split(":")[0] for x in found] == ["5", "6", "7", "9"], found
+
+
 @pytest.mark.parametrize("argv", [["bench.py", "--help"],
                                   ["-m", "megacu_b200.shapes_bench", "--help"],
                                   ["-m", "megacu_b200.mlp_bench", "--help"],
