@@ -1,0 +1,197 @@
+"""bench.py's JSON line, checked without a GPU.
+
+The GPU leg (`run_gpu`) runs with CPU stand-ins for its CUDA calls: CUDA
+events that report a fixed time per rank, a no-op in place of the fused
+kernel and of cuBLAS, a team whose tensors are host tensors, and the "cuda"
+device mapped to the host. bench.py itself is not changed: its source is
+executed with `torch.device("cuda"` read as `torch.device("cpu"`. The numbers
+mean nothing; the test checks that the line carries every key of the
+driver's contract, that its arithmetic follows from the step times (value,
+roofline fraction, bytes per step, launches), and, with two gloo ranks, that
+the reported time is the max over ranks and only rank 0 prints. The
+reference arm (`--impl reference`) runs for real, on a short sample.
+"""
+from __future__ import annotations
+
+import contextlib
+import io
+import json
+import os
+import subprocess
+import sys
+import types
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+M, N, K_TOTAL = 4096, 8192, 8192
+STEPS, WARMUP, HEAT = 4, 3, 2
+
+
+def _rank_ms(rank):
+    return 1.0 + 0.5 * rank  # rank 1 is the slower one
+
+
+def _install_fakes(rank, launches, patch):
+    """Replaces the CUDA-only calls bench.py makes; `patch(obj, name, value)`
+    sets an attribute (pytest's monkeypatch, or plain setattr in a child)."""
+    import torch
+
+    import megacu_b200 as mb
+
+    class Event:
+        def __init__(self, enable_timing=False):
+            pass
+
+        def record(self, stream=None):
+            pass
+
+        def elapsed_time(self, other):
+            return _rank_ms(rank)
+
+    class Team:
+        def __init__(self, rank, tp, device, heap, exchange, multicast_bytes=0):
+            self.multicast = False
+
+        def tensor(self, shape, dtype, multicast=False):
+            return torch.zeros(shape, dtype=dtype)
+
+        def barrier(self, stream):
+            pass
+
+        def close(self):
+            pass
+
+    def gemm_allreduce(a, b, out, *, workspace, events, problem, stream=None, device=0,
+                       team=None, **kw):
+        assert a.dtype == b.dtype == out.dtype == torch.bfloat16
+        assert out.shape == (M, N) and a.shape[1] == b.shape[0] == problem.k
+        launches.append(problem.k)
+
+    patch(torch.cuda, "Event", Event)
+    patch(torch.cuda, "set_device", lambda *a: None)
+    patch(torch.cuda, "synchronize", lambda *a: None)
+    patch(torch.cuda, "current_stream", lambda *a: None)
+    patch(torch.cuda, "current_device", lambda: 0)
+    patch(torch.Tensor, "pin_memory", lambda self: self)
+    patch(torch, "matmul", lambda a, b, out=None: out)
+    patch(mb, "Team", Team)
+    patch(mb, "gemm_allreduce", gemm_allreduce)
+    patch(mb, "events_status", lambda *a, **k: None)
+
+
+def _bench_module():
+    src = open(os.path.join(ROOT, "bench.py")).read()
+    assert src.count('torch.device("cuda"') >= 1
+    mod = types.ModuleType("bench_on_host")
+    mod.__file__ = os.path.join(ROOT, "bench.py")
+    exec(compile(src.replace('torch.device("cuda"', 'torch.device("cpu"'), "bench.py", "exec"),
+         mod.__dict__)
+    return mod
+
+
+def _args(cpu_seconds=0.2, no_cpu=False):
+    import argparse
+    return argparse.Namespace(steps=STEPS, warmup=WARMUP, heat_calls=HEAT,
+                              cpu_seconds=cpu_seconds, no_cpu=no_cpu)
+
+
+REQUIRED = {"metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+            "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+            "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks"}
+
+
+def _check_line(line, tp, ms):
+    assert REQUIRED <= set(line), REQUIRED - set(line)
+    assert line["n_gpus"] == tp and line["steps"] == STEPS and line["warmup"] == WARMUP
+    assert line["ms_per_step"] == pytest.approx(ms)
+    flops = 2.0 * M * N * K_TOTAL
+    assert line["value"] == pytest.approx(flops / (ms * 1e-3) / 1e12)
+    assert line["higher_is_better"] is True and line["scaling"] == "strong"
+    assert line["config"]["workload"] and line["config"]["tp"] == tp
+    roof = line["roofline"]
+    assert {"bound", "achieved", "peak", "unit", "frac", "traffic"} <= set(roof)
+    assert roof["achieved"] == pytest.approx(flops / tp / (ms * 1e-3) / 1e12)
+    assert roof["frac"] == pytest.approx(roof["achieved"] / roof["peak"])
+    e2e = line["e2e"]
+    k = K_TOTAL // tp
+    assert e2e["h2d_bytes_per_step"] == (M * k + k * N) * 2
+    assert e2e["d2h_bytes_per_step"] == (M // tp) * N * 2
+    assert line["gpu_launches"] == STEPS
+    assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(line["clocks"])
+
+
+def test_one_gpu_line(monkeypatch):
+    launches = []
+    _install_fakes(0, launches, monkeypatch.setattr)
+    bench = _bench_module()
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        bench.run_gpu(_args(), 0, 1, 0)
+    lines = [x for x in buf.getvalue().splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    _check_line(line, 1, _rank_ms(0))
+    cpu = line["cpu_baseline"]
+    assert {"value", "unit", "cores", "kind", "sample"} <= set(cpu) and cpu["kind"] == "port"
+    assert cpu["value"] > 0 and cpu["cores"] >= 1
+    # heat-up, warm-up and timed steps of the fused arm, then the end-to-end
+    # arm's warm-up and steps: every one a single launch of the kernel
+    e2e_steps, e2e_warmup = max(3, STEPS // 2), max(1, WARMUP // 2)
+    assert len(launches) == HEAT + WARMUP + STEPS + e2e_warmup + e2e_steps
+
+
+def _rank_main(rank, out_dir, port):
+    os.environ.update(RANK=str(rank), WORLD_SIZE="2", LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=60))
+    launches = []
+    _install_fakes(rank, launches, setattr)
+    bench = _bench_module()
+    buf = io.StringIO()
+    try:
+        with contextlib.redirect_stdout(buf):
+            bench.run_gpu(_args(no_cpu=True), rank, 2, rank)
+    finally:
+        dist.destroy_process_group()
+    with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+        json.dump({"stdout": buf.getvalue(), "launches": len(launches)}, f)
+
+
+def test_two_rank_line_takes_the_max_over_ranks(tmp_path):
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_rank_main, args=(str(tmp_path), port), nprocs=2, join=True)
+    got = [json.load(open(tmp_path / f"rank{r}.json")) for r in range(2)]
+    assert not any(x.startswith("{") for x in got[1]["stdout"].splitlines())
+    lines = [x for x in got[0]["stdout"].splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    _check_line(line, 2, max(_rank_ms(0), _rank_ms(1)))
+    assert line["cpu_baseline"] is None  # rank 0 at N = 1 only
+    assert line["exposed_comm"] is not None
+    # both ranks launched the same sequence (every launch is a collective)
+    assert got[0]["launches"] == got[1]["launches"]
+
+
+def test_reference_arm_line():
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1",
+                           "--warmup", "3", "--cpu-seconds", "0.5"], cwd=ROOT,
+                          capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [x for x in proc.stdout.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"] == {"value": line["value"], "unit": line["unit"],
+                           "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert line["cpu_baseline"]["value"] == line["value"]
+    assert {"kind", "cores", "sample"} <= set(line["cpu_baseline"])
