@@ -16,7 +16,10 @@ reported):
   single_launch  the same, all blocks in one persistent launch
   unfused        torch: x @ gate, x @ up (cuBLAS), silu(g) * u, act @ down,
                  then NCCL allreduce, per block
-Prints one JSON line on rank 0.
+Prints one JSON line on rank 0, with the call roofline (the slower of the
+GEMMs at the measured bf16 peak and the allreduces' bus bytes over NVLink at
+770 GB/s per direction) and each fused arm's largest difference from the
+unfused arm's output, relative to that output's largest magnitude.
 """
 from __future__ import annotations
 
@@ -24,7 +27,7 @@ import argparse
 import json
 import os
 
-from .measure import ClockSampler, interleaved, mean
+from .measure import NVLINK_GBS, ClockSampler, interleaved, mean, peaks
 
 
 def main() -> int:
@@ -110,7 +113,7 @@ def main() -> int:
             for arm in arms:
                 arm()
         torch.cuda.synchronize()
-        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world, device=dev)
     us = [mean(v) * 1e3 for v in ms]
     for s in arms_modes:
         mb.events_status(bufs[s]["events_down"], stream)
@@ -120,12 +123,31 @@ def main() -> int:
     flops = 2.0 * t * h * (2 * i) * layers + 2.0 * t * i * h * layers
     out_bytes = t * h * 2
     link = 2.0 * (world - 1) / world * out_bytes * layers
+    peak, peak_src = peaks()
+    t_gemm = flops / (peak * 1e12) * 1e6
+    t_link = link / (NVLINK_GBS * 1e9) * 1e6
+    # Parity of the last fused calls against the unfused chain (collective:
+    # every rank runs it).
+    ref = unfused().float()
+    torch.cuda.synchronize()
+    scale = float(ref.abs().max())
+    rel_err = {("single_launch" if s else "two_launches"):
+               float((outs[s].float() - ref).abs().max()) / max(scale, 1e-30)
+               for s in arms_modes}
     if rank == 0:
         line = {"workload": f"C5 {layers} MLP blocks T{t} H{h} I{args.inter}/tp bf16",
                 "tp": world, "steps": args.steps, "data": "synthetic",
                 "us_per_call": dict(zip(names, us)),
                 "tflops_per_gpu": {n: flops / (u * 1e-6) / 1e12 for n, u in zip(names, us)},
                 "flops_per_pe": flops, "allreduce_bus_bytes_per_pe": link,
+                "roofline_call": {
+                    "gemm_us_at_peak": t_gemm, "link_us_at_770GBps": t_link,
+                    "roofline_us": max(t_gemm, t_link),
+                    "frac": {n: max(t_gemm, t_link) / u for n, u in zip(names, us)},
+                    "peak_tflops": peak, "peak_source": peak_src,
+                    "note": "slower of the GEMMs at the measured peak and the allreduces' "
+                            "bus bytes 2(tp-1)/tp x output per block over NVLink"},
+                "max_rel_err_vs_unfused": rel_err,
                 "l2": "flushed (256 MiB write) before every timed step",
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)

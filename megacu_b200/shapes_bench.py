@@ -186,7 +186,7 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         torch.cuda.synchronize()
         if args.graph:
             arms, graphed = as_graphs(arms, names, stream)
-        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world, device=dev)
     mb.events_status(events, stream)
     if solo_events is not None:
         mb.events_status(solo_events, stream)
@@ -281,7 +281,7 @@ def run_allgather(args, rank, world, local, team_cache):
             fused()
             unfused()
         torch.cuda.synchronize()
-        ms = interleaved(arms, args.steps, args.warmup, align, stream, world)
+        ms = interleaved(arms, args.steps, args.warmup, align, stream, world, device=dev)
     mb.events_status(events, stream)
     if solo_events is not None:
         mb.events_status(solo_events, stream)
