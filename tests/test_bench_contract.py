@@ -19,75 +19,31 @@ import json
 import os
 import subprocess
 import sys
-import types
 
 import pytest
+
+import host_fakes
+from host_fakes import rank_ms as _rank_ms
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 M, N, K_TOTAL = 4096, 8192, 8192
 STEPS, WARMUP, HEAT = 4, 3, 2
 
 
-def _rank_ms(rank):
-    return 1.0 + 0.5 * rank  # rank 1 is the slower one
+def _check_kernel(name, args, kwargs):
+    import torch
+    assert name == "gemm_allreduce"
+    a, b, out = args
+    assert a.dtype == b.dtype == out.dtype == torch.bfloat16
+    assert out.shape == (M, N) and a.shape[1] == b.shape[0] == kwargs["problem"].k
 
 
 def _install_fakes(rank, launches, patch):
-    """Replaces the CUDA-only calls bench.py makes; `patch(obj, name, value)`
-    sets an attribute (pytest's monkeypatch, or plain setattr in a child)."""
-    import torch
-
-    import megacu_b200 as mb
-
-    class Event:
-        def __init__(self, enable_timing=False):
-            pass
-
-        def record(self, stream=None):
-            pass
-
-        def elapsed_time(self, other):
-            return _rank_ms(rank)
-
-    class Team:
-        def __init__(self, rank, tp, device, heap, exchange, multicast_bytes=0):
-            self.multicast = False
-
-        def tensor(self, shape, dtype, multicast=False):
-            return torch.zeros(shape, dtype=dtype)
-
-        def barrier(self, stream):
-            pass
-
-        def close(self):
-            pass
-
-    def gemm_allreduce(a, b, out, *, workspace, events, problem, stream=None, device=0,
-                       team=None, **kw):
-        assert a.dtype == b.dtype == out.dtype == torch.bfloat16
-        assert out.shape == (M, N) and a.shape[1] == b.shape[0] == problem.k
-        launches.append(problem.k)
-
-    patch(torch.cuda, "Event", Event)
-    patch(torch.cuda, "set_device", lambda *a: None)
-    patch(torch.cuda, "synchronize", lambda *a: None)
-    patch(torch.cuda, "current_stream", lambda *a: None)
-    patch(torch.cuda, "current_device", lambda: 0)
-    patch(torch.Tensor, "pin_memory", lambda self: self)
-    patch(torch, "matmul", lambda a, b, out=None: out)
-    patch(mb, "Team", Team)
-    patch(mb, "gemm_allreduce", gemm_allreduce)
-    patch(mb, "events_status", lambda *a, **k: None)
+    host_fakes.install(rank, patch, launches, _check_kernel)
 
 
 def _bench_module():
-    src = open(os.path.join(ROOT, "bench.py")).read()
-    assert src.count('torch.device("cuda"') >= 1
-    mod = types.ModuleType("bench_on_host")
-    mod.__file__ = os.path.join(ROOT, "bench.py")
-    exec(compile(src.replace('torch.device("cuda"', 'torch.device("cpu"'), "bench.py", "exec"),
-         mod.__dict__)
-    return mod
+    return host_fakes.load_source("bench.py")
 
 
 def _args(cpu_seconds=0.2, no_cpu=False):
