@@ -34,8 +34,12 @@ gemm_ar_kernel.cuh), one step per flag store or acquired wait:
 A launch ends only after all its own steps and waits (kernel completion), and
 call e + 1 of a PE starts after its call e ended (stream order).
 
-Planted mistakes (one parity plane, no `done` wait, no `read_done` wait) must
-each be found: the check has teeth.
+The single-launch MLP chain's protocol (`ChainModel`) is checked the same
+way over consecutive launches.
+
+Planted mistakes (one parity plane, no `done` wait, no `read_done` wait; for
+the chain: arrive flags zeroed with the counters, no final wait, no wait for
+the previous block) must each be found: the check has teeth.
 """
 from __future__ import annotations
 
@@ -171,6 +175,9 @@ class Model:
                 return f"PE {p} ended call {e} with out tile {t} of call {mem[('out', p, t)]}"
         return None
 
+    def begin(self, p, e, mem):
+        """Host work on PE p between its launches, before call e."""
+
     def explore(self):
         """Depth-first over every interleaving; returns (states, first error)."""
         start = self.initial()
@@ -196,7 +203,12 @@ class Model:
                 return len(seen), f"stuck: {state}"
             for p, e_next, prog_next, effect in moves:
                 m = dict(mem)
-                err = (effect(m) if effect is not None else self.check_end(p, e_next - 1, m))
+                if effect is not None:
+                    err = effect(m)
+                else:  # the launch of call e_next - 1 ended
+                    err = self.check_end(p, e_next - 1, m)
+                    if err is None and e_next <= self.calls:
+                        self.begin(p, e_next, m)
                 if err:
                     return len(seen), err
                 nxt = list(pes)
@@ -206,6 +218,161 @@ class Model:
                     seen.add(s)
                     stack.append(s)
         return len(seen), None
+
+
+class ChainModel(Model):
+    """The single-launch MLP chain (megacu_b200/csrc/kernels/chain_kernel.cuh):
+    `layers` blocks in one launch per call, `rows` token row blocks, per row
+    block `gu` gate/up tiles (local) and `dn` down tiles, DN tile (r, j) owned
+    by PE (r * dn + j) mod tp. Data values are (call, block) pairs.
+
+      GU(l, r, c)  block 0, or x_ready[l-1][r] holds all dn counts: read the
+                   row block of x (block 0) or of block l-1's output, write
+                   act[r][c], count act_ready[l][r]
+      DN(l, r, j)  act_ready[l][r] holds all gu counts: read act[r][*], write
+                   this PE's slot[r][j] (one plane, shared by the blocks),
+                   store arrive[l][me][(r, j)] = call into the owner
+      X(l, r, j)   (owner) every PE's arrive equals the call: read every PE's
+                   slot[r][j], store the sum into block l's output on every
+                   PE, count x_ready[l][r] there
+    Block outputs alternate between two buffers, the last one `out`. A launch
+    ends after its steps and once x_ready[layers-1][r] holds all dn counts for
+    every r; then the host zeroes the counters (act_ready, x_ready; the arrive
+    flags are epoch-tagged and kept) and writes the next call's x.
+    """
+
+    def __init__(self, tp, layers, rows, gu, dn, calls, zero_arrive=False, final_wait=True,
+                 wait_x=True):
+        super().__init__("chain", tp, rows * dn, calls)
+        self.layers, self.rows, self.gu, self.dn = layers, rows, gu, dn
+        self.zero_arrive, self.final_wait, self.wait_x = zero_arrive, final_wait, wait_x
+
+    def owner(self, r, j):
+        return (r * self.dn + j) % self.tp
+
+    def buf(self, l):
+        return "out" if (self.layers - 1 - l) % 2 == 0 else "work"
+
+    def initial(self):
+        mem = {}
+        L, R = self.layers, self.rows
+        for p in range(self.tp):
+            for r in range(R):
+                mem[("x", p, r)] = (1, -1)
+                for c in range(self.gu):
+                    mem[("act", p, r, c)] = (0, 0)
+                for j in range(self.dn):
+                    mem[("slot", p, r, j)] = (0, 0)
+                    for b in ("out", "work"):
+                        mem[(b, p, r, j)] = (0, 0)
+                for l in range(L):
+                    mem[("act_ready", p, l, r)] = 0
+                    mem[("x_ready", p, l, r)] = 0
+                    for q in range(self.tp):
+                        for j in range(self.dn):
+                            mem[("arrive", p, l, q, r, j)] = 0
+        return (tuple((1, frozenset()) for _ in range(self.tp)), tuple(sorted(mem.items())))
+
+    def steps(self, p, e, prog, mem):
+        L, R, tp = self.layers, self.rows, self.tp
+        out = []
+        for l, r in itertools.product(range(L), range(R)):
+            for c in range(self.gu):
+                if ("GU", l, r, c) in prog:
+                    continue
+
+                def gu(m, l=l, r=r, c=c):
+                    for j in range(self.dn):
+                        src = m[("x", p, r)] if l == 0 else m[(self.buf(l - 1), p, r, j)]
+                        want = (e, -1) if l == 0 else (e, l - 1)
+                        if src != want:
+                            return f"PE {p} call {e} GU{l} read input {src}, want {want}"
+                    m[("act", p, r, c)] = (e, l)
+                    m[("act_ready", p, l, r)] += 1
+                ready = (l == 0 or not self.wait_x
+                         or mem[("x_ready", p, l - 1, r)] == self.dn)
+                out.append((("GU", l, r, c), ready, gu))
+            for j in range(self.dn):
+                if ("DN", l, r, j) not in prog:
+                    def dn(m, l=l, r=r, j=j):
+                        for c in range(self.gu):
+                            if m[("act", p, r, c)] != (e, l):
+                                return f"PE {p} call {e} DN{l} read act {m[('act', p, r, c)]}"
+                        m[("slot", p, r, j)] = (e, l)
+                        m[("arrive", self.owner(r, j), l, p, r, j)] = e
+                    out.append((("DN", l, r, j), mem[("act_ready", p, l, r)] == self.gu, dn))
+                if self.owner(r, j) != p or ("X", l, r, j) in prog:
+                    continue
+
+                def x(m, l=l, r=r, j=j):
+                    for q in range(tp):
+                        if m[("slot", q, r, j)] != (e, l):
+                            return (f"PE {p} call {e} X{l} read PE {q}'s slot holding "
+                                    f"{m[('slot', q, r, j)]}")
+                    for y in range(tp):
+                        m[(self.buf(l), y, r, j)] = (e, l)
+                        m[("x_ready", y, l, r)] += 1
+                ready = all(mem[("arrive", p, l, q, r, j)] == e for q in range(tp))
+                out.append((("X", l, r, j), ready, x))
+        return out
+
+    def can_end(self, p, e, prog, mem):
+        L, R = self.layers, self.rows
+        for l, r in itertools.product(range(L), range(R)):
+            if any(("GU", l, r, c) not in prog for c in range(self.gu)):
+                return False
+            for j in range(self.dn):
+                if ("DN", l, r, j) not in prog:
+                    return False
+                if self.owner(r, j) == p and ("X", l, r, j) not in prog:
+                    return False
+        return not self.final_wait or all(
+            mem[("x_ready", p, L - 1, r)] == self.dn for r in range(R))
+
+    def check_end(self, p, e, mem):
+        for r, j in itertools.product(range(self.rows), range(self.dn)):
+            if mem[("out", p, r, j)] != (e, self.layers - 1):
+                return f"PE {p} ended call {e} with out {mem[('out', p, r, j)]}"
+        return None
+
+    def begin(self, p, e, mem):
+        for key in list(mem):
+            if key[0] in ("act_ready", "x_ready") and key[1] == p:
+                mem[key] = 0
+            if self.zero_arrive and key[0] == "arrive" and key[1] == p:
+                mem[key] = 0
+        for r in range(self.rows):
+            mem[("x", p, r)] = (e, -1)
+
+
+CHAIN_CASES = [
+    # tp, layers, rows, gu, dn, calls
+    (2, 3, 1, 1, 2, 2),   # three blocks: the output buffers are reused (l, l + 2)
+    (2, 2, 2, 1, 1, 3),   # two row blocks, one DN tile each, owned by different PEs
+    (2, 2, 2, 1, 2, 3),   # two row blocks of two DN tiles, three calls
+    (3, 3, 1, 1, 3, 2),   # three PEs, each owning one DN tile
+    (3, 2, 1, 1, 3, 3),
+]
+
+
+@pytest.mark.parametrize("tp,layers,rows,gu,dn,calls", CHAIN_CASES)
+def test_chain_protocol_has_no_race_or_deadlock(tp, layers, rows, gu, dn, calls):
+    states, err = ChainModel(tp, layers, rows, gu, dn, calls).explore()
+    assert err is None, err
+    assert states > 10
+
+
+def test_chain_planted_mistakes_are_found():
+    """Zeroing the arrive flags with the counters loses a fast peer's flag of
+    the next call; ending before the last block's counts ends with an
+    incomplete out; a GU tile that does not wait for the previous block reads
+    an old input."""
+    _, err = ChainModel(2, 1, 1, 1, 2, 2, zero_arrive=True).explore()
+    assert err is not None and "stuck" in err, err
+    _, err = ChainModel(2, 1, 1, 1, 2, 2, final_wait=False).explore()
+    assert err is not None and "ended call" in err, err
+    _, err = ChainModel(2, 2, 1, 1, 1, 1, wait_x=False).explore()
+    assert err is not None and "GU1 read input" in err, err
 
 
 CASES = [
