@@ -121,5 +121,6 @@ def same_process_team(devices, heap=1 << 30):
         mb.check(lib.megacu_b200_team_info(raw[pe], None, None, ctypes.byref(base),
                                            ctypes.byref(size)))
         t.heap_base, t.heap_bytes = base.value, size.value
+        t.multicast, t.multicast_error = False, None  # as a Team built without a region
         teams.append(t)
     return teams
