@@ -249,3 +249,31 @@ def test_tools_parse_their_arguments(argv):
     proc = subprocess.run([sys.executable, *argv], cwd=ROOT, capture_output=True, text=True,
                           timeout=300)
     assert proc.returncode == 0 and "usage" in proc.stdout.lower(), proc.stderr[-2000:]
+
+
+def test_same_process_team_sets_what_team_init_sets():
+    """tests/gpu_util.same_process_team builds Team objects without __init__
+    (one process, several GPUs): it must set every attribute __init__ sets,
+    or the multi-GPU tests would fail only on a B200."""
+    import ast
+
+    def assigned(fn, name):
+        out = set()
+        for node in ast.walk(fn):
+            targets = node.targets if isinstance(node, ast.Assign) else []
+            for t in targets:
+                elts = t.elts if isinstance(t, ast.Tuple) else [t]
+                for x in elts:
+                    if (isinstance(x, ast.Attribute) and isinstance(x.value, ast.Name)
+                            and x.value.id == name):
+                        out.add(x.attr)
+        return out
+
+    api = ast.parse(open(os.path.join(ROOT, "megacu_b200", "api.py")).read())
+    team = next(n for n in api.body if isinstance(n, ast.ClassDef) and n.name == "Team")
+    init = next(n for n in team.body if isinstance(n, ast.FunctionDef) and n.name == "__init__")
+    util = ast.parse(open(os.path.join(ROOT, "tests", "gpu_util.py")).read())
+    spt = next(n for n in util.body
+               if isinstance(n, ast.FunctionDef) and n.name == "same_process_team")
+    want = assigned(init, "self") - {"_finalizer"}  # close() tolerates its absence
+    assert want and want <= assigned(spt, "t"), want - assigned(spt, "t")
