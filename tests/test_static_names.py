@@ -126,9 +126,6 @@ def test_calls_fit_signatures(rel):
     assert bad_calls(os.path.join(ROOT, rel)) == []
 
 
-_NO_DEFAULT = object()
-
-
 def _ast_signature(fn):
     """inspect.Signature of an ast.FunctionDef (defaults as placeholders)."""
     import inspect
