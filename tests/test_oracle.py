@@ -271,3 +271,27 @@ def test_chain_event_oracle_is_consistent(layers, n_pes, tokens, hidden, inter):
     if n_pes > 1:
         assert int(c[:, 1].sum()) == layers * dn * quarters    # every (tile, quarter) reduced once
         assert (c[:, 3] == c[:, 1] * n_pes).all() and (c[:, 5] == n_pes).all()
+
+
+@pytest.mark.parametrize("n_pes,mode,one_shot", [(2, 0, True), (3, 0, False), (4, 1, False)])
+def test_bf16_graph_does_not_depend_on_k_or_data(n_pes, mode, one_shot):
+    """The event words and counters of a call depend on m, n, the tiles and
+    the PEs only: the full-size multi-GPU test computes them with k = 8."""
+    m, n, tile_n = 512, 384, 128
+    rng = np.random.default_rng(5)
+    graphs = []
+    for k, zero in ((8, True), (64, False)):
+        a = [np.zeros((m, k), np.float32) if zero else
+             rng.standard_normal((m, k)).astype(np.float32) for _ in range(n_pes)]
+        b = [np.zeros((k, n), np.float32) if zero else
+             rng.standard_normal((k, n)).astype(np.float32) for _ in range(n_pes)]
+        tiles = -(-m // 128) * -(-n // tile_n)
+        ev0 = [np.zeros(oracle_lib.event_tensor_words(n_pes, tiles), np.uint32)
+               for _ in range(n_pes)]
+        kw = dict(m=m, n=n, k=k, tile_n=tile_n, mode=mode, one_shot=one_shot)
+        r1 = oracle_lib.bf16_call(a, b, epoch=1, events=ev0, **kw)
+        r2 = oracle_lib.bf16_call(a, b, epoch=2, events=r1["events"], **kw)
+        graphs.append(([e.copy() for e in r2["events"]], r1["counters"] + r2["counters"]))
+    (ev_a, c_a), (ev_b, c_b) = graphs
+    assert all(np.array_equal(x, y) for x, y in zip(ev_a, ev_b))
+    assert np.array_equal(c_a, c_b)
