@@ -3,13 +3,8 @@ epoch comes from the launch counter in `events` (no per-call memset, no host
 barrier), so each replay is a complete call. One PE on cuda:0; the output of
 every replay must equal the directly launched call's bit for bit, and the
 completion counters must count every replay.
-
-These tests run only with MEGACU_B200_UNVERIFIED=1 until graph replay has
-had its first run on a B200.
 """
 from __future__ import annotations
-
-import os
 
 import pytest
 import torch
@@ -17,12 +12,7 @@ import torch
 import megacu_b200 as mb
 from gpu_util import inputs
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
-                       reason="CUDA graph replay awaiting its first B200 run "
-                              "(set MEGACU_B200_UNVERIFIED=1)"),
-]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("m,n,k,pairs", [(512, 1024, 256, mb.CTA_PAIRS_AUTO),

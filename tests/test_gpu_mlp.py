@@ -163,8 +163,7 @@ def _check_chain_events(prob, events_list, n_pes):
         assert mb.events_counters(ev) == want, f"PE {pe}: counters"
 
 
-@_UNVERIFIED
-@pytest.mark.parametrize("n_pes", [1, 2])
+@pytest.mark.parametrize("n_pes", [1, pytest.param(2, marks=_UNVERIFIED)])
 def test_single_launch_chain_events_match_oracle(n_pes):
     if gpu_count() < n_pes:
         pytest.skip("needs two GPUs")
