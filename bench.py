@@ -1,4 +1,4 @@
-"""Benchmark of the fused bf16 GEMM + allreduce megakernel.
+"""Benchmark of the fused bf16 GEMM + allreduce megakernel (benchmark config 2).
 
 Workload: row-parallel GEMM + allreduce, M = 4096, N = 8192, K = 8192 split
 over tp = N GPUs (each PE: A [4096, 8192/tp], B [8192/tp, 8192], bf16 N(0,

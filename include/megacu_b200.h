@@ -232,7 +232,7 @@ megacu_status megacu_cuda_allgather_gemm_bf16(
     megacu_driver_view driver, const void *a_shard, const void *b, void *gathered,
     void *out, void *events, megacu_gemm_ar_problem_v2 problem);
 
-/* ---- tensor-parallel MLP blocks (new, no counterpart in
+/* ---- tensor-parallel MLP blocks (benchmark config 5; new, no counterpart in
  *      megacu) -------------------------------------------------------------- */
 
 /*

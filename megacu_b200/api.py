@@ -392,7 +392,7 @@ def allgather_gemm(a_shard, b, gathered, out, *, events, problem: Problem, strea
                                                  problem.to_c(trace_ptr, cap)))
 
 
-# ---- tensor-parallel MLP blocks ----------------------------------
+# ---- tensor-parallel MLP blocks (benchmark config 5) ----------------------------------
 
 def swiglu_events_bytes(problem: Problem) -> int:
     out = ctypes.c_int64()

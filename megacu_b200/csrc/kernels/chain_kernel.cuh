@@ -1,4 +1,4 @@
-// One persistent launch of a chain of tensor-parallel MLP blocks (BASELINE
+// One persistent launch of a chain of tensor-parallel MLP blocks (benchmark
 // config 5; no counterpart in megacu):
 //
 //   for l = 0 .. layers-1:   act     = silu(x_l @ gate_l) * (x_l @ up_l)    (local)

@@ -1,4 +1,4 @@
-// Tensor-parallel MLP blocks (no counterpart in megacu):
+// Tensor-parallel MLP blocks (benchmark config 5, no counterpart in megacu):
 //   act   = silu(x @ w_gate) * (x @ w_up)      column-parallel, local
 //   x_out = allreduce_pe(act @ w_down)          row-parallel, fused exchange
 // megacu_cuda_gemm_swiglu_bf16 is the first line as one persistent launch of

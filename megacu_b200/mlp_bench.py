@@ -1,4 +1,4 @@
-"""Timing of the tensor-parallel MLP chain.
+"""Timing of the tensor-parallel MLP chain (benchmark config 5).
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \\
         --master-addr 127.0.0.1 --master-port 29600 -m megacu_b200.mlp_bench

@@ -1,4 +1,4 @@
-"""Timing of the fused megakernel at BASELINE configs 3 and 4, and of the
+"""Timing of the fused megakernel at benchmark configs 3 and 4, and of the
 all-gather + GEMM (bench.py times config 2, mlp_bench config 5).
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \\

@@ -61,7 +61,7 @@ void oracle_locate(int32_t m_tiles, int32_t n_tiles, int32_t n_pes, int32_t mode
                    int32_t group_m, int32_t r, int32_t out[4]);
 
 /*
- * Tensor-parallel MLP blocks (a B200 addition with no
+ * Tensor-parallel MLP blocks (benchmark config 5; a B200 addition with no
  * counterpart in megacu, so its semantics are pinned by this restatement):
  * for l = 0 .. layers-1, on every PE p,
  *   act_p = bf16(silu(x_l @ wg[l][p]) * (x_l @ wu[l][p]))   (fp32 products and

@@ -1,4 +1,4 @@
-"""Tensor-parallel MLP blocks through the C ABI against the
+"""Tensor-parallel MLP blocks (benchmark config 5) through the C ABI against the
 CPU oracle: the SwiGLU gate/up projection alone, and chains of blocks on one
 PE and on a two-GPU team (one process, peer exchange)."""
 from __future__ import annotations

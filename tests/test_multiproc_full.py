@@ -1,4 +1,4 @@
-"""Full-size multi-GPU parity (BASELINE configs 2 and 3 at their sizes, K
+"""Full-size multi-GPU parity (benchmark configs 2 and 3 at their sizes, K
 split over the ranks) under torchrun, one rank per GPU: tests/mp_full_worker.py.
 
 These tests run only with MEGACU_B200_UNVERIFIED=1 until the worker has had

@@ -1,7 +1,7 @@
 """The CPU oracle against the reference's golden vectors and its own invariants.
 
 Pins: the reference's known-answer tests (tests/golden/kat_gemm_allreduce.json,
-transcribed from its test sources by tests/golden/make_golden.py) and BASELINE
+transcribed from its test sources by tests/golden/make_golden.py) and benchmark
 config 1 (512^3 fp32, 128x128 tiles = 16 tile tasks, 2 logical ranks).
 """
 from __future__ import annotations
@@ -48,7 +48,7 @@ def test_kat_two_pe(kat):
 
 
 def test_config1_host_plumbing():
-    """512^3 fp32, N(0,1) seed 0, 16 tile tasks, 2 ranks x K/2."""
+    """benchmark config 1: 512^3 fp32, N(0,1) seed 0, 16 tile tasks, 2 ranks x K/2."""
     rng = np.random.default_rng(0)
     m = n = k = 512
     a = rng.standard_normal((m, k), dtype=np.float32)
