@@ -30,6 +30,8 @@ import os
 def _summary(tr, np):
     t0 = tr["t0"].astype(np.int64)
     t1 = tr["t1"].astype(np.int64)
+    if t0.size == 0:
+        return {"records": 0}  # the traced call recorded nothing
     base = t0.min()
 
     def us(x):
@@ -85,11 +87,12 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"))
+        dist.init_process_group("nccl", device_id=dev)
     gen = torch.Generator().manual_seed(100 + rank)
     stream = torch.cuda.current_stream()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     if args.allgather:
         m, n, k = args.m, args.n, args.k_total
         prob = mb.Problem(m, n, k, mode=mb.MODE_ALLGATHER, timeout_ns=20_000_000_000)
@@ -100,18 +103,18 @@ def main() -> int:
         use_mc = False
         shard = team.tensor((m // world, k), torch.bfloat16)
         shard.copy_((torch.randn(m // world, k, generator=gen) * 0.02).to(torch.bfloat16))
-        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
         events = team.tensor((ev_bytes // 4,), torch.int32)
-        gathered = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
-        out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        gathered = torch.empty((m, k), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
 
         def call(trace=None):
             mb.allgather_gemm(shard, b, gathered, out, events=events, problem=prob, stream=stream,
                               device=local, team=team if world > 1 else None, trace=trace)
     else:
         m, n, k = args.m, args.n, args.k_total // world
-        a = (torch.randn(m, k, generator=gen) * 0.02).to(torch.bfloat16).cuda()
-        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).cuda()
+        a = (torch.randn(m, k, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+        b = (torch.randn(k, n, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
         prob = mb.Problem(m, n, k, timeout_ns=20_000_000_000)
         plan = mb.plan(prob, world)
         ws_bytes, ev_bytes = mb.workspace_bytes(prob, world), mb.events_bytes(prob, world)
@@ -145,7 +148,7 @@ def main() -> int:
     # records: GEMM tiles, reduce sub-tasks (16 per tile at most) or copy
     # chunks (up to 128 per tile row and shard), and a few per worker
     trace = torch.zeros((plan.tiles * 64 + plan.m_tiles * 128) * 4, dtype=torch.int64,
-                        device="cuda")
+                        device=dev)
     traced_us = timed(trace)
     mb.events_status(events, stream)
     rec = trace.view(-1, 4).cpu().numpy().astype(np.uint64)

@@ -29,3 +29,9 @@ def test_summary_reads_copy_chunks_by_shard_distance():
     assert s["copy_chunks"] == 3 and s["copy_first_start_us"] == 1.0 and s["copy_end_us"] == 9.0
     assert s["copy_end_by_hops_us"] == {1: 4.0, 2: 9.0}
     assert s["copy_chunk_p50_us"] == 2.0
+
+
+def test_summary_of_an_empty_trace():
+    empty = np.zeros(0, np.uint64)
+    tr = {"kind": empty.astype(np.int64), "sub": empty.astype(np.int64), "t0": empty, "t1": empty}
+    assert timeline._summary(tr, np) == {"records": 0}

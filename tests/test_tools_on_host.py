@@ -2,7 +2,9 @@
 host_fakes.py): `shapes_bench` (config 4 decode shapes, both exchange
 choices, CUDA-graph arms) and `mlp_bench` (config 5, small sizes) parse their
 options, size their buffers within the team heap, time every arm, and print
-one JSON line on rank 0 whose time is the max over ranks."""
+one JSON line on rank 0 whose time is the max over ranks; `timeline` (fused
+call and all-gather) prints on rank 0 one line per PE with that PE's own
+times."""
 from __future__ import annotations
 
 import contextlib
@@ -16,17 +18,23 @@ import pytest
 
 import host_fakes
 
+# case name -> (tool module, its options)
 TOOLS = {
-    "shapes_bench": ["--config", "4", "--m", "16,64", "--steps", "2", "--heat-calls", "1"],
-    "shapes_bench_two_shot_graph": ["--config", "4", "--m", "64", "--algo", "two", "--graph",
-                                    "--steps", "2", "--heat-calls", "1"],
-    "mlp_bench": ["--tokens", "256", "--hidden", "512", "--inter", "1024", "--layers", "2",
-                  "--steps", "2", "--heat-calls", "1"],
+    "shapes_bench": ("shapes_bench", ["--config", "4", "--m", "16,64", "--steps", "2",
+                                      "--heat-calls", "1"]),
+    "shapes_bench_two_shot_graph": ("shapes_bench", ["--config", "4", "--m", "64", "--algo",
+                                                     "two", "--graph", "--steps", "2",
+                                                     "--heat-calls", "1"]),
+    "mlp_bench": ("mlp_bench", ["--tokens", "256", "--hidden", "512", "--inter", "1024",
+                                "--layers", "2", "--steps", "2", "--heat-calls", "1"]),
+    "timeline": ("timeline", ["--m", "512", "--n", "1024", "--k-total", "512", "--calls", "2"]),
+    "timeline_allgather": ("timeline", ["--m", "512", "--n", "1024", "--k-total", "512",
+                                        "--calls", "2", "--allgather"]),
 }
 
 
 def _run_tool(name, argv):
-    module = name.split("_two_shot")[0]
+    module = TOOLS[name][0]
     mod = host_fakes.load_source(f"megacu_b200/{module}.py", package="megacu_b200")
     old = sys.argv
     sys.argv = [module, *argv]
@@ -41,7 +49,14 @@ def _run_tool(name, argv):
 
 def _check(name, lines, tp):
     ms = host_fakes.rank_ms(tp - 1)  # the slowest rank's step time
-    if name.startswith("shapes_bench"):
+    if name.startswith("timeline"):
+        assert [x["pe"] for x in lines] == list(range(tp))
+        for pe, x in enumerate(lines):
+            assert x["tp"] == tp
+            assert x["call_us_median"] == pytest.approx(host_fakes.rank_ms(pe) * 1e3)
+            assert x["exchange"] == ("all-gather copies" if name.endswith("allgather") else
+                                     "peer" if tp > 1 else "none")
+    elif name.startswith("shapes_bench"):
         assert [x["m"] for x in lines] == ([16, 64] if name == "shapes_bench" else [64])
         for x in lines:
             assert x["tp"] == tp and x["n"] == 8192 and x["k_per_pe"] == 28672 // tp
@@ -67,7 +82,7 @@ def test_tool_on_one_rank(name, monkeypatch):
     monkeypatch.setenv("LOCAL_RANK", "0")
     launches = []
     host_fakes.install(0, monkeypatch.setattr, launches)
-    lines = _run_tool(name, TOOLS[name])
+    lines = _run_tool(name, TOOLS[name][1])
     _check(name, lines, 1)
     assert launches
 
@@ -76,7 +91,7 @@ def _rank_main(rank, out_dir, ports):
     launches = []
     host_fakes.install(rank, setattr, launches)
     got = {}
-    for (name, argv), port in zip(TOOLS.items(), ports):
+    for (name, (_, argv)), port in zip(TOOLS.items(), ports):
         os.environ.update(RANK=str(rank), WORLD_SIZE="2", LOCAL_RANK=str(rank),
                           MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         before = len(launches)
