@@ -151,3 +151,23 @@ def test_reference_arm_line():
                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert line["cpu_baseline"]["value"] == line["value"]
     assert {"kind", "cores", "sample"} <= set(line["cpu_baseline"])
+
+
+def test_reference_arm_under_torchrun_prints_once(tmp_path):
+    """The driver launches the reference arm like the GPU arm (torchrun for
+    N > 1): rank 0 alone works and prints; every rank exits 0."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    proc = subprocess.run(
+        ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run",
+         "--nnodes=1", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+         "--master-port", str(port), "bench.py", "--impl", "reference", "--gpus", "2",
+         "--steps", "1", "--warmup", "3", "--cpu-seconds", "0.5"],
+        cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [x for x in proc.stdout.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2 and line["config"]["tp"] == 2
