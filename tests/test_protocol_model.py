@@ -23,7 +23,10 @@ gemm_ar_kernel.cuh), one step per flag store or acquired wait:
     slot of tile t; final step F(t) after every source: store the sum into
     this PE's out (one-shot, reduce-scatter) or into every PE's out
     (two-shot);
-  * two-shot completion: once a PE's reduce steps are all done it stores
+  * in-switch two-shot: the owner's reduce is one step (one
+    `multimem.ld_reduce` over every PE's slot, once every flag equals e) and
+    its final step stores into every PE's out through the multicast mapping;
+  * two-shot completion (both kinds): once a PE's reduce steps are all done it stores
     `done` (source me) = e into every PE; a launch ends only after all tp
     `done` flags equal e;
   * all-gather: at launch start the PE's A shard (written by the host before
@@ -48,6 +51,7 @@ import itertools
 import pytest
 
 ONE_SHOT, TWO_SHOT, REDUCE_SCATTER, ALL_GATHER = "one_shot", "two_shot", "reduce_scatter", "gather"
+IN_SWITCH = "in_switch"  # two-shot whose owner reads and stores through the NVSwitch
 
 
 class Model:
@@ -59,7 +63,7 @@ class Model:
     def reducers(self, t):
         if self.mode == ONE_SHOT:
             return range(self.tp)
-        if self.mode == TWO_SHOT:
+        if self.mode in (TWO_SHOT, IN_SWITCH):
             return [t % self.tp]
         return [t * self.tp // self.tiles]  # the PE whose output rows hold tile t
 
@@ -67,11 +71,11 @@ class Model:
         return [t for t in range(self.tiles) if p in self.reducers(t)]
 
     def out_targets(self, p):
-        return range(self.tp) if self.mode == TWO_SHOT else [p]
+        return range(self.tp) if self.mode in (TWO_SHOT, IN_SWITCH) else [p]
 
     def out_tiles(self, p):
         """Output tiles PE p's out holds at the end of a call."""
-        if self.mode in (ONE_SHOT, TWO_SHOT):
+        if self.mode in (ONE_SHOT, TWO_SHOT, IN_SWITCH):
             return range(self.tiles)
         return self.owned(p)
 
@@ -127,6 +131,22 @@ class Model:
                         m[("arrive", r, pl, p, t)] = e
                 out.append((("W", t), True, write))
         for t in self.owned(p):
+            if self.mode == IN_SWITCH:
+                # one multimem.ld_reduce over every PE's slot, after every flag
+                if ("R", t) not in prog:
+                    def reduce_all(m, t=t):
+                        for q in range(tp):
+                            if m[("slot", q, pl, t)] != e:
+                                return (f"PE {p} call {e} reduced PE {q}'s slot of tile {t} "
+                                        f"holding call {m[('slot', q, pl, t)]}")
+                    ready = all(mem[("arrive", p, pl, q, t)] == e for q in range(tp))
+                    out.append((("R", t), ready, reduce_all))
+                if ("F", t) not in prog:
+                    def store_all(m, t=t):
+                        for x in range(tp):
+                            m[("out", x, t)] = e
+                    out.append((("F", t), ("R", t) in prog, store_all))
+                continue
             for q in range(tp):
                 if ("R", q, t) in prog:
                     continue
@@ -142,7 +162,7 @@ class Model:
                         m[("out", x, t)] = e
                 ready = all(("R", q, t) in prog for q in range(tp))
                 out.append((("F", t), ready, final))
-        if self.mode == TWO_SHOT and "D" not in prog:
+        if self.mode in (TWO_SHOT, IN_SWITCH) and "D" not in prog:
             def done(m):
                 for x in range(tp):
                     m[("done", x, pl, p)] = e
@@ -160,7 +180,7 @@ class Model:
             return False
         if any(("F", t) not in prog for t in self.owned(p)):
             return False
-        if self.mode == TWO_SHOT:
+        if self.mode in (TWO_SHOT, IN_SWITCH):
             if "D" not in prog:
                 return False
             if self.wait_done and any(mem[("done", p, pl, q)] != e for q in range(self.tp)):
@@ -380,6 +400,8 @@ CASES = [
     (ONE_SHOT, 3, 1, 3),
     (TWO_SHOT, 2, 2, 3),
     (TWO_SHOT, 3, 2, 3),   # one PE owns no tile: only the done flags hold it back
+    (IN_SWITCH, 2, 2, 3),
+    (IN_SWITCH, 3, 2, 3),
     (REDUCE_SCATTER, 2, 2, 3),
     (REDUCE_SCATTER, 3, 3, 3),
     (ALL_GATHER, 3, 1, 4),
@@ -411,10 +433,11 @@ def test_two_shot_done_wait_alone_protects_the_slots():
     assert err is not None, err
 
 
-def test_two_shot_without_done_wait_races():
+@pytest.mark.parametrize("mode", [TWO_SHOT, IN_SWITCH])
+def test_two_shot_without_done_wait_races(mode):
     """Without the done wait a PE ends its call before every owner stored its
     tiles into its out."""
-    _, err = Model(TWO_SHOT, 2, 2, 2, wait_done=False).explore()
+    _, err = Model(mode, 2, 2, 2, wait_done=False).explore()
     assert err is not None and "ended call" in err, err
 
 
