@@ -164,3 +164,55 @@ def test_team_context_manager_closes_once():
         assert same is t
     t.close()
     assert t.handle is None
+
+
+def _c_declarations():
+    """name -> (return kind, [parameter kinds]) of every function declared in
+    include/megacu_b200.h."""
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    src = open(os.path.join(root, "include", "megacu_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    kinds = {
+        "megacu_driver_view": "driver", "megacu_gemm_ar_problem": "problem",
+        "megacu_gemm_ar_problem_v2": "problem_v2", "megacu_mlp_chain_problem": "chain_problem",
+        "int32_t": "i32", "int64_t": "i64", "const char *": "str", "void **": "ptr*",
+        "const void *const *": "ptr*", "int32_t *": "i32*", "int64_t *": "i64*",
+        "uint64_t *": "u64*",
+    }
+    out = {}
+    decl = r"\b(megacu_status|int|const char \*)\s*(megacu_\w+)\s*\(([^;{]*?)\)\s*;"
+    for ret, name, params in re.findall(decl, src, re.S):
+        got = []
+        if params.strip() not in ("", "void"):
+            for p in params.split(","):
+                p = " ".join(p.split())
+                array = re.match(r"(.*?)\s*\w+\[\d+\]$", p)
+                t = array.group(1) + " *" if array else re.sub(r"\s*\b\w+$", "", p)
+                t = t.replace("const ", "") if t not in kinds else t
+                got.append(kinds.get(t, "ptr" if t.endswith("*") else t))
+        out[name] = ({"megacu_status": "status", "int": "int"}.get(ret, "str"), got)
+    return out
+
+
+def test_ctypes_prototypes_match_the_c_header():
+    """Every declared function has a ctypes prototype with the same return
+    type and the same parameter count and kinds (a mismatch would pass
+    garbage to the library only on a GPU call)."""
+    import ctypes
+
+    from megacu_b200 import _capi
+    P = ctypes.POINTER
+    kind_of = {_capi.DriverView: "driver", _capi.GemmArProblem: "problem",
+               _capi.GemmArProblemV2: "problem_v2", _capi.MlpChainProblem: "chain_problem",
+               ctypes.c_int32: "i32", ctypes.c_int64: "i64", ctypes.c_char_p: "str",
+               ctypes.c_void_p: "ptr", P(ctypes.c_void_p): "ptr*", P(ctypes.c_int32): "i32*",
+               P(ctypes.c_int64): "i64*", P(ctypes.c_uint64): "u64*"}
+    decls = _c_declarations()
+    assert len(decls) >= 40
+    assert set(decls) == set(_capi._PROTOTYPES), set(decls) ^ set(_capi._PROTOTYPES)
+    for name, (ret, params) in decls.items():
+        res, args = _capi._PROTOTYPES[name]
+        want = {_capi.Status: "status", ctypes.c_int: "int", ctypes.c_char_p: "str"}[res]
+        assert want == ret, name
+        assert [kind_of.get(a, repr(a)) for a in args] == params, name
