@@ -216,3 +216,38 @@ def test_ctypes_prototypes_match_the_c_header():
         want = {_capi.Status: "status", ctypes.c_int: "int", ctypes.c_char_p: "str"}[res]
         assert want == ret, name
         assert [kind_of.get(a, repr(a)) for a in args] == params, name
+
+
+def test_ctypes_struct_layouts_match_the_c_header(tmp_path):
+    """Size and every field offset of the C ABI's structs, as the C compiler
+    lays them out from include/megacu_b200.h, equal the ctypes mirrors'."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    from megacu_b200 import build
+    structs = {"megacu_status": _capi.Status, "megacu_launch_view": _capi.LaunchView,
+               "megacu_team_view": _capi.TeamView, "megacu_driver_view": _capi.DriverView,
+               "megacu_gemm_ar_problem": _capi.GemmArProblem,
+               "megacu_gemm_ar_problem_v2": _capi.GemmArProblemV2,
+               "megacu_mlp_chain_problem": _capi.MlpChainProblem}
+    lines, want = [], []
+    for c_name, py in structs.items():
+        lines.append(f'  printf("%zu\\n", sizeof({c_name}));')
+        want.append(ctypes.sizeof(py))
+        for field, _ in py._fields_:
+            lines.append(f'  printf("%zu\\n", offsetof({c_name}, {field}));')
+            want.append(getattr(py, field).offset)
+    src = ("#include <stddef.h>\n#include <stdio.h>\n#include <megacu_b200.h>\n"
+           "int main(void) {\n" + "\n".join(lines) + "\n  return 0;\n}\n")
+    (tmp_path / "layout.c").write_text(src)
+    exe = str(tmp_path / "layout")
+    proc = subprocess.run([cc, "-std=c99", "-Wall", "-Werror",
+                           "-I" + os.path.join(build.ROOT, "include"),
+                           str(tmp_path / "layout.c"), "-o", exe], capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr
+    got = [int(x) for x in subprocess.run([exe], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert got == want
