@@ -17,7 +17,9 @@ FILES = ["bench.py", "__graft_entry__.py", "megacu_b200/shapes_bench.py",
 def undefined_globals(path):
     src = open(path).read()
     top = symtable.symtable(src, path, "exec")
-    defined = set(top.get_identifiers())
+    # plus the module attributes Python defines for every module
+    defined = set(top.get_identifiers()) | {"__file__", "__name__", "__doc__", "__spec__",
+                                             "__package__", "__loader__"}
     missing = []
 
     def walk(table, where):
