@@ -3,14 +3,12 @@ A bit for bit, the output within the bf16 tolerance, the event tensor words
 and the completion counters exactly, over two consecutive calls (epochs 1
 and 2). One PE on cuda:0; two PEs on two GPUs driven by one process.
 
-The one-PE cases have passed on a B200 (bounds-checked and regular
-library); the two-PE case runs only with MEGACU_B200_UNVERIFIED=1 until it
-has too. The host side (plan, sizes, validation) and the oracle are covered
+Every case has passed on B200s with the bounds-checked and the regular
+library. The host side (plan, sizes, validation) and the oracle are covered
 without a GPU in test_allgather.py.
 """
 from __future__ import annotations
 
-import os
 
 import numpy as np
 import pytest
@@ -22,9 +20,6 @@ from conftest import gpu_count
 from gpu_util import REL_TOL, f32, rel_error, same_process_team, seeded_bf16
 
 pytestmark = pytest.mark.gpu
-_UNVERIFIED = pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
-                                 reason="two-PE all-gather awaiting its first B200 run "
-                                        "(set MEGACU_B200_UNVERIFIED=1)")
 
 
 def _inputs(seed, n_pes, m, n, k):
@@ -78,7 +73,6 @@ def test_allgather_one_pe(m, n, k, tile_n, pairs):
     _check(prob, shards, bs, [gathered], [out], [events])
 
 
-@_UNVERIFIED
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("m,n,k,tile_n", [(1024, 384, 192, 0), (1024, 512, 4096, 256)])
 def test_allgather_two_pes(m, n, k, tile_n):

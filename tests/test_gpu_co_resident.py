@@ -4,13 +4,11 @@ unit graph. Its operators are the phased launcher's, so the output must
 match that launcher and the oracle bit for bit, and the event tensor must
 hold megacu's ready values (tile + 1 in every PE's slot).
 
-The one-PE cases and the example have passed on a B200; the two-PE case
-runs only with MEGACU_B200_UNVERIFIED=1 until it has too. The lowering and
+Every case and the example have passed on B200s. The lowering and
 validation are covered without a GPU in test_co_resident.py.
 """
 from __future__ import annotations
 
-import os
 
 import numpy as np
 import pytest
@@ -22,9 +20,6 @@ from conftest import gpu_count
 from gpu_util import same_process_team
 
 pytestmark = pytest.mark.gpu
-_UNVERIFIED = pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
-                                 reason="two-PE co-resident loop awaiting its first B200 run "
-                                        "(set MEGACU_B200_UNVERIFIED=1)")
 
 
 @pytest.mark.parametrize("m,n,k,tm,tn", [(200, 136, 70, 16, 32), (256, 256, 64, 128, 128),
@@ -62,7 +57,6 @@ def test_one_pe_bit_exact_with_phased_launcher(m, n, k, tm, tn):
     assert events[1].tolist() == events[0].tolist() == list(range(1, tiles + 1))
 
 
-@_UNVERIFIED
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
 def test_two_pes_match_oracle():
     m, n, k, tm, tn = 256, 384, 96, 64, 128

@@ -3,7 +3,6 @@ CPU oracle: the SwiGLU gate/up projection alone, and chains of blocks on one
 PE and on a two-GPU team (one process, peer exchange)."""
 from __future__ import annotations
 
-import os
 
 import numpy as np
 import pytest
@@ -111,15 +110,8 @@ def test_mlp_chain_one_pe_matches_oracle(layers, single, pairs):
     _check_chain(x, wg, wu, wd, out, bufs["x_work"])
 
 
-# The single-launch chain's cross-GPU exchange has not had its first two-GPU
-# run yet: that case runs only with MEGACU_B200_UNVERIFIED=1 until it has.
-_UNVERIFIED = pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
-                                 reason="single-launch chain on two GPUs awaiting its first run "
-                                        "(set MEGACU_B200_UNVERIFIED=1)")
-
-
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("single", [False, pytest.param(True, marks=_UNVERIFIED)])
+@pytest.mark.parametrize("single", [False, True])
 def test_mlp_chain_two_gpus_matches_oracle(single):
     t, h, i, layers = 256, 256, 192, 2
     x = seeded_bf16(91, (t, h), 1.0)
@@ -163,7 +155,7 @@ def _check_chain_events(prob, events_list, n_pes):
         assert mb.events_counters(ev) == want, f"PE {pe}: counters"
 
 
-@pytest.mark.parametrize("n_pes", [1, pytest.param(2, marks=_UNVERIFIED)])
+@pytest.mark.parametrize("n_pes", [1, 2])
 def test_single_launch_chain_events_match_oracle(n_pes):
     if gpu_count() < n_pes:
         pytest.skip("needs two GPUs")

@@ -1,9 +1,8 @@
 """Full-size multi-GPU parity (benchmark configs 2 and 3 at their sizes, K
 split over the ranks) under torchrun, one rank per GPU: tests/mp_full_worker.py.
 
-These tests run only with MEGACU_B200_UNVERIFIED=1 until the worker has had
-its first run on B200s; the kernel paths it calls are the ones
-test_multiproc.py checks against the oracle at small sizes.
+The kernel paths it calls are the ones test_multiproc.py checks against the
+oracle at small sizes.
 """
 from __future__ import annotations
 
@@ -20,9 +19,6 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 pytestmark = [
     pytest.mark.gpu,
     pytest.mark.multigpu,
-    pytest.mark.skipif(os.environ.get("MEGACU_B200_UNVERIFIED") != "1",
-                       reason="full-size multi-GPU worker awaiting its first B200 run "
-                              "(set MEGACU_B200_UNVERIFIED=1)"),
     pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs"),
 ]
 
