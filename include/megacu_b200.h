@@ -354,13 +354,26 @@ megacu_status megacu_b200_co_resident_status(void *control, void *stream, int64_
  * until the process exits. Limits: team_n_pes must be 1 (unsupported/51);
  * at most 8183 output tiles (invalid_argument/52). Every call on a GPU shares
  * that array, so calls that overlap on the GPU race — issue them in stream
- * order. The first call on a device looks up the array's address with that
- * device current; make it before any stream capture.
+ * order. Each call clears the array's queue tickets and error word first,
+ * so an error is reported for the call that met it and never stops a later
+ * call. The first call on a device (and the first after its context was
+ * reset) looks up the array's address with that device current; make it
+ * before any stream capture.
  */
 megacu_status megacu_cuda_gemm_bf16_noalloc(megacu_driver_view driver,
                                             const void *a, const void *b,
                                             void *out,
                                             megacu_gemm_ar_problem_v2 problem);
+
+/*
+ * Device address (*events) and size (*bytes, may be NULL) of `device`'s
+ * built-in scratch used by megacu_cuda_gemm_bf16_noalloc (no counterpart in
+ * megacu). Allocates nothing. Pass the address to megacu_b200_events_status
+ * for the last call's error (read and cleared) and to
+ * megacu_b200_events_counters for completion counters summed over every
+ * allocation-free call on that GPU (counters[7] counts every error).
+ */
+megacu_status megacu_b200_noalloc_scratch(int32_t device, void **events, int64_t *bytes);
 
 /* Bytes of workspace / events a bf16 call needs for `problem` on n_pes PEs. */
 megacu_status megacu_b200_workspace_bytes(megacu_gemm_ar_problem_v2 problem,

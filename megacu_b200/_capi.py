@@ -101,6 +101,8 @@ _PROTOTYPES = {
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
     "megacu_cuda_gemm_bf16_noalloc":
         (Status, [DriverView, c_void_p, c_void_p, c_void_p, GemmArProblemV2]),
+    "megacu_b200_noalloc_scratch":
+        (Status, [c_int32, ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64)]),
     "megacu_b200_workspace_bytes":
         (Status, [GemmArProblemV2, c_int32, ctypes.POINTER(c_int64)]),
     "megacu_b200_events_bytes": (Status, [GemmArProblemV2, c_int32, ctypes.POINTER(c_int64)]),

@@ -48,6 +48,13 @@ PRELUDE = {
         int64_t ws_bytes = 4096, out_bytes = 4096;
         bool all_valid = true;
         unsigned char const *all_mc_handles = nullptr;""",
+    "void *scratch = nullptr;\nmegacu_b200_noalloc_scratch(": """
+        int device = 0;
+        cudaStream_t stream = nullptr;
+        void const *a = nullptr, *b = nullptr;
+        void *out = nullptr;
+        megacu_driver_view driver{};
+        megacu_gemm_ar_problem_v2 problem{};""",
 }
 
 HEADERS = """
@@ -103,7 +110,7 @@ def test_every_cpp_snippet_is_checked():
     assert len(_host_snippets()) + sum("co_resident" in b for b in cpp) == len(cpp)
 
 
-@pytest.mark.parametrize("i", range(3))
+@pytest.mark.parametrize("i", range(4))
 def test_host_snippet_compiles(tmp_path, i):
     gxx = shutil.which("g++")
     if gxx is None:
