@@ -13,6 +13,14 @@ are aligned by a device-side team barrier before every timed step, both
 outside the events; the whole timed region is bracketed by a barrier and a
 device synchronise; the reported time is the max over ranks.
 
+After the timing, every rank checks the output of the last timed call
+(``parity`` in the line): against an fp32 reference of the same inputs
+(each rank's slices multiplied in fp32, summed over the ranks by NCCL in
+fp32), bit identity of every rank's output, and the completion counters of
+every call against megacu's task graph; likewise the deterministic mode
+(fp32 partials on the wire, fixed PE-order sum), which must also give the
+same bits twice. A failed check makes the run exit non-zero after printing.
+
 ``--impl reference`` times the reference's path on the host cores instead:
 megacu has no CPU implementation of its GEMM/allreduce math (its numeric path
 is CUDA only), so this is the CPU restatement of its tile-task graph
@@ -32,8 +40,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from megacu_b200.measure import (NVLINK_GBS, ClockSampler, NvlinkCounters, interleaved,  # noqa: E402
-                                  mean, peaks, seeded)
+from megacu_b200.measure import (NVLINK_GBS, REL_TOL, STRICT_FLOOR, ClockSampler,  # noqa: E402
+                                  NvlinkCounters, all_ranks, burst_peak, expected_counters,
+                                  interleaved, mean, output_errors, peaks, ranks_identical,
+                                  reference_sum, seeded)
 
 M, N, K_TOTAL = 4096, 8192, 8192
 WORKLOAD = "C2 row-parallel GEMM+allreduce M4096 N8192 K8192/tp bf16"
@@ -121,6 +131,108 @@ def run_reference(args, rank):
 # GPU leg
 # ---------------------------------------------------------------------------
 
+def exchange_rate(trace, plan, tp, rank, in_switch, dev):
+    """NVLink bytes a PE sends and receives in one call, over its exchange
+    window from the kernel's trace; per rank and their mean / min."""
+    import torch
+    import torch.distributed as dist
+    rec = trace.view(-1, 4).cpu().numpy().astype(np.uint64)
+    rec = rec[rec[:, 3] != 0]
+    red = (rec[:, 0] & 0xFF) == 2
+    window_s = float(rec[red, 3].max() - rec[red, 2].min()) * 1e-9 if red.any() else 0.0
+    s_out = M * N * 2
+    s_wire = M * N * plan.wire_bytes
+    if in_switch:
+        # the switch reads every PE's whole partial for the owners' reductions
+        # and multicasts each owner's sum into every PE's out
+        sent, received = s_wire + s_out / tp, s_wire / tp + s_out
+    elif plan.one_shot:
+        sent = received = (tp - 1) * s_wire
+    else:
+        sent = received = (tp - 1) / tp * (s_wire + s_out)
+    mine = torch.zeros((tp, 3), dtype=torch.float64, device=dev)
+    mine[rank] = torch.tensor([window_s, sent, received], dtype=torch.float64)
+    dist.all_reduce(mine)
+    rows = mine.tolist()
+    rates = [(x[1] / x[0] / 1e9 if x[0] > 0 else 0.0, x[2] / x[0] / 1e9 if x[0] > 0 else 0.0)
+             for x in rows]
+    return {"sent_bytes_per_pe": sent, "received_bytes_per_pe": received,
+            "window_us": [round(x[0] * 1e6, 2) for x in rows],
+            "sent_gbs": [round(r[0], 1) for r in rates],
+            "received_gbs": [round(r[1], 1) for r in rates],
+            "sent_gbs_mean": sum(r[0] for r in rates) / tp,
+            "received_gbs_mean": sum(r[1] for r in rates) / tp,
+            "vs_measured_770_gbs": max(sum(r[0] for r in rates), sum(r[1] for r in rates))
+            / tp / NVLINK_GBS,
+            "vs_nominal_900_gbs": max(sum(r[0] for r in rates), sum(r[1] for r in rates))
+            / tp / 900.0,
+            "source": "one traced call: first to last reduce sub-task of each PE "
+                      "(%globaltimer); bytes per PE from the plan "
+                      + ("(in-switch: partial read by the switch + 1/tp multicast out; "
+                         "(1/tp) reduced + out multicast in)" if in_switch else
+                         "(peer loads)")}
+
+
+def check_outputs(a, b, out, c, unfused, plan, tp, rank, dev, launched, events, stream,
+                  det=None):
+    """Checks the last timed call on every rank (the same collectives on every
+    rank, in the same order): the output against the fp32 reference of the
+    same inputs summed over the ranks, bit identity across ranks, and the
+    completion counters of every call on `events` (`launched` counts them)
+    against megacu's task graph; the unfused baseline's output against the
+    same reference; the deterministic mode (`det`) likewise, run once more for
+    bit identity with its last timed call."""
+    import torch
+
+    import megacu_b200 as mb
+    torch.cuda.synchronize()
+    want, scale = reference_sum(a, b, tp)
+    bf16_wire = tp > 1 and plan.wire_bytes == 2
+    parity = {"reference": "each rank's bf16 slices multiplied in fp32 (TF32 off), summed over "
+                           "the ranks by NCCL in fp32",
+              "tol": REL_TOL,
+              "max_rel_err_denominator": "sum over ranks of |partial| + RMS(want) (bf16 "
+                                         "partials on the wire)" if bf16_wire else
+                                         "|want| + RMS(want)",
+              "strict_floor": f"|want| >= {STRICT_FLOOR} x RMS(want)"}
+    parity.update(output_errors(out, want, scale if bf16_wire else None))
+    parity["ranks_identical"] = ranks_identical(out, tp)
+    per_call = expected_counters(tp, rank, plan.m_tiles, plan.n_tiles, plan.tile_n,
+                                 plan.one_shot)
+    counters_ok = mb.events_counters(events, stream) == [launched["fused"] * x for x in per_call]
+    ok = parity["max_rel_err"] < REL_TOL and parity["ranks_identical"] and counters_ok
+    if not bf16_wire:
+        ok = ok and parity["max_rel_err_strict"] < REL_TOL
+    # the unfused cuBLAS + NCCL output of the same inputs, against the same reference
+    unfused()
+    torch.cuda.synchronize()
+    parity["unfused_cublas_nccl"] = output_errors(c, want)
+    if det is not None:
+        det_prob, det_out, det_events, det_call, align = det
+        first = det_out.clone()
+        align()
+        det_call()
+        torch.cuda.synchronize()
+        mb.events_status(det_events, stream)
+        d = output_errors(det_out, want)
+        d["bit_reproducible"] = bool(torch.equal(first, det_out))
+        d["ranks_identical"] = ranks_identical(det_out, tp)
+        det_plan = mb.plan(det_prob, tp)
+        det_per_call = expected_counters(tp, rank, det_plan.m_tiles, det_plan.n_tiles,
+                                         det_plan.tile_n, det_plan.one_shot)
+        det_counters_ok = (mb.events_counters(det_events, stream) ==
+                           [launched["deterministic"] * x for x in det_per_call])
+        counters_ok = counters_ok and det_counters_ok
+        ok = (ok and d["max_rel_err"] < REL_TOL and d["max_rel_err_strict"] < REL_TOL and
+              d["bit_reproducible"] and d["ranks_identical"] and det_counters_ok)
+        parity["deterministic"] = d
+        del first
+    del want, scale
+    parity["counters_ok"] = all_ranks(counters_ok, tp, dev)
+    parity["ok"] = all_ranks(ok, tp, dev)
+    return parity
+
+
 def run_gpu(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -143,7 +255,14 @@ def run_gpu(args, rank, world, local_rank):
     plan = mb.plan(prob, tp)
     ws_bytes = mb.workspace_bytes(prob, tp)
     ev_bytes = mb.events_bytes(prob, tp)
-    heap = ws_bytes + ev_bytes + M * N * 2 + (64 << 20)
+    # The deterministic mode (fp32 partials on the wire, PE-order sum over
+    # peer loads, bit-reproducible) is timed and checked beside the default
+    # at tp > 1, with buffers of its own.
+    det_prob = mb.Problem(M, N, k, deterministic=True, timeout_ns=30_000_000_000)
+    det_ws_bytes = mb.workspace_bytes(det_prob, tp) if tp > 1 else 0
+    det_ev_bytes = mb.events_bytes(det_prob, tp) if tp > 1 else 0
+    det_bytes = det_ws_bytes + det_ev_bytes + M * N * 2 if tp > 1 else 0
+    heap = ws_bytes + ev_bytes + M * N * 2 + det_bytes + (64 << 20)
     exchange = mb.torch_exchange() if tp > 1 else None
     # Two-shot allreduce: workspace and out in a multicast region select the
     # in-switch reduction (NVLS); without one the exchange uses peer loads.
@@ -164,9 +283,12 @@ def run_gpu(args, rank, world, local_rank):
     out_host = torch.empty((rows_back, N), dtype=torch.bfloat16).pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
-    def call(aa, bb):
+    launched = {"fused": 0, "deterministic": 0}  # launches on each events buffer
+
+    def call(aa, bb, trace=None):
+        launched["fused"] += 1
         mb.gemm_allreduce(aa, bb, out, workspace=ws, events=events, problem=prob, stream=stream,
-                          device=local_rank, team=team if tp > 1 else None)
+                          device=local_rank, team=team if tp > 1 else None, trace=trace)
 
     def align():
         flush.fill_(1)
@@ -209,7 +331,16 @@ def run_gpu(args, rank, world, local_rank):
             mb.gemm_allreduce(a, b, solo_out, workspace=None, events=solo_events,
                               problem=solo_prob, stream=stream, device=local_rank)
 
-        arms.append(kernel_without_exchange)
+        det_ws = team.tensor((max(det_ws_bytes, 16),), torch.uint8)
+        det_events = team.tensor((det_ev_bytes // 4,), torch.int32)
+        det_out = team.tensor((M, N), torch.bfloat16)
+
+        def deterministic():
+            launched["deterministic"] += 1
+            mb.gemm_allreduce(a, b, det_out, workspace=det_ws, events=det_events,
+                              problem=det_prob, stream=stream, device=local_rank, team=team)
+
+        arms += [kernel_without_exchange, deterministic]
 
     # The clock sampler runs from the heat-up through the timed steps. The
     # heat-up (a fixed number of untimed calls of both arms, the same on every
@@ -225,6 +356,7 @@ def run_gpu(args, rank, world, local_rank):
     times = [mean(x) for x in step_ms]
     ms_fused, ms_unfused, ms_gemm = times[:3]
     ms_solo = times[3] if tp > 1 else None
+    ms_det = times[4] if tp > 1 else None
     fused_sorted = sorted(step_ms[0])
     last = len(fused_sorted) - 1
     fused_stats = {q: fused_sorted[min(last, int(frac * len(fused_sorted)))] * 1e3
@@ -232,6 +364,7 @@ def run_gpu(args, rank, world, local_rank):
     mb.events_status(events, stream)
     if tp > 1:
         mb.events_status(solo_events, stream)
+        mb.events_status(det_events, stream)
     flops_total = 2.0 * M * N * K_TOTAL
     flops_rank = flops_total / tp
     value = flops_total / (ms_fused * 1e-3) / 1e12
@@ -279,6 +412,26 @@ def run_gpu(args, rank, world, local_rank):
     h2d = a_host.numel() * 2 + b_host.numel() * 2
     d2h = out_host.numel() * 2
 
+    # ---- exchange rate from the kernel's own trace (tp > 1) ----
+    # One traced call (L2 flushed, PEs aligned): the exchange window of a PE
+    # runs from its first reduce sub-task's start to its last one's end
+    # (%globaltimer, trace kind 2); the bytes a PE sends and receives over
+    # NVLink in it follow from the plan.
+    nvlink_achieved = None
+    if tp > 1:
+        trace = torch.zeros(plan.tiles * 64 * 4, dtype=torch.int64, device=dev)
+        align()
+        call(a, b, trace=trace)
+        torch.cuda.synchronize()
+        mb.events_status(events, stream)
+        nvlink_achieved = exchange_rate(trace, plan, tp, rank, use_mc, dev)
+        del trace
+
+    # ---- output check of the timed calls ----
+    parity = check_outputs(a, b, out, c, unfused, plan, tp, rank, dev, launched, events, stream,
+                           det=(det_prob, det_out, det_events, deterministic, align)
+                           if tp > 1 else None)
+
     # ---- CPU baseline (rank 0, N = 1 only) ----
     cpu = None
     if rank == 0 and tp == 1 and not args.no_cpu:
@@ -288,7 +441,11 @@ def run_gpu(args, rank, world, local_rank):
                "sample": f"{done} output tiles of 128x256 with full K={K_TOTAL} "
                          f"({el:.1f} s of CPU time, oracle/ restatement)"}
 
-    peak, peak_src = peaks()
+    # One call timed after an L2 flush is held against the burst peak; the
+    # sustained one (a seconds-long cuBLAS loop under the power cap) is given
+    # beside it.
+    peak, peak_src = burst_peak()
+    peak_sustained, _ = peaks()
     achieved = flops_rank / (ms_fused * 1e-3) / 1e12
     # North-star roofline: the slower of the GEMM at the measured peak and the
     # allreduce's bytes per PE over NVLink (its bus bytes, 2 (tp-1)/tp of the
@@ -326,6 +483,8 @@ def run_gpu(args, rank, world, local_rank):
             "gpu_launches": args.steps * launches_per_step,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "peak_source": peak_src,
+                         "frac_of_sustained": achieved / peak_sustained,
+                         "peak_sustained": peak_sustained,
                          "traffic": traffic,
                          "kernel": "gemm_ar_megakernel", "per_launch_flops": flops_rank},
             "roofline_call": {"bound": "nvlink" if t_link_us > t_gemm_us else "tensor",
@@ -342,6 +501,12 @@ def run_gpu(args, rank, world, local_rank):
                 "note": "fused call minus the same kernel on one PE with this PE's K slice "
                         "(no exchange), timed interleaved with the other arms"},
             "nvlink_measured": nvlink,
+            "nvlink_achieved": nvlink_achieved,
+            "deterministic": None if ms_det is None else {
+                "us": ms_det * 1e3, "tflops": flops_total / (ms_det * 1e-3) / 1e12,
+                "note": "deterministic = 1: fp32 partials over peer loads, PE-order sum, "
+                        "bit-reproducible; timed interleaved with the other arms"},
+            "parity": parity,
             "cpu_baseline": cpu,
             "unfused_cublas_nccl": {"us": ms_unfused * 1e3, "gemm_us": ms_gemm * 1e3,
                                     "comm_us": max(ms_unfused - ms_gemm, 0.0) * 1e3,
@@ -352,6 +517,7 @@ def run_gpu(args, rank, world, local_rank):
         }
         print(json.dumps(line), flush=True)
     team.close()
+    return parity["ok"]
 
 
 def main():
@@ -382,11 +548,15 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_gpu(args, rank, world, local_rank)
+        ok = run_gpu(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+    if not ok:
+        print(f"rank {rank}: output check failed (see the line's parity object)",
+              file=sys.stderr, flush=True)
+        sys.exit(1)
 
 
 if __name__ == "__main__":

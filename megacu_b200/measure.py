@@ -11,6 +11,11 @@
 * ``NvlinkCounters``: NVML NVLink payload counters of one GPU.
 * ``interleaved``: CUDA-event timing of several arms, interleaved step by
   step, the max over ranks of each step.
+* ``reference_sum``, ``output_errors``, ``ranks_identical``,
+  ``expected_counters``: the output check every timing tool runs on the
+  calls it timed (an fp32 reference of the same inputs summed over the ranks
+  by NCCL, both relative-error measures, bit identity across ranks, and the
+  completion counters of megacu's task graph).
 """
 from __future__ import annotations
 
@@ -39,6 +44,19 @@ def _peaks_file():
             return json.load(f)
     except Exception:
         return None
+
+
+def burst_peak():
+    """The dense bf16 peak of a kernel timed in isolation: the measured burst
+    cuBLAS figure, else the sustained one, else the fallback."""
+    p = _peaks_file()
+    try:
+        if "bf16_tflops" in p:
+            return float(p["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+        return (float(p["bf16_tflops_sustained"]),
+                "measured (MEASURED_PEAKS.json bf16_tflops_sustained)")
+    except Exception:
+        return FALLBACK_TFLOPS, "fallback (1.59 PFLOP/s, no MEASURED_PEAKS.json)"
 
 
 def peaks():
@@ -198,3 +216,124 @@ def mean(xs):
 
 def p50(xs):
     return statistics.median(xs)
+
+
+# ---------------------------------------------------------------------------
+# Output check of the timed calls
+# ---------------------------------------------------------------------------
+
+# Tolerance of the bf16 path (north star: max relative error 1e-2, bf16
+# inputs, fp32 accumulate) and the floor of the strict measure: elements with
+# |want| below STRICT_FLOOR x RMS(want) (about 0.08 % of a Gaussian output)
+# are left out of max |got - want| / |want|, whose denominator vanishes there.
+REL_TOL = 1e-2
+STRICT_FLOOR = 1e-3
+
+
+def reference_sum(a, b, world, rows=1024):
+    """fp32 reference of the allreduced output and its condition: this rank's
+    bf16 slices multiplied in fp32 (TF32 off), then summed over the ranks by
+    NCCL in fp32. Returns (want, scale), scale = the sum over ranks of
+    |partial| per element (what a bf16 partial's rounding is relative to)."""
+    import torch
+    import torch.distributed as dist
+    torch.backends.cuda.matmul.allow_tf32 = False
+    bf = b.float()
+    m, n = a.shape[0], b.shape[1]
+    want = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    scale = torch.empty_like(want)
+    for r0 in range(0, m, rows):
+        part = torch.matmul(a[r0:r0 + rows].float(), bf)
+        want[r0:r0 + rows] = part
+        scale[r0:r0 + rows] = part.abs()
+    del bf
+    if world > 1:
+        dist.all_reduce(want)
+        dist.all_reduce(scale)
+    return want, scale
+
+
+def output_errors(got, want, scale=None, rows=1024):
+    """Both relative-error measures of `got` (any float dtype) against the
+    fp32 `want`:
+
+    * ``max_rel_err``: max |got - want| / (s + RMS(want)), s = |want|, or
+      `scale` where given (the sum of the partials' magnitudes, for bf16
+      partials on the wire, which are exact only to a bf16 ulp of
+      themselves);
+    * ``max_rel_err_strict``: max |got - want| / |want| over the elements with
+      |want| >= STRICT_FLOOR x RMS(want).
+
+    A NaN anywhere makes both NaN (which fails every comparison)."""
+    import torch
+    m = want.shape[0]
+    sq = 0.0
+    for r0 in range(0, m, rows):
+        sq += float(want[r0:r0 + rows].double().pow(2).sum())
+    rms = (sq / max(want.numel(), 1)) ** 0.5
+    floor = STRICT_FLOOR * rms
+    loose = strict = 0.0
+    for r0 in range(0, m, rows):
+        w = want[r0:r0 + rows]
+        err = (got[r0:r0 + rows].float() - w).abs_()
+        aw = w.abs()
+        s = aw if scale is None else scale[r0:r0 + rows]
+        loose = max(loose, float((err / (s + (rms + 1e-30))).max())) if err.numel() else loose
+        keep = (aw >= floor) & (aw > 0)
+        if bool(keep.any()):
+            strict = max(strict, float((err[keep] / aw[keep]).max()))
+        if bool(torch.isnan(err).any()):
+            return {"max_rel_err": float("nan"), "max_rel_err_strict": float("nan")}
+    return {"max_rel_err": loose, "max_rel_err_strict": strict}
+
+
+def ranks_identical(t, world):
+    """True on every rank when every rank's `t` holds the same bits as rank 0's."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return True
+    ref = t.clone()
+    dist.broadcast(ref, 0)
+    same = torch.tensor([1 if torch.equal(ref, t) else 0], dtype=torch.int32, device=t.device)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    return bool(same.item())
+
+
+def all_ranks(flag, world, device):
+    """True when `flag` is true on every rank (every rank gets the answer)."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return bool(flag)
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def expected_counters(n_pes, me, m_tiles, n_tiles, tile_n, one_shot, mode=0):
+    """Completion counters (layout.h's ctr_* order) that one call of the bf16
+    kernel adds on PE `me`, for shapes whose every tile is whole (m a
+    multiple of 128, n of tile_n). megacu's task graph per tile: task 0 (the
+    GEMM tile) and its publish, per 32-row quarter, to each PE that reduces
+    the tile; task 2 per (reduced tile, quarter, 64-column block), after
+    acquiring every PE's partial of that quarter; in a two-shot allreduce the
+    owner's stores into every PE's out count as final publishes, and each PE
+    acquires every PE's done flag once. The tests pin this against the
+    oracle's graph."""
+    tiles = m_tiles * n_tiles
+    blocks = tile_n // 64
+    c = [0] * 8
+    c[0] = tiles
+    c[6] = 1
+    if n_pes == 1:
+        c[2] = tiles * 4
+        return c
+    c[2] = tiles * 4 * (n_pes if one_shot else 1)
+    reduced = tiles if one_shot else (tiles - me + n_pes - 1) // n_pes
+    c[1] = reduced * 4 * blocks
+    c[3] = c[1] * n_pes
+    if mode == 0 and not one_shot:
+        c[4] = c[1] * n_pes
+        c[5] = n_pes
+    return c

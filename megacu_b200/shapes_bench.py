@@ -29,12 +29,21 @@ outside the CUDA events; every step's time is the max over ranks:
                            the fused time minus this is the exchange time
                            the kernel did not hide
 Configs 3 and ag report the mean per call, config 4 the p50. Prints one JSON
-line per shape on rank 0. ``--graph`` times every arm as the replay of a CUDA
-graph captured from it (launch overhead out of the measurement; an arm whose
-capture fails is timed as launched and marked so). ``--algo one|two`` forces
-the allreduce exchange of config 4 (auto picks one-shot for one tile row),
-and ``--multicast`` puts a two-shot call's workspace and output in the team's
-multicast region (the in-switch reduction).
+line per shape on rank 0. After the timing every rank checks the last timed
+fused call (``parity``): its output against an fp32 reference of the same
+inputs (each rank's slices multiplied in fp32, summed over the ranks by NCCL
+in fp32; for `ag` the gathered A from NCCL's all-gather times this PE's B in
+fp32), every rank's allreduce output bit-identical, the completion counters
+of every launch against megacu's task graph (configs 3 and 4), and for `ag`
+the gathered A bit for bit; the unfused output is held to the same
+reference. A failed check makes the run exit non-zero.
+
+``--graph`` times every arm as the replay of a CUDA graph captured from it
+(launch overhead out of the measurement; an arm whose capture fails is timed
+as launched and marked so). ``--algo one|two`` forces the allreduce exchange
+of config 4 (auto picks one-shot for one tile row), and ``--multicast`` puts
+a two-shot call's workspace and output in the team's multicast region (the
+in-switch reduction).
 """
 from __future__ import annotations
 
@@ -42,8 +51,9 @@ import argparse
 import json
 import os
 
-from .measure import (NVLINK_GBS, ClockSampler, hbm_peak, interleaved, mean, p50, peaks,
-                      seeded)
+from .measure import (NVLINK_GBS, REL_TOL, STRICT_FLOOR, ClockSampler, all_ranks,
+                      expected_counters, hbm_peak, interleaved, mean, output_errors, p50,
+                      peaks, ranks_identical, reference_sum, seeded)
 
 C3 = dict(m=8192, n=8192, k_total=28672)
 C4 = dict(m=(16, 32, 64, 128), n=8192, k_total=28672)
@@ -190,6 +200,8 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
     mb.events_status(events, stream)
     if solo_events is not None:
         mb.events_status(solo_events, stream)
+    parity = check_shape(a, b, out, c, c_rs, unfused, pl, config, tp, rank, dev, events, stream,
+                         launches=heat + args.warmup + args.steps)
     stat = mean if config == 3 else p50
     us = {name: stat(v) * 1e3 for name, v in zip(names, ms)}
     flops_job = 2.0 * m * n * k_total
@@ -209,9 +221,55 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         "l2": "flushed (256 MiB write) before every timed step",
         "cuda_graph_replay": graphed,
         "clocks": clocks.summary(),
+        "parity": parity,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    return parity["ok"]
+
+
+def _parity_header(bf16_wire):
+    return {"reference": "each rank's bf16 slices multiplied in fp32 (TF32 off), summed over "
+                         "the ranks by NCCL in fp32",
+            "tol": REL_TOL,
+            "max_rel_err_denominator": "sum over ranks of |partial| + RMS(want) (bf16 partials "
+                                       "on the wire)" if bf16_wire else "|want| + RMS(want)",
+            "strict_floor": f"|want| >= {STRICT_FLOOR} x RMS(want)"}
+
+
+def check_shape(a, b, out, c, c_rs, unfused, pl, config, tp, rank, dev, events, stream,
+                launches):
+    """Checks the last timed fused call of configs 3 / 4 on every rank (the
+    same collectives on every rank, in the same order)."""
+    import torch
+
+    import megacu_b200 as mb
+    torch.cuda.synchronize()
+    want, scale = reference_sum(a, b, tp)
+    rows = out.shape[0]
+    if config == 3:  # this PE's rows of the reduce-scattered sum
+        want = want[rank * rows:(rank + 1) * rows]
+        scale = scale[rank * rows:(rank + 1) * rows]
+    bf16_wire = tp > 1 and pl.wire_bytes == 2
+    parity = _parity_header(bf16_wire)
+    parity.update(output_errors(out, want, scale if bf16_wire else None))
+    parity["ranks_identical"] = ranks_identical(out, tp) if config == 4 else None
+    mode = 1 if config == 3 else 0
+    per_call = expected_counters(tp, rank, pl.m_tiles, pl.n_tiles, pl.tile_n, pl.one_shot, mode)
+    whole = out.shape[0] % 128 == 0 or config == 3
+    counters = mb.events_counters(events, stream)
+    counters_ok = (counters == [launches * x for x in per_call]) if whole else (
+        counters[6] == launches and counters[7] == 0)
+    ok = parity["max_rel_err"] < REL_TOL and counters_ok and parity["ranks_identical"] is not False
+    if not bf16_wire:
+        ok = ok and parity["max_rel_err_strict"] < REL_TOL
+    unfused()
+    torch.cuda.synchronize()
+    parity["unfused_cublas_nccl"] = output_errors(c_rs if (config == 3 and tp > 1) else c, want)
+    del want, scale
+    parity["counters_ok"] = all_ranks(counters_ok, tp, dev)
+    parity["ok"] = all_ranks(ok, tp, dev)
+    return parity
 
 
 def run_allgather(args, rank, world, local, team_cache):
@@ -285,6 +343,26 @@ def run_allgather(args, rank, world, local, team_cache):
     mb.events_status(events, stream)
     if solo_events is not None:
         mb.events_status(solo_events, stream)
+    # Check of the last timed call: the gathered A bit for bit against NCCL's
+    # all-gather of the same shards (the unfused arm's g_nccl), the output
+    # against g_nccl @ B in fp32 (one PE's GEMM: the strict measure applies).
+    torch.cuda.synchronize()
+    unfused()
+    torch.cuda.synchronize()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    want = torch.empty((m, n), dtype=torch.float32, device=dev)
+    bf = b.float()
+    for r0 in range(0, m, 1024):
+        want[r0:r0 + 1024] = torch.matmul(g_nccl[r0:r0 + 1024].float(), bf)
+    del bf
+    parity = _parity_header(False)
+    parity.update(output_errors(out, want))
+    parity["gathered_bit_exact"] = bool(torch.equal(gathered, g_nccl))
+    parity["unfused_cublas_nccl"] = output_errors(c, want)
+    del want
+    ok = (parity["max_rel_err"] < REL_TOL and parity["max_rel_err_strict"] < REL_TOL and
+          parity["gathered_bit_exact"])
+    parity["ok"] = all_ranks(ok, tp, dev)
     us = {name: mean(v) * 1e3 for name, v in zip(names, ms)}
     flops_pe = 2.0 * m * n * k
     line = {
@@ -299,9 +377,11 @@ def run_allgather(args, rank, world, local, team_cache):
         "exposed_comm_us": (us["fused"] - us["kernel_without_exchange"]) if tp > 1 else None,
         "l2": "flushed (256 MiB write) before every timed step",
         "clocks": clocks.summary(),
+        "parity": parity,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    return parity["ok"]
 
 
 def main() -> int:
@@ -348,21 +428,24 @@ def main() -> int:
                              multicast_bytes=multicast_bytes))
         return teams[0]
 
+    ok = True
     try:
         if args.config == "ag":
-            run_allgather(args, rank, world, local, team_cache)
+            ok = run_allgather(args, rank, world, local, team_cache)
         elif args.config == "3":
-            run_shape(args, 3, C3["m"], C3["n"], C3["k_total"], rank, world, local, team_cache)
+            ok = run_shape(args, 3, C3["m"], C3["n"], C3["k_total"], rank, world, local,
+                           team_cache)
         else:
             ms = [int(x) for x in args.m.split(",") if x] or list(C4["m"])
             for m in ms:
-                run_shape(args, 4, m, C4["n"], C4["k_total"], rank, world, local, team_cache)
+                ok = run_shape(args, 4, m, C4["n"], C4["k_total"], rank, world, local,
+                               team_cache) and ok
         for t in teams:
             t.close()
     finally:
         if world > 1:
             dist.destroy_process_group()
-    return 0
+    return 0 if ok else 1
 
 
 if __name__ == "__main__":

@@ -75,6 +75,15 @@ def _check_line(line, tp, ms):
     assert e2e["d2h_bytes_per_step"] == (M // tp) * N * 2
     assert line["gpu_launches"] == STEPS
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(line["clocks"])
+    # the output check ran on the stand-ins' outputs (zeros against a zero
+    # reference) and the counters of every call matched the oracle's graph
+    par = line["parity"]
+    assert {"max_rel_err", "max_rel_err_strict", "ranks_identical", "counters_ok",
+            "unfused_cublas_nccl", "ok"} <= set(par)
+    assert par["counters_ok"] is True and par["ok"] is True
+    if tp > 1:
+        assert {"bit_reproducible", "max_rel_err_strict"} <= set(par["deterministic"])
+        assert line["deterministic"]["us"] == pytest.approx(ms * 1e3)
 
 
 def test_one_gpu_line(monkeypatch):

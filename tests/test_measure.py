@@ -104,3 +104,37 @@ def test_decode_link_bytes_by_exchange():
     assert nvls["link_bytes_per_pe"] == pytest.approx(9 / 8 * out)
     # at M = 128 the one-shot exchange, not the weight stream, bounds the call
     assert one["bound"] == "nvlink" and two["bound"] == "hbm"
+
+
+@pytest.mark.parametrize("n_pes,m,n,tile_n,one_shot,mode", [
+    (1, 512, 768, 256, False, 0), (2, 512, 1024, 256, True, 0), (2, 1024, 512, 128, False, 0),
+    (4, 1024, 1024, 256, False, 0), (8, 1024, 2048, 256, False, 0), (8, 128, 1024, 64, True, 0),
+    (4, 1024, 768, 256, False, 1), (8, 2048, 512, 128, False, 1)])
+def test_expected_counters_equal_the_oracle_graph(n_pes, m, n, tile_n, one_shot, mode):
+    """The timing tools' closed form of one call's completion counters is the
+    oracle's task graph (which depends on the shape, not on k or the data)."""
+    import numpy as np
+
+    import oracle_lib
+    k = 8
+    a = [np.zeros((m, k), np.float32)] * n_pes
+    b = [np.zeros((k, n), np.float32)] * n_pes
+    ref = oracle_lib.bf16_call(a, b, m=m, n=n, k=k, tile_n=tile_n, mode=mode,
+                               one_shot=one_shot)
+    for pe in range(n_pes):
+        got = measure.expected_counters(n_pes, pe, m // 128, n // tile_n, tile_n, one_shot, mode)
+        assert got == ref["counters"][pe].tolist(), pe
+
+
+def test_output_errors_measures():
+    import torch
+    want = torch.tensor([[1.0, -2.0, 1e-6, 4.0]])
+    got = torch.tensor([[1.005, -2.0, 0.0, 4.0]])
+    e = measure.output_errors(got, want)
+    rms = float(want.pow(2).mean().sqrt())
+    assert e["max_rel_err_strict"] == pytest.approx(0.005, rel=1e-4)  # 1e-6 is below the floor
+    assert e["max_rel_err"] == pytest.approx(0.005 / (1.0 + rms), rel=1e-4)
+    scaled = measure.output_errors(got, want, scale=torch.full_like(want, 10.0))
+    assert scaled["max_rel_err"] == pytest.approx(0.005 / (10.0 + rms), rel=1e-4)
+    bad = measure.output_errors(torch.tensor([[float("nan"), 1.0, 1.0, 1.0]]), want)
+    assert not bad["max_rel_err"] < 1.0 and not bad["max_rel_err_strict"] < 1.0

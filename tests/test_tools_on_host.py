@@ -41,7 +41,10 @@ def _run_tool(name, argv):
     buf = io.StringIO()
     try:
         with contextlib.redirect_stdout(buf):
-            assert mod.main() == 0
+            rc = mod.main()
+        if rc != 0:
+            print(buf.getvalue()[-3000:], file=sys.stderr)
+        assert rc == 0
     finally:
         sys.argv = old
     return [json.loads(x) for x in buf.getvalue().splitlines() if x.startswith("{")]
