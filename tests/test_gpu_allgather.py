@@ -17,7 +17,7 @@ import torch
 import megacu_b200 as mb
 import oracle_lib
 from conftest import gpu_count
-from gpu_util import REL_TOL, f32, rel_error, same_process_team, seeded_bf16
+from gpu_util import assert_close, f32, same_process_team, seeded_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -42,8 +42,7 @@ def _check(prob, shards, bs, gathered, outs, events):
                                      group_m=pl.group_m, epoch=2, events=ref1["events"])
     for pe in range(n_pes):
         assert np.array_equal(f32(gathered[pe]), np.concatenate(s32)), f"PE {pe}: gathered A"
-        err = rel_error(f32(outs[pe]), ref2["out"][pe])
-        assert err < REL_TOL, f"PE {pe}: rel error {err}"
+        assert_close(f32(outs[pe]), ref2["out"][pe], what=f"PE {pe}:")
         got = events[pe][64:].cpu().numpy().view(np.uint32)
         assert np.array_equal(got, ref2["events"][pe]), f"PE {pe}: event tensor"
         counters = mb.events_counters(events[pe])

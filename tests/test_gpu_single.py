@@ -14,7 +14,7 @@ import torch
 import megacu_b200 as mb
 import oracle_lib
 from conftest import gpu_count
-from gpu_util import REL_TOL, SinglePE, f32, inputs, rel_error, trace_records
+from gpu_util import REL_TOL, SinglePE, assert_close, f32, inputs, rel_error, trace_records
 
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(gpu_count() < 1, reason="needs a CUDA GPU")]
@@ -42,7 +42,7 @@ def test_bf16_tp1_matches_oracle(m, n, k, tile_n, pairs):
     torch.cuda.synchronize()
     want = oracle_lib.bf16_call([f32(a[0])], [f32(b[0])], m=m, n=n, k=k,
                                 tile_n=ctx.plan.tile_n)["out"][0]
-    assert rel_error(f32(out), want) < REL_TOL
+    assert_close(f32(out), want)
 
 
 @pytest.mark.parametrize("pairs", [mb.CTA_PAIRS_OFF, mb.CTA_PAIRS_ON])
@@ -112,7 +112,7 @@ def test_bf16_bench_shape_sampled_tiles():
     out = ctx.run(ad, bd)
     torch.cuda.synchronize()
     full = torch.matmul(ad.float(), bd.float())
-    assert rel_error(out.float().cpu().numpy(), full.cpu().numpy()) < REL_TOL
+    assert_close(out.float().cpu().numpy(), full.cpu().numpy(), what="whole output vs torch fp32")
     pl = ctx.plan
     rng = np.random.default_rng(0)
     ids = np.sort(rng.choice(pl.tiles, 6, replace=False)).astype(np.int32)
@@ -122,7 +122,7 @@ def test_bf16_bench_shape_sampled_tiles():
     for t in ids:
         r0, c0 = (t // pl.n_tiles) * 128, (t % pl.n_tiles) * pl.tile_n
         sl = (slice(r0, r0 + 128), slice(c0, c0 + pl.tile_n))
-        assert rel_error(got[sl], want[sl]) < REL_TOL
+        assert_close(got[sl], want[sl], what=f"tile {t}")
 
 
 # ---- megacu's fp32 phased launcher ------------------------------------------------
