@@ -54,8 +54,9 @@ typedef struct megacu_status {
  *   24 team handle does not match   25 buffer outside the symmetric heap
  *   26 reduce-scatter or all-gather m not a multiple of tp * 128
  *   27 CTA pairs requested but the tile grid cannot hold them
- *   28 workspace / out in the multicast region of a call that cannot reduce
- *      in the switch (not a two-shot bf16-wire allreduce, or only one of them)
+ *   28 in-switch reduction not possible: the fp32 wire with the workspace in
+ *      the multicast region, or a two-shot allreduce with only one of
+ *      workspace and out there
  *   29 outside a single-launch MLP chain's limits (more than 6 blocks, or
  *      the fp32 wire)
  *   30 cuTensorMapEncodeTiled failed

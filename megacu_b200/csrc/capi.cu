@@ -300,6 +300,8 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   }
   team_impl *team = nullptr;
   bool via_switch = false;
+  // Two-shot allreduce: every owner stores its sums into every PE's out.
+  bool const out_symmetric = n_pes > 1 && problem.mode == MEGACU_MODE_ALLREDUCE && !pl.one_shot;
   if (n_pes > 1) {
     team = as_team(driver.team.team);
     if (team == nullptr) {
@@ -308,17 +310,19 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
     if (!team->connected || team->n_pes != n_pes || team->my_pe != my_pe) {
       return fail(MEGACU_INVALID_ARGUMENT, 24, "team handle does not match team_view");
     }
-    bool const out_symmetric = problem.mode == MEGACU_MODE_ALLREDUCE && !pl.one_shot;
     std::int64_t const out_bytes = problem.m * problem.n * 2;
-    // Workspace and out in the multicast region select the in-switch
-    // reduction, which exists for the two-shot bf16-wire allreduce only.
+    // A workspace in the multicast region selects the in-switch reduction
+    // (bf16 wire): a reducer reads every PE's partial of a block with one
+    // load, summed by the NVSwitch. A two-shot allreduce also stores each
+    // sum through the switch into every PE's out, so its out must lie in the
+    // region too; one-shot and reduce-scatter store into this PE's own out.
     bool const ws_mc = team->mc.contains(workspace, pl.workspace_bytes);
     bool const out_mc = team->mc.contains(out, out_bytes);
-    if (ws_mc || out_mc) {
-      if (!ws_mc || !out_mc || !out_symmetric || pl.wire_bytes != 2) {
+    if (ws_mc || (out_symmetric && out_mc)) {
+      if (!ws_mc || pl.wire_bytes != 2 || (out_symmetric && !out_mc)) {
         return fail(MEGACU_UNSUPPORTED, 28,
-                    "in-switch reduction needs workspace and out both in the multicast region "
-                    "and a two-shot allreduce with the bf16 wire");
+                    "in-switch reduction needs the bf16 wire and the workspace (for a two-shot "
+                    "allreduce also out) in the multicast region");
       }
       via_switch = true;
     }
@@ -359,13 +363,14 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   prm.mode = problem.mode == MEGACU_MODE_REDUCE_SCATTER ? mode_reduce_scatter : mode_allreduce;
   prm.one_shot = pl.one_shot;
   prm.group_m = pl.group_m;
-  // The reduce queue: every (reduced tile, quarter, 64-column block), the
-  // reduced tiles being this PE's own (two-shot, reduce-scatter) or all
-  // tiles (one-shot), in raster order.
+  // The reduce queue: every (reduced tile, 32-row quarter, 64-column block),
+  // the reduced tiles being this PE's own (two-shot, reduce-scatter) or all
+  // tiles (one-shot), in raster order. The in-switch reduction hands out
+  // (tile, quarter) tickets and reduces their blocks in order.
   tile_schedule const sched{pl.m_tiles, pl.n_tiles, n_pes, prm.mode, pl.group_m};
   std::int32_t const reduced_tiles =
       n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
-  prm.n_comm = reduced_tiles * kQuarters * (pl.tile_n / 64);
+  prm.n_comm = reduced_tiles * kQuarters * (via_switch ? 1 : pl.tile_n / 64);
   // Warps per CTA running exchange sub-tasks. The in-switch reduction
   // saturates the fabric with one per SM; more only lengthen its queues and
   // with them every sub-task's latency and the drain at the end (tp = 8, C2:
@@ -380,7 +385,7 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   prm.events = static_cast<std::uint32_t *>(events);
   if (via_switch) {
     prm.mc_workspace = team->mc.alias(workspace);
-    prm.mc_out = reinterpret_cast<__nv_bfloat16 *>(team->mc.alias(out));
+    if (out_symmetric) prm.mc_out = reinterpret_cast<__nv_bfloat16 *>(team->mc.alias(out));
   }
   if (team != nullptr) {
     prm.peers = team->peers;

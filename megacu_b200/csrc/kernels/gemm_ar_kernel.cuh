@@ -90,7 +90,7 @@ struct gemm_ar_params {
   std::int32_t mode;          // mode_allreduce / mode_reduce_scatter
   std::int32_t one_shot;      // 1: every PE reduces every tile
   std::int32_t group_m;
-  std::int32_t n_comm;        // communication sub-tasks (tiles x quarters x blocks)
+  std::int32_t n_comm;        // communication sub-tasks (reduced tiles x quarters)
   std::int32_t comm_warps;    // warps per CTA running them: the last comm_warps of 2..9
   std::int32_t rows_per_pe;   // reduce-scatter: output rows per PE
   std::uint64_t timeout_ns;   // bound of cross-GPU waits
@@ -238,7 +238,7 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], uint4 w) {
 // fences once, and the last worker of this PE announces "all my blocks are
 // written" to every PE (finish_pushes).
 template <int BN, bool kWireF32>
-__device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedule const &sched,
+__device__ __forceinline__ void comm_tasks_peer(gemm_ar_params const &p, tile_schedule const &sched,
                                            std::uint32_t parity, std::uint32_t epoch,
                                            std::uint32_t *my_events,
                                            std::uint32_t const *abort_word, std::uint8_t *xpose,
@@ -302,18 +302,6 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
           acc[h / 2][(h % 2) * 4 + 3] += __uint_as_float(w[h].w);
         }
       }
-    } else if (p.mc_workspace != nullptr) {
-      // One load per vector returns the sum over every PE's slot, reduced in
-      // the NVSwitch (fp32 accumulation, one bf16 rounding): the bf16 values
-      // are exact in fp32, so the packing below reproduces them.
-      char const *mc = p.mc_workspace + in_slot;
-      uint4 w[8];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        w[g] = ptx::multimem_ld_reduce_bf16x8(mc + (cb * 8 + g) * kVecStride);
-      }
-#pragma unroll
-      for (int g = 0; g < 8; ++g) add_bf16x8(acc[g], w[g]);
     } else {
 #pragma unroll 1
       for (std::int32_t src = 0; src < p.n_pes; src += 2) {
@@ -356,22 +344,16 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
     // Every PE's out in two-shot allreduce (one multicast store each with
     // the in-switch reduction; else starting with the next PE, so the PEs
     // spread their stores over the links), this PE's out otherwise.
-    bool const via_switch = !kWireF32 && p.mc_out != nullptr;
-    std::int32_t const n_out = push_all && !via_switch ? p.n_pes : 1;
+    std::int32_t const n_out = push_all ? p.n_pes : 1;
     for (std::int32_t d = 0; d < n_out; ++d) {
       std::int32_t const pe = push_all ? (p.my_pe + 1 + d) % p.n_pes : p.my_pe;
-      __nv_bfloat16 *dst = via_switch ? p.mc_out : push_all ? p.peers.translate(p.out, pe) : p.out;
+      __nv_bfloat16 *dst = push_all ? p.peers.translate(p.out, pe) : p.out;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
         uint4 const q = *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
         if (row0 + rr < p.m && col < p.n) {
-          __nv_bfloat16 *at = dst + static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
-          if (via_switch) {
-            ptx::multimem_st_v4(at, q);
-          } else {
-            ptx::st_v4(at, q);
-          }
+          ptx::st_v4(dst + static_cast<std::int64_t>(out_row0 + rr) * p.n + col, q);
         }
       }
     }
@@ -382,6 +364,115 @@ __device__ __forceinline__ void comm_tasks(gemm_ar_params const &p, tile_schedul
       if (push_all) count(p, ctr_final_publish, p.n_pes);
       trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
     }
+  }
+}
+
+// In-switch reduction worker (task 2 with the workspace in the team's
+// multicast region, bf16 wire): one warp takes sub-tasks = (reduced tile,
+// 32-row quarter) in raster order; the reduced tiles are this PE's own
+// (two-shot allreduce, reduce-scatter) or all of them (one-shot). For each:
+// acquire every PE's arrive flag of the quarter once, then for each 64-column
+// block in order read the sum over every PE's slot with one
+// `multimem.ld_reduce` per 16-byte vector (fp32 accumulation in the NVSwitch,
+// one bf16 rounding), transpose 32 x 64 through `xpose` and store it
+// row-major: in two-shot allreduce with one `multimem.st` per vector into
+// every PE's out, else into this PE's out. Once a block is staged in shared
+// memory the next block's loads are issued, so they are in flight while the
+// block is stored; the next ticket is drawn while the current one runs.
+template <int BN>
+__device__ __forceinline__ void comm_tasks_switch(gemm_ar_params const &p,
+                                                  tile_schedule const &sched,
+                                                  std::uint32_t parity, std::uint32_t epoch,
+                                                  std::uint32_t *my_events,
+                                                  std::uint32_t const *abort_word,
+                                                  std::uint8_t *xpose, std::uint32_t lane) {
+  constexpr int kBlocks = BN / 64;
+  constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * 2;
+  constexpr std::int64_t kVecStride = kBlockM * 16;  // bytes between wire vectors of a row
+  control_block *ctrl = control(p);
+  bool const push_all = p.mode == mode_allreduce && !p.one_shot;  // then p.mc_out is set
+  std::int32_t const g = static_cast<std::int32_t>(lane) % 8;      // 16 B column group of a row
+  std::uint32_t ticket = draw_ticket(&ctrl->reduce_ticket, lane);
+  while (ticket < static_cast<std::uint32_t>(p.n_comm)) {
+    // Draw the next ticket now; its atomic completes while this one runs.
+    std::uint32_t next_raw = 0;
+    if (lane == 0) next_raw = atomicAdd(&ctrl->reduce_ticket, 1u);
+    std::int32_t const j = static_cast<std::int32_t>(ticket) / kQuarters;
+    std::int32_t const quarter = static_cast<std::int32_t>(ticket) % kQuarters;
+    std::int32_t const r = p.one_shot ? j : j * p.n_pes + p.my_pe;
+    tile_coord const c = locate(sched, r);
+    std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+    // Blocks of this quarter that hold output elements: the first `blocks`.
+    std::int32_t blocks = 0;
+#pragma unroll
+    for (int cb = 0; cb < kBlocks; ++cb) {
+      blocks += block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb) ? 1 : 0;
+    }
+    if (blocks == 0) {  // no output element lives in this quarter
+      ticket = __shfl_sync(0xffffffffu, next_raw, 0);
+      continue;
+    }
+    // Task 2 "before": every PE's partial of this quarter is ready.
+    bool ok = true;
+    if (static_cast<std::int32_t>(lane) < p.n_pes) {
+      ok = wait_flag(my_events + arrive_index(parity, lane, tile, quarter, p.n_pes, p.tiles),
+                     epoch, abort_word, p.timeout_ns);
+      if (!ok) record_error(p, err_remote_timeout, tile, lane, 8);
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      break;
+    }
+    __syncwarp();  // orders every lane's loads after the lanes' acquires
+    std::uint64_t const t0 = ptx::now_ns();
+    // Lane = row of the quarter; vector (v, row) of a slot at (v * 128 + row) * 16.
+    char const *mc = p.mc_workspace + slot_offset(parity, tile, p.tiles, kSlotBytes) +
+                     (static_cast<std::int64_t>(quarter) * 32 + lane) * 16;
+    std::int32_t const row0 = c.tile_row * kBlockM + quarter * 32;
+    std::int32_t const out_row0 =
+        p.mode == mode_reduce_scatter ? row0 - c.owner * p.rows_per_pe : row0;
+    uint4 w[8];
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg) w[gg] = ptx::multimem_ld_reduce_bf16x8(mc + gg * kVecStride);
+#pragma unroll 1
+    for (int cb = 0; cb < blocks; ++cb) {
+      // Row `lane` of the block -> shared memory, 16 B per 8 columns,
+      // XOR-swizzled so that both the write and the read are conflict-free.
+#pragma unroll
+      for (int gg = 0; gg < 8; ++gg) {
+        *reinterpret_cast<uint4 *>(xpose + lane * 128 + ((gg ^ (lane & 7)) * 16)) = w[gg];
+      }
+      __syncwarp();
+      if (cb + 1 < blocks) {
+#pragma unroll
+        for (int gg = 0; gg < 8; ++gg) {
+          w[gg] = ptx::multimem_ld_reduce_bf16x8(mc + ((cb + 1) * 8 + gg) * kVecStride);
+        }
+      }
+      // Read back row-major: 8 lanes cover one 128 B row segment.
+      std::int32_t const col = c.tile_col * BN + cb * 64 + g * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        std::int32_t const rr = i * 4 + static_cast<std::int32_t>(lane) / 8;
+        uint4 const q =
+            *reinterpret_cast<uint4 const *>(xpose + rr * 128 + ((g ^ (rr & 7)) * 16));
+        if (row0 + rr < p.m && col < p.n) {
+          std::int64_t const at = static_cast<std::int64_t>(out_row0 + rr) * p.n + col;
+          if (push_all) {
+            ptx::multimem_st_v4(p.mc_out + at, q);
+          } else {
+            ptx::st_v4(p.out + at, q);
+          }
+        }
+      }
+      __syncwarp();  // every lane has read xpose before the next block writes it
+    }
+    if (lane == 0) {
+      count(p, ctr_reduce_tasks, static_cast<unsigned long long>(blocks));
+      count(p, ctr_partial_acquire, static_cast<unsigned long long>(blocks) * p.n_pes);
+      if (push_all) count(p, ctr_final_publish, static_cast<unsigned long long>(blocks) * p.n_pes);
+      trace(p, 2, static_cast<std::uint32_t>(quarter), ticket, tile, t0);
+    }
+    ticket = __shfl_sync(0xffffffffu, next_raw, 0);
   }
 }
 
@@ -1117,14 +1208,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         detail::wait_all_reads(p, epoch, my_events, gw, abort_word, lane);
       }
     }
-  } else if (p.n_pes > 1 && warp >= first_comm_warp) {
-    int const worker = warp - kEpilogueWarp0;  // 0..7
-    std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
-    detail::comm_tasks<BN, kWireF32>(p, sched, parity, epoch, my_events, abort_word, xpose, lane);
-    if (p.mode == mode_allreduce && !p.one_shot) {
-      detail::finish_pushes(p, parity, epoch, my_events, lane);
-      if (blockIdx.x == 0 && warp == first_comm_warp) {
-        detail::wait_all_pushes(p, parity, epoch, my_events, abort_word, lane);
+  } else if constexpr (!kSwiGLU) {  // the SwiGLU variant runs on one PE: no exchange
+    if (p.n_pes > 1 && warp >= first_comm_warp) {
+      int const worker = warp - kEpilogueWarp0;  // 0..7
+      std::uint8_t *xpose = reduce_smem + worker * (32 * 128);
+      if constexpr (!kWireF32) {
+        if (p.mc_workspace != nullptr) {
+          detail::comm_tasks_switch<BN>(p, sched, parity, epoch, my_events, abort_word, xpose,
+                                        lane);
+        } else {
+          detail::comm_tasks_peer<BN, false>(p, sched, parity, epoch, my_events, abort_word,
+                                             xpose, lane);
+        }
+      } else {
+        detail::comm_tasks_peer<BN, true>(p, sched, parity, epoch, my_events, abort_word, xpose,
+                                          lane);
+      }
+      if (p.mode == mode_allreduce && !p.one_shot) {
+        detail::finish_pushes(p, parity, epoch, my_events, lane);
+        if (blockIdx.x == 0 && warp == first_comm_warp) {
+          detail::wait_all_pushes(p, parity, epoch, my_events, abort_word, lane);
+        }
       }
     }
   }

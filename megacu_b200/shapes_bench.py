@@ -42,8 +42,9 @@ reference. A failed check makes the run exit non-zero.
 (launch overhead out of the measurement; an arm whose capture fails is timed
 as launched and marked so). ``--algo one|two`` forces the allreduce exchange
 of config 4 (auto picks one-shot for one tile row), and ``--multicast`` puts
-a two-shot call's workspace and output in the team's multicast region (the
-in-switch reduction).
+the workspace and output in the team's multicast region: the in-switch
+reduction (each block's sum over the PEs read with one load through the
+NVSwitch; a two-shot allreduce also stores through it).
 """
 from __future__ import annotations
 
@@ -69,12 +70,20 @@ def roofline(config, m, n, k, tp, us, one_shot=True, in_switch=False):
     hbm, hbm_src = hbm_peak()
     flops = 2.0 * m * n * k
     out_bytes = m * n * 2
-    if config == 3:
+    # Bytes a PE moves in its busier NVLink direction. Through the switch a
+    # reducer's load reads every PE's slot, the requester's own included.
+    if config == 3 and in_switch:
+        link = out_bytes                          # every partial tile read once by its owner
+        link_kind = "in-switch reduce-scatter 1 x output"
+    elif config == 3:
         link = (tp - 1) / tp * out_bytes          # reduce-scatter bus bytes
         link_kind = "reduce-scatter (tp-1)/tp x output"
     elif config == "ag":
         link = (tp - 1) / tp * m * k * 2          # the other PEs' shards of A, received
         link_kind = "all-gather (tp-1)/tp x A"
+    elif one_shot and in_switch:
+        link = tp * out_bytes                     # every PE reads every PE's partial
+        link_kind = "in-switch one-shot tp x output"
     elif one_shot:
         link = (tp - 1) * out_bytes               # one-shot: every partial to every peer
         link_kind = "one-shot (tp-1) x output"
@@ -141,7 +150,7 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
     ws_bytes = max(mb.workspace_bytes(prob, tp), 16)
     ev_bytes = mb.events_bytes(prob, tp)
     rows = m // tp if config == 3 else m
-    want_mc = (args.multicast and tp > 1 and mode == mb.MODE_ALLREDUCE and not pl.one_shot)
+    want_mc = args.multicast and tp > 1
     team = team_cache(ws_bytes + ev_bytes + rows * n * 2 + (64 << 20),
                       (ws_bytes + rows * n * 2 + (1 << 20)) if want_mc else 0)
     use_mc = want_mc and team.multicast
@@ -398,7 +407,7 @@ def main() -> int:
     ap.add_argument("--algo", choices=("auto", "one", "two"), default="auto",
                     help="config 4: the allreduce exchange (auto: one-shot for one tile row)")
     ap.add_argument("--multicast", action="store_true",
-                    help="two-shot calls reduce in the switch (team multicast region)")
+                    help="reduce in the switch (workspace and out in the team multicast region)")
     ap.add_argument("--graph", action="store_true",
                     help="time each arm as the replay of a CUDA graph captured from it")
     ap.add_argument("--heat-calls", type=int, default=-1,

@@ -256,7 +256,9 @@ int oracle_bf16_call(const oracle_bf16_problem *p, const float *const *a,
     for (int32_t me = 0; me < np && rc == 0; ++me) {
       /* Task 2 queue: every (reduced tile, 32-row quarter, 64-column block),
        * the reduced tiles being this PE's own (two-shot, reduce-scatter) or
-       * all of them (one-shot), in raster order. */
+       * all of them (one-shot), in raster order. (The kernel's queue hands
+       * out (tile, quarter) tickets and reduces their blocks in order: the
+       * same sequence.) */
       int32_t const reduced = p->one_shot ? tiles : (tiles > me ? (tiles - me + np - 1) / np : 0);
       for (int32_t ticket = 0; ticket < reduced * per_tile && rc == 0; ++ticket) {
         int32_t const j = ticket / per_tile;

@@ -36,6 +36,10 @@ CASES = [
     (512, 1024, 256, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0, True),
     (384, 520, 136, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 0, True),  # ragged m, n
     (768, 1024, 200, mb.MODE_ALLREDUCE, mb.ALGO_TWO_SHOT, False, 256, True),  # CTA pairs
+    (64, 2048, 512, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0, True),  # one-shot (decode)
+    (300, 1000, 200, mb.MODE_ALLREDUCE, mb.ALGO_ONE_SHOT, False, 0, True),  # one-shot, ragged
+    (1024, 768, 320, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 0, True),
+    (1024, 512, 128, mb.MODE_REDUCE_SCATTER, mb.ALGO_AUTO, False, 256, True),  # RS, CTA pairs
 ]
 MULTICAST_BYTES = 1 << 29
 
@@ -93,9 +97,9 @@ def main() -> int:
             failures.append(f"case {idx}: counters {counters} != {2 * ref['counters'][rank]}")
         dist.barrier()
     if team.multicast:
-        # Buffers in the multicast region of a call that cannot reduce in the
-        # switch (one-shot) are refused before any launch.
-        prob = mb.Problem(64, 2048, 64, algo=mb.ALGO_ONE_SHOT)
+        # A workspace in the multicast region of a call that cannot reduce in
+        # the switch (fp32 partials on the wire) is refused before any launch.
+        prob = mb.Problem(64, 2048, 64, algo=mb.ALGO_ONE_SHOT, deterministic=True)
         ws = team.tensor((mb.workspace_bytes(prob, world),), torch.uint8, multicast=True)
         ev = team.tensor((mb.events_bytes(prob, world) // 4,), torch.int32)
         out = team.tensor((64, 2048), torch.bfloat16, multicast=True)
@@ -104,10 +108,10 @@ def main() -> int:
         try:
             mb.gemm_allreduce(a, b, out, workspace=ws, events=ev, problem=prob, stream=stream,
                               device=local, team=team)
-            failures.append("one-shot call with multicast buffers was not refused")
+            failures.append("fp32-wire call with multicast buffers was not refused")
         except mb.MegacuError as err:
             if err.detail != 28:
-                failures.append(f"one-shot call with multicast buffers: {err}")
+                failures.append(f"fp32-wire call with multicast buffers: {err}")
     torch.cuda.synchronize()
     dist.barrier()
     team.close()
