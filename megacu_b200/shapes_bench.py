@@ -410,6 +410,9 @@ def main() -> int:
                     help="reduce in the switch (workspace and out in the team multicast region)")
     ap.add_argument("--graph", action="store_true",
                     help="time each arm as the replay of a CUDA graph captured from it")
+    ap.add_argument("--k-total", type=int, default=0,
+                    help="configs 3 and 4: the total K split over the PEs (default the "
+                         "config's 28672); e.g. 3584 on one GPU is one PE's GEMM at tp = 8")
     ap.add_argument("--heat-calls", type=int, default=-1,
                     help="untimed calls of the fused and unfused arms before timing "
                          "(default: about two seconds of work)")
@@ -442,13 +445,13 @@ def main() -> int:
         if args.config == "ag":
             ok = run_allgather(args, rank, world, local, team_cache)
         elif args.config == "3":
-            ok = run_shape(args, 3, C3["m"], C3["n"], C3["k_total"], rank, world, local,
-                           team_cache)
+            ok = run_shape(args, 3, C3["m"], C3["n"], args.k_total or C3["k_total"], rank,
+                           world, local, team_cache)
         else:
             ms = [int(x) for x in args.m.split(",") if x] or list(C4["m"])
             for m in ms:
-                ok = run_shape(args, 4, m, C4["n"], C4["k_total"], rank, world, local,
-                               team_cache) and ok
+                ok = run_shape(args, 4, m, C4["n"], args.k_total or C4["k_total"], rank,
+                               world, local, team_cache) and ok
         for t in teams:
             t.close()
     finally:
