@@ -257,6 +257,22 @@ def tensor_from_pointer(ptr: int, shape, dtype, device: int, owner=None):
 
 # ---- driver views ------------------------------------------------------------------
 
+_VIEWS: dict = {}  # (stream handle, device) -> DriverView of a one-PE call
+
+
+def _launch_view(stream, device: int, team: Optional[Team]) -> DriverView:
+    """driver_view() for the launch wrappers below, built once per (stream,
+    device) and team: the struct is passed by value, so the cached object is
+    never changed by a call. (driver_view itself returns a fresh struct, which
+    callers may modify.)"""
+    key = (_stream_handle(stream), device)
+    cache = _VIEWS if team is None else team.__dict__.setdefault("_views", {})
+    d = cache.get(key)
+    if d is None:
+        d = cache[key] = driver_view(stream, device, team)
+    return d
+
+
 def driver_view(stream=None, device: int = 0, team: Optional[Team] = None) -> DriverView:
     """megacu's driver_view{launch_view, team_view} for this PE."""
     d = DriverView()
@@ -287,14 +303,27 @@ class Problem:
     timeout_ns: int = 0
     cta_pairs: int = _capi.CTA_PAIRS_AUTO
 
+    def __setattr__(self, name, value):
+        object.__setattr__(self, name, value)
+        self.__dict__.pop("_c", None)  # a changed field rebuilds the C struct
+
     def to_c(self, trace_ptr: Optional[int] = None, trace_capacity: int = 0) -> GemmArProblemV2:
-        return GemmArProblemV2(m=self.m, n=self.n, k=self.k, tile_m=0, tile_n=self.tile_n,
-                               mode=self.mode, algo=self.algo,
-                               deterministic=1 if self.deterministic else 0,
-                               dtype=_capi.DTYPE_BF16, num_ctas=self.num_ctas,
-                               cta_pairs=self.cta_pairs,
-                               timeout_ns=self.timeout_ns, trace=trace_ptr,
-                               trace_capacity=trace_capacity)
+        """The C struct (passed by value). Without a trace it is built once and
+        reused until a field changes."""
+        if trace_ptr is None and trace_capacity == 0:
+            c = self.__dict__.get("_c")
+            if c is not None:
+                return c
+        c = GemmArProblemV2(m=self.m, n=self.n, k=self.k, tile_m=0, tile_n=self.tile_n,
+                            mode=self.mode, algo=self.algo,
+                            deterministic=1 if self.deterministic else 0,
+                            dtype=_capi.DTYPE_BF16, num_ctas=self.num_ctas,
+                            cta_pairs=self.cta_pairs,
+                            timeout_ns=self.timeout_ns, trace=trace_ptr,
+                            trace_capacity=trace_capacity)
+        if trace_ptr is None and trace_capacity == 0:
+            self.__dict__["_c"] = c
+        return c
 
 
 def workspace_bytes(problem: Problem, n_pes: int) -> int:
@@ -361,7 +390,7 @@ def gemm_allreduce(a, b, out, *, workspace, events, problem: Problem, stream=Non
     """
     trace_ptr = _ptr(trace)
     cap = trace.numel() // 4 if trace is not None else 0
-    d = driver_view(stream, device, team)
+    d = _launch_view(stream, device, team)
     p = problem.to_c(trace_ptr, cap)
     args = (d, _ptr(a), _ptr(b), _ptr(workspace), _ptr(out), _ptr(events), p)
     if orchestrate:
@@ -386,7 +415,7 @@ def allgather_gemm(a_shard, b, gathered, out, *, events, problem: Problem, strea
     problem.mode = _capi.MODE_ALLGATHER
     trace_ptr = _ptr(trace)
     cap = trace.numel() // 4 if trace is not None else 0
-    d = driver_view(stream, device, team)
+    d = _launch_view(stream, device, team)
     check(lib().megacu_cuda_allgather_gemm_bf16(d, _ptr(a_shard), _ptr(b), _ptr(gathered),
                                                  _ptr(out), _ptr(events),
                                                  problem.to_c(trace_ptr, cap)))
@@ -406,8 +435,8 @@ def gemm_swiglu(x, w_gate, w_up, act, *, events, problem: Problem, stream=None,
     tokens, n = act columns, k = hidden."""
     trace_ptr = _ptr(trace)
     cap = trace.numel() // 4 if trace is not None else 0
-    check(lib().megacu_cuda_gemm_swiglu_bf16(driver_view(stream, device), _ptr(x), _ptr(w_gate),
-                                             _ptr(w_up), _ptr(act), _ptr(events),
+    check(lib().megacu_cuda_gemm_swiglu_bf16(_launch_view(stream, device, None), _ptr(x),
+                                             _ptr(w_gate), _ptr(w_up), _ptr(act), _ptr(events),
                                              problem.to_c(trace_ptr, cap)))
 
 
@@ -452,7 +481,7 @@ def mlp_chain(x, w_gate, w_up, w_down, out, *, act, workspace, x_work, events_sw
     if not (len(w_gate) == len(w_up) == len(w_down) == n):
         raise ValueError("one gate, up and down weight per layer")
     arr = lambda ws: (ctypes.c_void_p * n)(*[_ptr(w) for w in ws])
-    check(lib().megacu_cuda_mlp_chain_bf16(driver_view(stream, device, team), _ptr(x),
+    check(lib().megacu_cuda_mlp_chain_bf16(_launch_view(stream, device, team), _ptr(x),
                                            arr(w_gate), arr(w_up), arr(w_down), _ptr(act),
                                            _ptr(workspace), _ptr(x_work), _ptr(out),
                                            _ptr(events_swiglu), _ptr(events_down),

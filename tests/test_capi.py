@@ -251,3 +251,17 @@ def test_ctypes_struct_layouts_match_the_c_header(tmp_path):
     got = [int(x) for x in subprocess.run([exe], capture_output=True, text=True,
                                           check=True).stdout.split()]
     assert got == want
+
+
+def test_problem_struct_is_rebuilt_after_a_field_changes():
+    """Problem.to_c caches the C struct of a call without a trace; changing a
+    field must rebuild it, and a traced call always gets a fresh one."""
+    p = mb.Problem(256, 512, 128)
+    first = p.to_c()
+    assert p.to_c() is first
+    p.tile_n = 128
+    again = p.to_c()
+    assert again is not first and again.tile_n == 128 and first.tile_n == 0
+    traced = p.to_c(0x1000, 4)
+    assert traced.trace == 0x1000 and traced.trace_capacity == 4 and p.to_c() is again
+    assert p == mb.Problem(256, 512, 128, tile_n=128)  # equality still compares fields only
