@@ -111,7 +111,8 @@ def roofline(config, m, n, k, tp, us, one_shot=True, in_switch=False):
 def as_graphs(arms, names, stream):
     """CUDA-graph versions of the arms (each captured from one call after the
     warm-up); an arm that cannot be captured stays as it is. Returns the arms
-    and, per arm, whether it is a graph replay."""
+    and, per arm, whether it is a graph replay. The arms launch on the current
+    stream, which inside the capture is the capturing stream."""
     import torch
 
     out, graphed = [], {}
@@ -162,8 +163,9 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def fused():
-        mb.gemm_allreduce(a, b, out, workspace=ws, events=events, problem=prob, stream=stream,
-                          device=local, team=team if tp > 1 else None)
+        mb.gemm_allreduce(a, b, out, workspace=ws, events=events, problem=prob,
+                          stream=torch.cuda.current_stream(), device=local,
+                          team=team if tp > 1 else None)
 
     def unfused():
         torch.matmul(a, b, out=c)
@@ -186,7 +188,7 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
 
         def kernel_without_exchange():
             mb.gemm_allreduce(a, b, solo_out, workspace=None, events=solo_events,
-                              problem=solo_prob, stream=stream, device=local)
+                              problem=solo_prob, stream=torch.cuda.current_stream(), device=local)
 
         arms.append(kernel_without_exchange)
         names.append("kernel_without_exchange")
@@ -309,7 +311,8 @@ def run_allgather(args, rank, world, local, team_cache):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     def fused():
-        mb.allgather_gemm(shard, b, gathered, out, events=events, problem=prob, stream=stream,
+        mb.allgather_gemm(shard, b, gathered, out, events=events, problem=prob,
+                          stream=torch.cuda.current_stream(),
                           device=local, team=team if tp > 1 else None)
 
     def unfused():
@@ -332,7 +335,7 @@ def run_allgather(args, rank, world, local, team_cache):
 
         def kernel_without_exchange():
             mb.gemm_allreduce(g_nccl, b, solo_out, workspace=None, events=solo_events,
-                              problem=solo_prob, stream=stream, device=local)
+                              problem=solo_prob, stream=torch.cuda.current_stream(), device=local)
 
         arms.append(kernel_without_exchange)
         names.append("kernel_without_exchange")
