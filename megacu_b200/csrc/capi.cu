@@ -150,6 +150,48 @@ std::int32_t sched_mode(std::int32_t mode) {
 constexpr std::int32_t kPlanSms = 148;  // plans must not depend on the local device
 constexpr std::int32_t kSwitchCommWarps = 1;
 
+// One tile row (m <= 128, e.g. decode shapes): every CTA runs all of K for
+// its tile, and a tcgen05.mma of a narrow tile costs about as much as a wide
+// one, so the time goes with the k-blocks per CTA. The tile width and K split
+// (gemm_ar_params::k_split: 1 or 2 CTAs per tile, a cluster) chosen here
+// keep the most of `sms` SMs busy, then split K. A split needs two k-blocks
+// per CTA at least, and the other rank's accumulator rows (active 32-row
+// quarters x tile_n fp32) must fit rank 0's stage ring. (Measured on one
+// B200 at M 16-128, N 8192, K 3584, CUDA-graph replays: tile_n 128 split in
+// two 28.8-30.7 us, tile_n 64 unsplit 30.7 us, tile_n 256 split in four
+// 32.8-36.9 us: the four-way reduction and the HBM contention of four CTAs
+// streaming one column panel cost more than they save.)
+struct row_split {
+  std::int32_t tile_n;
+  std::int32_t k_split;
+};
+
+row_split one_row_split(std::int64_t m, std::int64_t n, std::int64_t k, std::int32_t sms,
+                        std::int32_t tile_n) {
+  std::int64_t const rows = m < kBlockM ? m : kBlockM;
+  std::int64_t const quarters = (rows + 31) / 32;
+  std::int64_t const k_blocks = (k + kBlockK - 1) / kBlockK;
+  row_split best{tile_n != 0 ? tile_n : 64, 1};
+  std::int64_t best_ctas = -1;
+  for (std::int32_t tn : {256, 128, 64}) {
+    if (tile_n != 0 && tn != tile_n) continue;
+    std::int64_t const tiles = (n + tn - 1) / tn;
+    for (std::int32_t ks : {2, 1}) {
+      bool const fits =
+          ks == 1 || (tiles * ks <= sms && k_blocks >= 2 * ks &&
+                      (ks - 1) * quarters * 32 * tn * 4 <= gemm_config<64>::ring_bytes);
+      if (!fits) continue;
+      std::int64_t const ctas = (tiles < sms ? tiles : sms) * ks;
+      if (ctas > best_ctas || (ctas == best_ctas && ks > best.k_split)) {
+        best = {tn, ks};
+        best_ctas = ctas;
+      }
+      break;  // the largest split that fits this width
+    }
+  }
+  return best;
+}
+
 megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, bf16_plan &out) {
   if (p.m <= 0 || p.n <= 0 || p.k <= 0) {
     return fail(MEGACU_INVALID_ARGUMENT, 1, "invalid problem");
@@ -186,6 +228,8 @@ megacu_status make_plan(megacu_gemm_ar_problem_v2 const &p, std::int32_t n_pes, 
       return fail(MEGACU_UNSUPPORTED, 22, "tile_n must be 0, 64, 128 or 256");
     }
     pl.tile_n = p.tile_n;
+  } else if (pl.m_tiles == 1 && p.mode != MEGACU_MODE_ALLGATHER) {
+    pl.tile_n = one_row_split(p.m, p.n, p.k, kPlanSms, 0).tile_n;
   } else {
     pl.tile_n = 64;
     for (std::int32_t cand : {256, 128}) {
@@ -345,13 +389,19 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
     return fail(MEGACU_INVALID_ARGUMENT, 24, "team was created on another device");
   }
 
+  // One tile row (m < 128, decode shapes): each load brings only the rows of
+  // A that exist (rounded up to 8), so the ring holds more, smaller stages.
+  std::int32_t const a_box_rows =
+      (problem.m < kBlockM && !pl.pairs) ? static_cast<std::int32_t>((problem.m + 7) / 8 * 8)
+                                         : kBlockM;
   CUtensorMap map_a, map_b;
-  if (!encode_bf16_map(&map_a, a, problem.m, problem.k, kBlockM) ||
+  if (!encode_bf16_map(&map_a, a, problem.m, problem.k, static_cast<std::uint32_t>(a_box_rows)) ||
       !encode_bf16_map(&map_b, b, problem.k, problem.n, kBlockK)) {
     return fail(MEGACU_BACKEND_ERROR, 30, "cuTensorMapEncodeTiled failed");
   }
 
   gemm_ar_params prm{};
+  prm.a_box_rows = a_box_rows;
   prm.m = static_cast<std::int32_t>(problem.m);
   prm.n = static_cast<std::int32_t>(problem.n);
   prm.k = static_cast<std::int32_t>(problem.k);
@@ -397,6 +447,9 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   prm.trace_capacity = problem.trace != nullptr ? problem.trace_capacity : 0;
 
   int grid = problem.num_ctas > 0 ? problem.num_ctas : sm_count(device);
+  if (pl.m_tiles == 1 && !pl.pairs && problem.num_ctas <= 0) {
+    prm.k_split = one_row_split(problem.m, problem.n, problem.k, grid, pl.tile_n).k_split;
+  }
   auto stream = static_cast<cudaStream_t>(driver.launch.stream);
   bool const f32 = pl.wire_bytes == 4;
   e = launch_bf16_plan(f32, pl.tile_n, pl.pairs != 0, device, grid, stream, map_a, map_b, prm);

@@ -75,11 +75,20 @@ struct gemm_config {
   // Bytes one stage's full barrier waits for (the leader's counts both CTAs).
   static constexpr int tx_bytes = kPair ? 2 * stage_bytes : stage_bytes;
   static constexpr int stages = (192 * 1024) / stage_bytes;    // 4 / 6 / 8; pairs 8 / 6
+  static constexpr int ring_bytes = stages * stage_bytes;      // 192 KiB
+  // One CTA per tile with fewer A rows than 128 (one tile row, m < 128): each
+  // TMA load brings only the first a_box_rows rows of A, a stage shrinks to
+  // a_box_rows * 128 B + b_bytes, and up to max_stages such stages fit the
+  // same ring (the MMA still reads 128 rows; rows past a_box_rows hold
+  // whatever lies there and only produce accumulator rows that are never
+  // stored).
+  static constexpr int max_stages = kPair ? stages : 24;
   static constexpr int col_blocks = BN / 64;                   // sub-tasks per quarter
   static constexpr int reduce_bytes = kWorkerWarps * 32 * 128; // transpose tiles
-  static constexpr int n_barriers = 2 * stages + 4 + 2 * kTaskRing + 1;
+  static constexpr int n_barriers = 2 * max_stages + 4 + 2 * kTaskRing + 3;
   static constexpr int aux_bytes = n_barriers * 8 + kTaskRing * 4 + 16;
-  static constexpr int smem_bytes = 1024 + stages * stage_bytes + reduce_bytes + aux_bytes;
+  static constexpr int smem_bytes = 1024 + ring_bytes + reduce_bytes + aux_bytes;
+  static_assert(smem_bytes <= 232448, "dynamic shared memory per CTA");
   static constexpr int tmem_columns = 2 * BN;
 };
 
@@ -112,6 +121,16 @@ struct gemm_ar_params {
   __nv_bfloat16 *gathered;
   std::int32_t chunk_rows;
   std::int32_t chunks_per_block;
+  // Rows of A one TMA load brings: 0 or 128 = a whole tile; fewer (a
+  // multiple of 8, covering m) for one tile row without CTA pairs, so that
+  // more, smaller stages hide the load latency (map_a's box has this height).
+  std::int32_t a_box_rows;
+  // 0 or 1: one CTA per tile. 2 or 4 (one tile row, no CTA pairs, launched as
+  // clusters of that size, at most one tile per cluster): the cluster's CTAs
+  // compute the same tile over consecutive ranges of K and rank 0 adds the
+  // others' accumulators (received in its stage ring through distributed
+  // shared memory) before its epilogue.
+  std::int32_t k_split;
 };
 
 namespace detail {
@@ -726,16 +745,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::uint32_t const raw_addr = ptx::smem_addr(smem_raw);
   std::uint8_t *smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   std::uint8_t *stages = smem;
-  std::uint8_t *reduce_smem = smem + cfg::stages * cfg::stage_bytes;
+  std::uint8_t *reduce_smem = smem + cfg::ring_bytes;
   auto *bars = reinterpret_cast<std::uint64_t *>(reduce_smem + cfg::reduce_bytes);
   std::uint64_t *full = bars;
-  std::uint64_t *empty = full + cfg::stages;
-  std::uint64_t *acc_full = empty + cfg::stages;
+  std::uint64_t *empty = full + cfg::max_stages;
+  std::uint64_t *acc_full = empty + cfg::max_stages;
   std::uint64_t *acc_empty = acc_full + 2;
   std::uint64_t *task_full = acc_empty + 2;
   std::uint64_t *task_empty = task_full + kTaskRing;
   std::uint64_t *mma_done = task_empty + kTaskRing;
-  auto *ring = reinterpret_cast<std::int32_t volatile *>(mma_done + 1);
+  std::uint64_t *ring_free = mma_done + 1;  // K split: rank 0's stage ring may be written
+  std::uint64_t *recv_full = ring_free + 1; // K split: the other ranks' accumulators arrived
+  auto *ring = reinterpret_cast<std::int32_t volatile *>(recv_full + 1);
   auto *tmem_slot = reinterpret_cast<std::uint32_t *>(const_cast<std::int32_t *>(ring) + kTaskRing);
   auto *epoch_slot = tmem_slot + 1;
 
@@ -759,13 +780,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tile_of = [&](std::int32_t q) {
     return kPair ? pair_raster(sched, q, static_cast<std::int32_t>(cta_rank)) : q;
   };
+  // Stage ring: rows of A per load, bytes per stage and stages (see
+  // gemm_config::max_stages); stage bases stay 1024-byte aligned.
+  std::int32_t const a_rows = (!kPair && p.a_box_rows > 0) ? p.a_box_rows : kBlockM;
+  std::uint32_t const a_bytes = static_cast<std::uint32_t>(a_rows) * 128u;
+  std::uint32_t const stage_bytes = kPair ? cfg::stage_bytes : a_bytes + cfg::b_bytes;
+  std::uint32_t const n_stages =
+      kPair ? cfg::stages
+            : (cfg::ring_bytes / stage_bytes < static_cast<std::uint32_t>(cfg::max_stages)
+                   ? cfg::ring_bytes / stage_bytes
+                   : static_cast<std::uint32_t>(cfg::max_stages));
+  std::uint32_t const tx_bytes = kPair ? cfg::tx_bytes : stage_bytes;
+  // K split over a cluster (gemm_ar_params::k_split): this CTA's rank and its
+  // k-blocks [kb_begin, kb_end) (the host keeps k_blocks >= k_split).
+  std::int32_t const k_split = (!kPair && p.k_split > 1) ? p.k_split : 1;
+  std::uint32_t const split_rank = k_split > 1 ? ptx::cluster_ctarank() : 0u;
+  std::int32_t const kb_begin = static_cast<std::int32_t>(split_rank) * k_blocks / k_split;
+  std::int32_t const kb_end = (static_cast<std::int32_t>(split_rank) + 1) * k_blocks / k_split;
 
   if (threadIdx.x == 0) {
     // Arrivals per phase. Pairs: the leader's acc_empty also counts the
     // follower's 4 epilogue warps, its task_empty the follower's 4 epilogue
     // warps and producer; the follower's own empty / acc_full / task_full
     // are arrived by the leader (one each).
-    for (int s = 0; s < cfg::stages; ++s) {
+    for (std::uint32_t s = 0; s < n_stages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
@@ -778,6 +816,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(&task_empty[i], kPair ? 10 : 5);
     }
     ptx::mbar_init(mma_done, 1);
+    if (k_split > 1) {
+      ptx::mbar_init(ring_free, 1);                            // rank 0's one arrive
+      ptx::mbar_init(recv_full, 4 * static_cast<std::uint32_t>(k_split - 1));  // epilogue warps
+    }
     ptx::fence_barrier_init();
     *epoch_slot = ptx::ld_relaxed_gpu(&ctrl->launch_count) + 1u;
     ptx::prefetch_tensor_map(&map_a);
@@ -795,8 +837,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   ptx::tc_fence_before_sync();
   __syncthreads();
-  if constexpr (kPair) {
-    ptx::cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  if (kPair || k_split > 1) {
+    ptx::cluster_sync();  // every CTA's barriers are initialised before any remote arrive
   }
   ptx::tc_fence_after_sync();
   std::uint32_t const tmem_base = *tmem_slot;
@@ -821,6 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- task fetcher + TMA producer ----------------
     if (lane == 0) {
       std::uint32_t it = 0;
+      std::uint32_t stage = 0, phase = 0;  // it % n_stages, (it / n_stages) & 1
       bool ok = true;
       for (std::uint32_t n = 0; ok; ++n) {
         std::uint32_t const slot = n % kTaskRing;
@@ -833,9 +876,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             detail::record_error(p, err_local_timeout, 0, 0, 1);
             break;
           }
-          std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
-          q = ticket < static_cast<std::uint32_t>(gemm_units) ? static_cast<std::int32_t>(ticket)
-                                                              : -1;
+          if (k_split > 1) {
+            // K split: cluster c computes tile c, once (the host launches a
+            // cluster for every tile).
+            std::int32_t const cluster = static_cast<std::int32_t>(blockIdx.x) / k_split;
+            q = (n == 0 && cluster < gemm_units) ? cluster : -1;
+          } else {
+            std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
+            q = ticket < static_cast<std::uint32_t>(gemm_units) ? static_cast<std::int32_t>(ticket)
+                                                                : -1;
+          }
           ring[slot] = q;
           if constexpr (kPair) {
             ptx::st_shared_remote(ptx::map_to_rank(const_cast<std::int32_t *>(&ring[slot]), 1), q);
@@ -897,27 +947,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (cta_rank == 0) detail::count(p, ctr_partial_acquire, kPair ? 2 : 1);
           }
         }
-        for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
-          std::uint32_t const s = it % cfg::stages;
-          if (!bar_wait<kPair>(&empty[s], ((it / cfg::stages) & 1u) ^ 1u, abort_word,
+        for (std::int32_t kb = kb_begin; kb < kb_end; ++kb, ++it) {
+          std::uint32_t const s = stage;
+          if (!bar_wait<kPair>(&empty[s], phase ^ 1u, abort_word,
                                pipe_timeout)) {
             detail::record_error(p, err_local_timeout, r, 0, 2);
             ok = false;
             break;
           }
-          std::uint8_t *sa = stages + s * cfg::stage_bytes;
-          std::uint8_t *sb = sa + cfg::a_bytes;
+          std::uint8_t *sa = stages + s * stage_bytes;
+          std::uint8_t *sb = sa + a_bytes;
           if constexpr (kPair) {
             // The pair MMAs that freed this stage read the follower's copy
             // too: pass the event on (from the second use of the stage on).
             // Relaxed: the event orders async-proxy work only (MMA reads
             // complete, then the follower's TMA overwrites), and the arrive
             // follows this thread's acquire of the MMA's commit.
-            if (leader && it >= static_cast<std::uint32_t>(cfg::stages)) {
+            if (leader && it >= n_stages) {
               ptx::mbar_arrive_remote_relaxed(ptx::map_to_rank(&empty[s], 1));
             }
             std::uint32_t const bar = ptx::map_to_rank(&full[s], 0);
-            if (leader) ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
+            if (leader) ptx::mbar_arrive_expect_tx(&full[s], tx_bytes);
             ptx::tma_load_2d_pair(amap, bar, sa, kb * kBlockK, a_row);
 #pragma unroll
             for (int panel = 0; panel < cfg::b_cols / 64; ++panel) {
@@ -925,7 +975,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     b_col0 + panel * 64, kb * kBlockK);
             }
           } else {
-            ptx::mbar_arrive_expect_tx(&full[s], cfg::tx_bytes);
+            ptx::mbar_arrive_expect_tx(&full[s], tx_bytes);
             ptx::tma_load_2d(amap, &full[s], sa, kb * kBlockK, a_row);
 #pragma unroll
             for (int panel = 0; panel < BN / 64; ++panel) {
@@ -936,6 +986,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                kb * kBlockK);
             }
           }
+          if (++stage == n_stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
       // Drain: the most recent load of every stage must have landed before
@@ -943,9 +997,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // follower's loads complete on the leader's barriers; the leader's
       // drain covers them, and the follower cannot exit before the leader
       // reaches the closing cluster barrier.
-      for (std::uint32_t back = 1; leader && back <= cfg::stages && back <= it; ++back) {
+      for (std::uint32_t back = 1; leader && back <= n_stages && back <= it; ++back) {
         std::uint32_t const i = it - back;
-        bar_wait<kPair>(&full[i % cfg::stages], (i / cfg::stages) & 1u, nullptr);
+        bar_wait<kPair>(&full[i % n_stages], (i / n_stages) & 1u, nullptr);
       }
     }
     __syncwarp();
@@ -955,7 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // holds its half of the TMEM allocation.)
     if (lane == 0 && leader) {
       std::uint32_t const idesc = ptx::idesc_bf16_f32(kPair ? 2 * kBlockM : kBlockM, BN, true);
-      std::uint32_t it = 0;
+      std::uint32_t stage = 0, phase = 0;  // position in the stage ring
       for (std::uint32_t n = 0;; ++n) {
         std::uint32_t const slot = n % kTaskRing;
         if (!ptx::mbar_wait(&task_full[slot], (n / kTaskRing) & 1u, abort_word, pipe_timeout)) {
@@ -975,16 +1029,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after_sync();
         std::uint32_t const d_tmem = tmem_base + buf * BN;
         bool ok = true;
-        for (std::int32_t kb = 0; kb < k_blocks; ++kb, ++it) {
-          std::uint32_t const s = it % cfg::stages;
-          if (!bar_wait<kPair>(&full[s], (it / cfg::stages) & 1u, abort_word, pipe_timeout)) {
+        for (std::int32_t kb = kb_begin; kb < kb_end; ++kb) {
+          std::uint32_t const s = stage;
+          if (!bar_wait<kPair>(&full[s], phase, abort_word, pipe_timeout)) {
             detail::record_error(p, err_local_timeout, r, 0, 5);
             ok = false;
             break;
           }
           ptx::tc_fence_after_sync();
-          std::uint32_t const a_addr = ptx::smem_addr(stages + s * cfg::stage_bytes);
-          std::uint32_t const b_addr = a_addr + cfg::a_bytes;
+          std::uint32_t const a_addr = ptx::smem_addr(stages + s * stage_bytes);
+          std::uint32_t const b_addr = a_addr + a_bytes;
 #pragma unroll
           for (int kk = 0; kk < kBlockK / 16; ++kk) {
             // A: K-major, 128 B swizzle, 8-row groups 1024 B apart; a K step
@@ -996,7 +1050,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // same offsets in both CTAs; each CTA holds its half of B.)
             std::uint64_t const b_desc =
                 ptx::smem_desc_sw128(b_addr + kk * 2048, cfg::b_panel_bytes, 1024);
-            std::uint32_t const acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            std::uint32_t const acc = (kb > kb_begin || kk > 0) ? 1u : 0u;
             if constexpr (kPair) {
               ptx::umma_f16_pair(d_tmem, a_desc, b_desc, idesc, acc);
             } else {
@@ -1007,6 +1061,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::umma_commit_pair(&empty[s]);
           } else {
             ptx::umma_commit(&empty[s]);
+          }
+          if (++stage == n_stages) {
+            stage = 0;
+            phase ^= 1u;
           }
         }
         if (!ok) {
@@ -1080,6 +1138,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       // written nor published, and no reduce task exists for it.
       bool const active = c.tile_row * kBlockM + quarter * 32 < p.m;
 
+      // K split: ranks > 0 send their accumulator rows into rank 0's stage
+      // ring (free once rank 0's MMAs are done); rank 0 adds them below, in
+      // rank order. Layout, fp32: [rank - 1][quarter < n_active][32-column
+      // chunk][4-column group][row][4 columns], so a warp's 16-byte accesses
+      // cover 512 contiguous bytes on both sides.
+      std::int32_t const rows_here = p.m - c.tile_row * kBlockM;
+      std::int32_t const n_active = ((rows_here < kBlockM ? rows_here : kBlockM) + 31) / 32;
+      float *const recv = reinterpret_cast<float *>(stages);
+      if (k_split > 1) {
+        if (split_rank != 0) {
+          if (!__all_sync(0xffffffffu,
+                          ptx::mbar_wait_cluster(ring_free, n & 1u, abort_word, pipe_timeout))) {
+            if (lane == 0) detail::record_error(p, err_local_timeout, r, split_rank, 32);
+            break;
+          }
+#pragma unroll 1
+          for (int ch = 0; active && ch < BN / 32; ++ch) {
+            std::uint32_t v[32];
+            ptx::tmem_load_32x32b_x32(t_row + ch * 32, v);
+            ptx::tmem_wait_load();
+            std::uint32_t const dst = ptx::map_to_rank(
+                recv + ((((static_cast<std::int32_t>(split_rank) - 1) * n_active + quarter) *
+                             (BN / 32) + ch) * 1024 + static_cast<std::int32_t>(lane) * 4),
+                0);
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              ptx::st_shared_remote_v4(dst + j4 * 512, v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2],
+                                       v[4 * j4 + 3]);
+            }
+          }
+          ptx::tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::mbar_arrive_remote(ptx::map_to_rank(recv_full, 0));  // release: the rows above
+            ptx::mbar_arrive(&acc_empty[buf]);
+          }
+          continue;
+        }
+        if (warp == kEpilogueWarp0 && lane == 0) {
+          for (std::int32_t rk = 1; rk < k_split; ++rk) {
+            ptx::mbar_arrive_remote(ptx::map_to_rank(ring_free, static_cast<std::uint32_t>(rk)));
+          }
+        }
+        if (!__all_sync(0xffffffffu,
+                        ptx::mbar_wait_cluster(recv_full, n & 1u, abort_word, pipe_timeout))) {
+          if (lane == 0) detail::record_error(p, err_local_timeout, r, 0, 33);
+          break;
+        }
+      }
+
       if constexpr (kSwiGLU) {
         // act[row, col] = silu(gate) * up, from accumulator columns col and
         // BN/2 + col, in fp32, rounded once to bf16.
@@ -1118,6 +1226,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         std::uint32_t v[32];
         ptx::tmem_load_32x32b_x32(t_row + ch * 32, v);
         ptx::tmem_wait_load();
+        for (std::int32_t rk = 1; rk < k_split; ++rk) {
+          float4 const *src = reinterpret_cast<float4 const *>(
+              recv + (((rk - 1) * n_active + quarter) * (BN / 32) + ch) * 1024 +
+              static_cast<std::int32_t>(lane) * 4);
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 const f = src[j4 * 32];
+            v[4 * j4 + 0] = __float_as_uint(__uint_as_float(v[4 * j4 + 0]) + f.x);
+            v[4 * j4 + 1] = __float_as_uint(__uint_as_float(v[4 * j4 + 1]) + f.y);
+            v[4 * j4 + 2] = __float_as_uint(__uint_as_float(v[4 * j4 + 2]) + f.z);
+            v[4 * j4 + 3] = __float_as_uint(__uint_as_float(v[4 * j4 + 3]) + f.w);
+          }
+        }
         if (kGather || p.n_pes == 1) {
           if (grow < p.m) {
             __nv_bfloat16 *dst = p.out + static_cast<std::int64_t>(grow) * p.n;
@@ -1237,8 +1358,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   ptx::tc_fence_before_sync();
   __syncthreads();
-  if constexpr (kPair) {
-    // No remote arrive, MMA or TMA write may still target the other CTA.
+  if (kPair || k_split > 1) {
+    // No remote arrive, store, MMA or TMA write may still target another CTA.
     ptx::cluster_sync();
   }
   ptx::tc_fence_after_sync();

@@ -57,13 +57,56 @@ cudaError_t launch_persistent(int device, int grid, cudaStream_t stream, Args co
   }
 }
 
+// K split (gemm_ar_params::k_split > 1, one CTA per tile otherwise): clusters
+// of k_split CTAs, one cluster per GEMM tile. Falls back to one CTA per tile
+// (k_split = 1 on the usual persistent grid) when the device cannot hold
+// that many clusters at once, since a cluster computes one tile only.
+template <auto Kernel, int kSmem>
+cudaError_t launch_split(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
+                         CUtensorMap const &mb, CUtensorMap const &mb2, gemm_ar_params prm) {
+  static std::atomic<int> max_clusters[kLaunchMaxDevices][5] = {};
+  bool const known = device >= 0 && device < kLaunchMaxDevices;
+  int const ks = prm.k_split;
+  cudaError_t e = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(ks);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = known ? max_clusters[device][ks].load(std::memory_order_acquire) : 0;
+  if (clusters == 0) {
+    cfg.gridDim = dim3(static_cast<unsigned>(ks), 1, 1);
+    e = cudaOccupancyMaxActiveClusters(&clusters, Kernel, &cfg);
+    if (e != cudaSuccess) return e;
+    if (known) max_clusters[device][ks].store(clusters, std::memory_order_release);
+  }
+  if (clusters < prm.tiles) {
+    prm.k_split = 1;
+    return launch_persistent<Kernel, false, kSmem>(device, grid, stream, ma, mb, mb2, prm);
+  }
+  cfg.gridDim = dim3(static_cast<unsigned>(prm.tiles * ks), 1, 1);
+  return cudaLaunchKernelEx(&cfg, Kernel, ma, mb, mb2, prm);
+}
+
 template <int BN, bool kWireF32, bool kPair, bool kSwiGLU = false, bool kGather = false>
 cudaError_t launch_variant(int device, int grid, cudaStream_t stream, CUtensorMap const &ma,
                            CUtensorMap const &mb, CUtensorMap const &mb2,
                            gemm_ar_params const &prm) {
-  return launch_persistent<&gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU, kGather>, kPair,
-                           gemm_config<BN, kPair>::smem_bytes>(device, grid, stream, ma, mb, mb2,
-                                                               prm);
+  constexpr auto kKernel = &gemm_ar_megakernel<BN, kWireF32, kPair, kSwiGLU, kGather>;
+  constexpr int kSmem = gemm_config<BN, kPair>::smem_bytes;
+  if constexpr (!kPair && !kSwiGLU && !kGather) {
+    if (prm.k_split > 1) {
+      return launch_split<kKernel, kSmem>(device, grid, stream, ma, mb, mb2, prm);
+    }
+  }
+  return launch_persistent<kKernel, kPair, kSmem>(device, grid, stream, ma, mb, mb2, prm);
 }
 
 // Launches the variant a plan picked: tile_n 64 / 128 / 256, CTA pairs

@@ -240,6 +240,15 @@ __device__ __forceinline__ void st_shared_remote(std::uint32_t cluster_addr, std
   asm volatile("st.shared::cluster.u32 [%0], %1;" :: "r"(cluster_addr), "r"(v) : "memory");
 }
 
+
+// 16 bytes into the shared memory of a CTA of this cluster.
+__device__ __forceinline__ void st_shared_remote_v4(std::uint32_t cluster_addr, std::uint32_t a,
+                                                    std::uint32_t b, std::uint32_t c,
+                                                    std::uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};"
+               :: "r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_test_cluster(std::uint32_t bar, std::uint32_t parity) {
   std::uint32_t done;
   asm volatile(

@@ -29,6 +29,10 @@ GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "kat_gemm_allreduce.j
     (384, 384, 520, 128),
     (1024, 1024, 1024, 256),
     (16, 8192, 3584, 0),     # decode shape: one 16-row tile row, tile_n 64
+    (1, 1024, 704, 0),       # one token: an 8-row A box, 19 stages
+    (37, 520, 200, 128),     # ragged token count (40-row box), ragged n and k
+    (100, 2048, 3584, 256),  # 104-row box, tile_n 256
+    (64, 4096, 1024, 0),     # the 64-row box
     (130, 264, 8, 64),       # k shorter than one k-block
     (200, 264, 72, 128),     # one CTA pair: ragged lower tile, ragged last column tile
     (512, 768, 1000, 256),   # pairs with tile_n 256, k not a multiple of 64
