@@ -421,6 +421,12 @@ megacu_status run_bf16(megacu_driver_view driver, void const *a, void const *b, 
   std::int32_t const reduced_tiles =
       n_pes == 1 ? 0 : (pl.one_shot ? pl.tiles : owned_tiles(sched, my_pe));
   prm.n_comm = reduced_tiles * kQuarters * (via_switch ? 1 : pl.tile_n / 64);
+  // One-shot peer exchange of one tile row, bf16 wire: 16-column slices.
+  prm.comm_slices = (pl.one_shot && pl.m_tiles == 1 && !via_switch && pl.wire_bytes == 2 &&
+                     prm.mode == mode_allreduce)
+                        ? 1
+                        : 0;
+  if (prm.comm_slices) prm.n_comm *= 4;
   // Warps per CTA running exchange sub-tasks. The in-switch reduction
   // saturates the fabric with one per SM; more only lengthen its queues and
   // with them every sub-task's latency and the drain at the end (tp = 8, C2:

@@ -131,6 +131,10 @@ struct gemm_ar_params {
   // others' accumulators (received in its stage ring through distributed
   // shared memory) before its epilogue.
   std::int32_t k_split;
+  // 1: one-shot peer exchange of one tile row (decode shapes, bf16 wire):
+  // sub-tasks are 16-column slices of a block (comm_tasks_slices), so that a
+  // warp loads one slice from every PE in one round trip.
+  std::int32_t comm_slices;
 };
 
 namespace detail {
@@ -381,6 +385,105 @@ __device__ __forceinline__ void comm_tasks_peer(gemm_ar_params const &p, tile_sc
       count(p, ctr_reduce_tasks, 1);
       count(p, ctr_partial_acquire, p.n_pes);
       if (push_all) count(p, ctr_final_publish, p.n_pes);
+      trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
+    }
+  }
+}
+
+// One-shot peer exchange of one tile row (decode shapes, bf16 wire): the few
+// blocks such a call has leave most worker warps idle, while a block summed
+// by one warp takes one NVLink round trip per pair of PEs. Here a sub-task is
+// (tile, 32-row quarter, 64-column block, 16-column slice): a warp acquires
+// the quarter's flags, loads its slice (two 16-byte vectors per row) from every
+// PE at once, sums in PE order 0..n_pes-1 in fp32 (the same sum as
+// comm_tasks_peer), rounds once to bf16 and stores its rows into this PE's
+// out. Counters and trace records are kept per block (slice 0), as the task
+// graph counts them.
+template <int BN>
+__device__ __forceinline__ void comm_tasks_slices(gemm_ar_params const &p,
+                                                  tile_schedule const &sched,
+                                                  std::uint32_t parity, std::uint32_t epoch,
+                                                  std::uint32_t *my_events,
+                                                  std::uint32_t const *abort_word,
+                                                  std::uint32_t lane) {
+  constexpr int kBlocks = BN / 64;
+  constexpr int kSlices = 4;                          // 16 columns each
+  constexpr std::int64_t kSlotBytes = std::int64_t(kBlockM) * BN * 2;
+  constexpr std::int64_t kVecStride = kBlockM * 16;  // bytes between wire vectors of a row
+  constexpr int kMaxPes = megacu::nvshmem::max_team_pes;
+  control_block *ctrl = control(p);
+  for (;;) {
+    std::uint32_t const ticket = draw_ticket(&ctrl->reduce_ticket, lane);
+    if (ticket >= static_cast<std::uint32_t>(p.n_comm)) {
+      break;
+    }
+    std::int32_t const j = static_cast<std::int32_t>(ticket) / (kQuarters * kBlocks * kSlices);
+    std::int32_t const rem = static_cast<std::int32_t>(ticket) % (kQuarters * kBlocks * kSlices);
+    std::int32_t const quarter = rem / (kBlocks * kSlices);
+    std::int32_t const cb = (rem / kSlices) % kBlocks;
+    std::int32_t const sl = rem % kSlices;
+    tile_coord const c = locate(sched, j);  // one-shot: every tile, raster order
+    std::int32_t const tile = c.tile_row * p.n_tiles + c.tile_col;
+    if (!block_exists<BN>(p, c.tile_row, c.tile_col, quarter, cb)) {
+      continue;  // no output element lives in this block
+    }
+    bool ok = true;
+    if (static_cast<std::int32_t>(lane) < p.n_pes) {
+      ok = wait_flag(my_events + arrive_index(parity, lane, tile, quarter, p.n_pes, p.tiles),
+                     epoch, abort_word, p.timeout_ns);
+      if (!ok) record_error(p, err_remote_timeout, tile, lane, 8);
+    }
+    if (!__all_sync(0xffffffffu, ok)) {
+      break;
+    }
+    __syncwarp();  // orders every lane's loads after the lanes' acquires
+    std::uint64_t const t0 = ptx::now_ns();
+    // Lane = row of the quarter; vector (v, row) of a slot at (v * 128 + row) * 16.
+    std::int64_t const in_slot = slot_offset(parity, tile, p.tiles, kSlotBytes) +
+                                 (static_cast<std::int64_t>(quarter) * 32 + lane) * 16 +
+                                 static_cast<std::int64_t>(cb * 8 + sl * 2) * kVecStride;
+    uint4 w[kMaxPes][2];
+#pragma unroll
+    for (int src = 0; src < kMaxPes; ++src) {
+      if (src < p.n_pes) {
+        char const *base = p.peers.translate(p.workspace, src) + in_slot;
+        w[src][0] = ptx::ld_cg_v4(base);
+        w[src][1] = ptx::ld_cg_v4(base + kVecStride);
+      }
+    }
+    float acc[2][8];
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[v][e] = 0.0f;
+    }
+#pragma unroll
+    for (int src = 0; src < kMaxPes; ++src) {
+      if (src < p.n_pes) {
+        add_bf16x8(acc[0], w[src][0]);
+        add_bf16x8(acc[1], w[src][1]);
+      }
+    }
+    std::int32_t const row = c.tile_row * kBlockM + quarter * 32 + static_cast<std::int32_t>(lane);
+    std::int32_t const col = c.tile_col * BN + cb * 64 + sl * 16;
+    if (row < p.m) {
+      __nv_bfloat16 *at = p.out + static_cast<std::int64_t>(row) * p.n + col;
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        if (col + v * 8 < p.n) {
+          uint4 q;
+          q.x = ptx::pack_bf16x2(acc[v][0], acc[v][1]);
+          q.y = ptx::pack_bf16x2(acc[v][2], acc[v][3]);
+          q.z = ptx::pack_bf16x2(acc[v][4], acc[v][5]);
+          q.w = ptx::pack_bf16x2(acc[v][6], acc[v][7]);
+          ptx::st_v4(at + v * 8, q);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && sl == 0) {
+      count(p, ctr_reduce_tasks, 1);
+      count(p, ctr_partial_acquire, p.n_pes);
       trace(p, 2, quarter * kBlocks + cb, ticket, tile, t0);
     }
   }
@@ -1337,6 +1440,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.mc_workspace != nullptr) {
           detail::comm_tasks_switch<BN>(p, sched, parity, epoch, my_events, abort_word, xpose,
                                         lane);
+        } else if (p.comm_slices) {
+          detail::comm_tasks_slices<BN>(p, sched, parity, epoch, my_events, abort_word, lane);
         } else {
           detail::comm_tasks_peer<BN, false>(p, sched, parity, epoch, my_events, abort_word,
                                              xpose, lane);
