@@ -902,6 +902,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::int32_t const kb_end = (static_cast<std::int32_t>(split_rank) + 1) * k_blocks / k_split;
 
   if (threadIdx.x == 0) {
+    // The launch counter and the tensor maps are fetched first, so that their
+    // latency overlaps the barrier set-up below.
+    std::uint32_t const launches = ptx::ld_relaxed_gpu(&ctrl->launch_count);
+    ptx::prefetch_tensor_map(&map_a);
+    ptx::prefetch_tensor_map(&map_b);
+    if constexpr (kSwiGLU || kGather) ptx::prefetch_tensor_map(&map_b2);
     // Arrivals per phase. Pairs: the leader's acc_empty also counts the
     // follower's 4 epilogue warps, its task_empty the follower's 4 epilogue
     // warps and producer; the follower's own empty / acc_full / task_full
@@ -924,10 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(recv_full, 4 * static_cast<std::uint32_t>(k_split - 1));  // epilogue warps
     }
     ptx::fence_barrier_init();
-    *epoch_slot = ptx::ld_relaxed_gpu(&ctrl->launch_count) + 1u;
-    ptx::prefetch_tensor_map(&map_a);
-    ptx::prefetch_tensor_map(&map_b);
-    if constexpr (kSwiGLU || kGather) ptx::prefetch_tensor_map(&map_b2);
+    *epoch_slot = launches + 1u;
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -985,7 +988,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             std::int32_t const cluster = static_cast<std::int32_t>(blockIdx.x) / k_split;
             q = (n == 0 && cluster < gemm_units) ? cluster : -1;
           } else {
-            std::uint32_t const ticket = atomicAdd(&ctrl->gemm_ticket, 1u);
+            // The first ticket of a CTA (of a pair) is its index in the grid;
+            // later ones come from the queue, past those (one global atomic
+            // less before the first load).
+            std::uint32_t const units_in_grid = gridDim.x / (kPair ? 2u : 1u);
+            std::uint32_t const ticket = n == 0 ? blockIdx.x / (kPair ? 2u : 1u)
+                                                : units_in_grid + atomicAdd(&ctrl->gemm_ticket, 1u);
             q = ticket < static_cast<std::uint32_t>(gemm_units) ? static_cast<std::int32_t>(ticket)
                                                                 : -1;
           }
