@@ -265,3 +265,16 @@ def test_problem_struct_is_rebuilt_after_a_field_changes():
     traced = p.to_c(0x1000, 4)
     assert traced.trace == 0x1000 and traced.trace_capacity == 4 and p.to_c() is again
     assert p == mb.Problem(256, 512, 128, tile_n=128)  # equality still compares fields only
+
+
+@pytest.mark.parametrize("m,n,k,tile_n", [
+    (16, 8192, 3584, 128),   # config 4: 64 tiles, each split over K between two CTAs
+    (128, 8192, 3584, 128),
+    (64, 1024, 1024, 64),    # 16 tiles of 64: split in two fills more SMs than wider tiles
+    (1, 65536, 256, 256),    # 256 tiles of 256 already cover the SMs: no split
+    (16, 8192, 64, 64),      # one k-block: no split; the narrowest tiles give the most CTAs
+])
+def test_one_tile_row_plan_width(m, n, k, tile_n):
+    """One tile row (decode shapes): the plan picks the tile width that, with
+    the K split the launcher may add, keeps the most SMs busy."""
+    assert mb.plan(mb.Problem(m, n, k), 8).tile_n == tile_n
