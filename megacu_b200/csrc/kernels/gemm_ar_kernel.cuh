@@ -900,6 +900,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   std::uint32_t const split_rank = k_split > 1 ? ptx::cluster_ctarank() : 0u;
   std::int32_t const kb_begin = static_cast<std::int32_t>(split_rank) * k_blocks / k_split;
   std::int32_t const kb_end = (static_cast<std::int32_t>(split_rank) + 1) * k_blocks / k_split;
+  // Single-CTA plain tiles: the first ticket is static, so thread 0 (the
+  // producer) issues the first tile's first `pre_issued` stage loads right
+  // after setting up the barriers, and the rest of the set-up (TMEM
+  // allocation, block and cluster barriers) overlaps their latency. The
+  // producer's loop then starts past them.
+  constexpr bool kEarlyLoads = !kPair && !kSwiGLU && !kGather;
+  std::uint32_t pre_issued = 0;
 
   if (threadIdx.x == 0) {
     // The launch counter and the tensor maps are fetched first, so that their
@@ -931,6 +938,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::fence_barrier_init();
     *epoch_slot = launches + 1u;
+    if constexpr (kEarlyLoads) {
+      // The first ticket exactly as the producer's loop takes it below.
+      std::int32_t const first = static_cast<std::int32_t>(blockIdx.x) / k_split;
+      std::int32_t const kbs = kb_end - kb_begin;
+      if (first < gemm_units && kbs > 0) {
+        ptx::fence_proxy_async_shared();  // the inits above before the loads' complete_tx
+        tile_coord const c = locate(sched, first);
+        pre_issued = kbs < static_cast<std::int32_t>(n_stages) ? static_cast<std::uint32_t>(kbs)
+                                                               : n_stages;
+        for (std::uint32_t s = 0; s < pre_issued; ++s) {
+          std::int32_t const kk = (kb_begin + static_cast<std::int32_t>(s)) * kBlockK;
+          std::uint8_t *sa = stages + s * stage_bytes;
+          ptx::mbar_arrive_expect_tx(&full[s], tx_bytes);
+          ptx::tma_load_2d(&map_a, &full[s], sa, kk, c.tile_row * kBlockM);
+#pragma unroll
+          for (int panel = 0; panel < BN / 64; ++panel) {
+            ptx::tma_load_2d(&map_b, &full[s], sa + a_bytes + panel * cfg::b_panel_bytes,
+                             c.tile_col * BN + panel * 64, kk);
+          }
+        }
+      }
+    }
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -968,8 +997,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- task fetcher + TMA producer ----------------
     if (lane == 0) {
-      std::uint32_t it = 0;
-      std::uint32_t stage = 0, phase = 0;  // it % n_stages, (it / n_stages) & 1
+      // Past the loads issued during the set-up (pre_issued <= n_stages).
+      std::uint32_t it = pre_issued;
+      std::uint32_t stage = pre_issued == n_stages ? 0u : pre_issued;  // it % n_stages
+      std::uint32_t phase = pre_issued == n_stages ? 1u : 0u;          // (it / n_stages) & 1
       bool ok = true;
       for (std::uint32_t n = 0; ok; ++n) {
         std::uint32_t const slot = n % kTaskRing;
@@ -1058,7 +1089,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (cta_rank == 0) detail::count(p, ctr_partial_acquire, kPair ? 2 : 1);
           }
         }
-        for (std::int32_t kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        std::int32_t const kb_first =
+            kb_begin + (n == 0 ? static_cast<std::int32_t>(pre_issued) : 0);
+        for (std::int32_t kb = kb_first; kb < kb_end; ++kb, ++it) {
           std::uint32_t const s = stage;
           if (!bar_wait<kPair>(&empty[s], phase ^ 1u, abort_word,
                                pipe_timeout)) {
@@ -1499,7 +1532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ctrl->launch_count = epoch;
       atomicAdd(&ctrl->counters[ctr_launches], 1ull);
-      __threadfence();
+      // No fence: nothing of this launch reads these words again, and the
+      // next launch is stream-ordered after this one.
       atomicExch(&ctrl->done_ctas, 0u);
     }
   }

@@ -218,6 +218,18 @@ def p50(xs):
     return statistics.median(xs)
 
 
+def timer_tick_us(samples_ms):
+    """The event timer's step as seen in per-step times (ms lists): the
+    smallest positive difference between two distinct samples, in
+    microseconds, or None with fewer than two distinct values. On some B200
+    hosts CUDA events advance in 2.048 us steps, so a p50 of calls of a few
+    tens of microseconds moves in those steps; the mean over many steps does
+    not (the call's phase against the tick varies from step to step)."""
+    values = sorted({round(x * 1e3, 4) for xs in samples_ms for x in xs})
+    gaps = [b - a for a, b in zip(values, values[1:]) if b - a > 0]
+    return round(min(gaps), 4) if gaps else None
+
+
 # ---------------------------------------------------------------------------
 # Output check of the timed calls
 # ---------------------------------------------------------------------------

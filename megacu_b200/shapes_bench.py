@@ -28,7 +28,10 @@ outside the CUDA events; every step's time is the max over ranks:
                            slice; for `ag` the whole gathered A) (tp > 1):
                            the fused time minus this is the exchange time
                            the kernel did not hide
-Configs 3 and ag report the mean per call, config 4 the p50. Prints one JSON
+Configs 3 and ag report the mean per call, config 4 the p50 (and the mean,
+``us_per_call_mean``, beside the step of the event timer seen in the samples,
+``timer_tick_us``: where events advance in 2.048 us steps, a p50 of calls of
+a few tens of microseconds moves in those steps and the mean does not). Prints one JSON
 line per shape on rank 0. After the timing every rank checks the last timed
 fused call (``parity``): its output against an fp32 reference of the same
 inputs (each rank's slices multiplied in fp32, summed over the ranks by NCCL
@@ -54,7 +57,7 @@ import os
 
 from .measure import (NVLINK_GBS, REL_TOL, STRICT_FLOOR, ClockSampler, all_ranks,
                       expected_counters, hbm_peak, interleaved, mean, output_errors, p50,
-                      peaks, ranks_identical, reference_sum, seeded)
+                      peaks, ranks_identical, reference_sum, seeded, timer_tick_us)
 
 C3 = dict(m=8192, n=8192, k_total=28672)
 C4 = dict(m=(16, 32, 64, 128), n=8192, k_total=28672)
@@ -222,6 +225,8 @@ def run_shape(args, config, m, n, k_total, rank, world, local, team_cache):
         "tp": tp, "m": m, "n": n, "k_per_pe": k, "steps": args.steps, "warmup": args.warmup,
         "statistic": "mean" if config == 3 else "p50", "data": "synthetic",
         "us_per_call": us,
+        "us_per_call_mean": {name: mean(v) * 1e3 for name, v in zip(names, ms)},
+        "timer_tick_us": timer_tick_us(ms),
         "tflops_per_gpu": {name: flops_job / tp / (u * 1e-6) / 1e12 for name, u in us.items()},
         "plan": {"tile": [pl.tile_m, pl.tile_n], "tiles": pl.tiles, "one_shot": pl.one_shot,
                  "cta_pairs": pl.cta_pairs, "gemm_units": pl.gemm_units,

@@ -138,3 +138,12 @@ def test_output_errors_measures():
     assert scaled["max_rel_err"] == pytest.approx(0.005 / (10.0 + rms), rel=1e-4)
     bad = measure.output_errors(torch.tensor([[float("nan"), 1.0, 1.0, 1.0]]), want)
     assert not bad["max_rel_err"] < 1.0 and not bad["max_rel_err_strict"] < 1.0
+
+
+def test_timer_tick_is_the_smallest_step_between_samples():
+    tick = 2.048e-3  # ms
+    samples = [[14 * tick, 15 * tick, 14 * tick], [9 * tick, 12 * tick]]
+    assert measure.timer_tick_us(samples) == pytest.approx(2.048)
+    assert measure.timer_tick_us([[0.0301, 0.03042, 0.0301]]) == pytest.approx(0.32)
+    assert measure.timer_tick_us([[0.03, 0.03]]) is None
+    assert measure.timer_tick_us([[]]) is None
