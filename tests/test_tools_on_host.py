@@ -64,6 +64,8 @@ def _check(name, lines, tp):
         for x in lines:
             assert x["tp"] == tp and x["n"] == 8192 and x["k_per_pe"] == 28672 // tp
             assert x["us_per_call"]["fused"] == pytest.approx(ms * 1e3)
+            assert x["us_per_call_mean"] == pytest.approx(x["us_per_call"])  # constant stand-in
+            assert x["timer_tick_us"] is None  # every stand-in step takes the same time
             assert {"tensor", "hbm", "nvlink"} <= set(x["roofline_call"]["terms_us"])
             assert ("kernel_without_exchange" in x["us_per_call"]) == (tp > 1)
         if name != "shapes_bench":
